@@ -1,0 +1,193 @@
+/*
+ * qgemv_b200.h -- C ABI of libqgemv_b200.so, the sm_100a (B200) q8_0 / q4_0
+ * quantized GEMV library.
+ *
+ * Rules for every entry point:
+ *   - Pointers are device pointers owned by the caller (for example
+ *     torch.Tensor.data_ptr() of CUDA tensors); nothing is allocated on the
+ *     GEMV path.
+ *   - `stream` is a cudaStream_t (NULL = the legacy default stream); work is
+ *     enqueued on it and the call returns without synchronising.
+ *   - The return value is a qgemv_status; 0 means the work was enqueued.
+ *     The library never exits or aborts.  qgemv_last_error() returns a
+ *     message for the last failure on the calling thread.
+ *   - Arguments are validated before anything is launched: K % 32 == 0,
+ *     M, K >= 0, row counts and K below 2^31, alignment (quant planes, AoS
+ *     blocks and roof buffers 16 bytes; scale planes 2 bytes; x and y 4
+ *     bytes), ldx >= K and ldy >= M.
+ *
+ * Layouts (ggml, byte-identical; the reference declares them at
+ * src/qgemv_kernels.cuh:16-26):
+ *   q8_0 block: fp16 d (little endian) + 32 x int8              = 34 bytes
+ *   q4_0 block: fp16 d (little endian) + 16 bytes, byte i = q[i] | q[i+16] << 4
+ *                                                               = 18 bytes
+ *   SoA planes: quants [M][K] int8 (q8_0) or [M][K/2] uint8 (q4_0), scales
+ *   [M][K/32] fp16 (passed as uint16_t bits).  AoS: [M][K/32] blocks.
+ *   Activations X: `ncols` vectors of K fp32, vector n at x + n * ldx.
+ *   Outputs Y: `ncols` vectors of M fp32, vector n at y + n * ldy.
+ *   Y[n][r] = sum_k dequant(W)[r][k] * X[n][k].
+ */
+#ifndef QGEMV_B200_H_
+#define QGEMV_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define QGEMV_API __attribute__((visibility("default")))
+
+typedef enum qgemv_status {
+  QGEMV_OK = 0,
+  QGEMV_ERR_NULL = 1,        /* a required pointer is NULL                    */
+  QGEMV_ERR_SHAPE = 2,       /* negative size, K % 32 != 0, ld too small, ... */
+  QGEMV_ERR_ALIGN = 3,       /* a pointer is not aligned as required          */
+  QGEMV_ERR_CUDA = 4,        /* a CUDA runtime call or launch failed          */
+  QGEMV_ERR_UNSUPPORTED = 5, /* shape beyond what this build handles          */
+  QGEMV_ERR_TIMEOUT = 6,     /* a bounded device-side wait ran out            */
+  QGEMV_ERR_ARG = 7          /* another invalid argument (format, flag, ...)  */
+} qgemv_status;
+
+typedef enum qgemv_format { QGEMV_Q8_0 = 8, QGEMV_Q4_0 = 4 } qgemv_format;
+
+typedef struct qgemv_device_info {
+  char name[256];
+  int device;
+  int cc_major, cc_minor;
+  int sms;
+  int l2_bytes;
+  int mem_clock_khz;
+  int bus_width_bits;
+  int sm_clock_khz;
+  int smem_per_block_optin;
+  double datasheet_gbps; /* 2 * mem_clock * bus_width / 8, as src/bench.cu:267-271 */
+} qgemv_device_info;
+
+/* Library version, e.g. 100 for 1.0.0. */
+QGEMV_API int qgemv_version(void);
+
+/* Message for the last failed call on this thread ("" if none). */
+QGEMV_API const char* qgemv_last_error(void);
+
+/* Constant name of a status code. */
+QGEMV_API const char* qgemv_status_string(int status);
+
+/* Properties of `device`, the fields the reference prints in its device JSON
+ * line (src/bench.cu:261-272). */
+QGEMV_API int qgemv_device_info_get(int device, qgemv_device_info* out);
+
+/* ---------------------------------------------------------------- GEMV --- */
+
+/* q8_0 SoA GEMV.  Replaces qgemv_q8_v5_soa_smem (best) and the SoA ladder
+ * qgemv_q8_v3_soa_vec / qgemv_q8_v4_split<2,4>
+ * (src/qgemv_kernels.cuh:110-175, 264-291; launches src/bench.cu:403-419),
+ * whose signature was (Q, D, x, y, M, K) for one column.  q: int8 [M][K],
+ * d: fp16 bits [M][K/32].  ncols in [0, 1<<20]: more than 16 columns are done
+ * 16 at a time. */
+QGEMV_API int qgemv_q8_0_soa(const void* q, const void* d, const float* x, float* y,
+                             int64_t M, int64_t K, int32_t ncols, int64_t ldx, int64_t ldy,
+                             void* stream);
+
+/* q4_0 SoA GEMV.  Replaces qgemv_q4_v5_soa_smem (best), qgemv_q4_v3_soa_vec and
+ * qgemv_q4_v6_fastunpack (src/qgemv_kernels.cuh:228-254, 323-352, 373-414;
+ * launches src/bench.cu:430-440).  The v6 kernel also took per-block sums of
+ * x (src/bench.cu:341-349); no such input is needed here.  q: uint8 [M][K/2]. */
+QGEMV_API int qgemv_q4_0_soa(const void* q, const void* d, const float* x, float* y,
+                             int64_t M, int64_t K, int32_t ncols, int64_t ldx, int64_t ldy,
+                             void* stream);
+
+/* GEMV straight from ggml/GGUF blocks (no repack).  Replaces the AoS kernels
+ * qgemv_q8_v0_naive / v1_warp / v2_smem_x and qgemv_q4_v0 / v1 / v2
+ * (src/qgemv_kernels.cuh:39-104, 180-224, 294-320; launches
+ * src/bench.cu:393-402, 420-429), signature (W, x, y, M, K).  blocks:
+ * [M][K/32] blocks of 34 (q8_0) or 18 (q4_0) bytes, 16-byte aligned base. */
+QGEMV_API int qgemv_q8_0_aos(const void* blocks, const float* x, float* y, int64_t M,
+                             int64_t K, int32_t ncols, int64_t ldx, int64_t ldy, void* stream);
+QGEMV_API int qgemv_q4_0_aos(const void* blocks, const float* x, float* y, int64_t M,
+                             int64_t K, int32_t ncols, int64_t ldx, int64_t ldy, void* stream);
+
+/* Kernel ladder (the reference's --only selection of one of its 13 kernel
+ * configurations, src/bench.cu:256,358): single-column SoA GEMV with
+ * configuration `variant` in [0, qgemv_soa_variant_count()), named by
+ * qgemv_soa_variant_name().  grid > 0 forces the number of CTAs (0 = the
+ * persistent default).  Same arguments and result as qgemv_q8_0_soa /
+ * qgemv_q4_0_soa with ncols = 1. */
+QGEMV_API int qgemv_soa_variant_count(void);
+QGEMV_API const char* qgemv_soa_variant_name(int variant);
+QGEMV_API int qgemv_soa_variant(int format, int variant, int32_t grid, const void* q,
+                                const void* d, const float* x, float* y, int64_t M, int64_t K,
+                                void* stream);
+
+/* ------------------------------------------------------- quantize / repack --- */
+
+/* GPU quantizer, byte-identical to quantize_q8_0 / quantize_q4_0 of the
+ * reference's python/qformats.py:17-40 (and src/bench.cu:32-69).  w: fp32
+ * [M][ldw] (ldw >= K).  Writes the SoA planes q (q8_0: int8 [M][K], q4_0:
+ * uint8 [M][K/2]) and d (fp16 bits [M][K/32]). */
+QGEMV_API int qgemv_quantize_soa(int format, const float* w, int64_t M, int64_t K, int64_t ldw,
+                                 void* q, void* d, void* stream);
+
+/* Same quantizer, writing ggml blocks [M][K/32] (34 or 18 bytes each). */
+QGEMV_API int qgemv_quantize_aos(int format, const float* w, int64_t M, int64_t K,
+                                 int64_t ldw, void* blocks, void* stream);
+
+/* fp32 dequantization of SoA planes, as dequant_q8_0 / dequant_q4_0 of
+ * python/qformats.py:43-56.  w: fp32 [M][K]. */
+QGEMV_API int qgemv_dequant_soa(int format, const void* q, const void* d, float* w, int64_t M,
+                                int64_t K, void* stream);
+
+/* AoS <-> SoA repack (src/bench.cu:300-314).  to_soa = 1: blocks -> (q, d);
+ * to_soa = 0: (q, d) -> blocks. */
+QGEMV_API int qgemv_repack(int format, int to_soa, void* blocks, void* q, void* d, int64_t M,
+                           int64_t K, void* stream);
+
+/* --------------------------------------------------------------- roof --- */
+
+/* Streaming-read roof probe: reads `bytes` (multiple of 16) with 128-bit
+ * loads, grid = SMs x blocks_per_sm CTAs of 256 threads.  Replaces
+ * stream_read / run_ceiling (src/bench.cu:162-191).  sink: >= 2 uint32 of
+ * device memory, written only on a data-dependent branch. */
+QGEMV_API int qgemv_roof_stream_read(const void* buf, size_t bytes, uint32_t* sink,
+                                     int32_t blocks_per_sm, void* stream);
+
+/* The same read with 1-D TMA bulk copies into a shared-memory ring (one CTA
+ * per SM).  status: one device int, set to QGEMV_ERR_TIMEOUT if a bounded
+ * mbarrier wait ran out (the caller zeroes it before the call). */
+QGEMV_API int qgemv_roof_bulk_read(const void* buf, size_t bytes, uint32_t* sink, int* status,
+                                   void* stream);
+
+/* Device-to-device copy roof (src/bench.cu:193-202): cudaMemcpyAsync. */
+QGEMV_API int qgemv_roof_d2d(void* dst, const void* src, size_t bytes, void* stream);
+
+/* ------------------------------------------------------------- timing --- */
+
+/* One GEMV of a timed step, over `ncopies` copies of the same-shaped weights
+ * (copy i % ncopies is used in step i, so the working set can exceed L2). */
+typedef struct qgemv_call_desc {
+  int32_t format;        /* QGEMV_Q8_0 or QGEMV_Q4_0                     */
+  int32_t layout;        /* 0 = SoA planes (q, d), 1 = AoS blocks (q)    */
+  int32_t ncopies;       /* entries in q (and d)                         */
+  int32_t ncols;         /* activation vectors                           */
+  int64_t M, K, ldx, ldy;
+  const void* const* q;  /* quant planes, or AoS block buffers           */
+  const void* const* d;  /* scale planes (SoA), else NULL                */
+  const float* x;
+  float* y;
+} qgemv_call_desc;
+
+/* Timing harness (replaces time_kernel, src/bench.cu:134-156): issues
+ * `warmup` untimed steps, then `steps` steps back to back on `stream`; a step
+ * runs every call of `calls` once.  A CUDA event is recorded before the first
+ * timed step and after every call.  ms_out[0] = total device time of the timed
+ * steps; ms_out[1 + j] = summed device time of call j (ncalls + 1 floats).
+ * Synchronises `stream` before returning. */
+QGEMV_API int qgemv_time_steps(const qgemv_call_desc* calls, int32_t ncalls, int32_t warmup,
+                               int32_t steps, void* stream, float* ms_out);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* QGEMV_B200_H_ */

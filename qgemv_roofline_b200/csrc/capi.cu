@@ -1,0 +1,340 @@
+// C ABI of libqgemv_b200.so (declared in include/qgemv_b200.h): argument
+// validation, error reporting and dispatch to the kernel files.
+//
+// The reference had no error channel: its harness printed and called exit(1)
+// on any CUDA error (src/bench.cu:19-27) and rejected K % 512 != 0
+// (src/bench.cu:259).  Here every entry point validates first, returns a
+// status code, keeps a per-thread message, and accepts any K % 32 == 0.
+#include "qgemv_b200.h"
+
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <map>
+#include <set>
+#include <utility>
+
+#include "qgemv_common.cuh"
+#include "qgemv_internal.h"
+
+namespace qg {
+
+static thread_local char g_err[512] = "";
+
+int set_error(int code, const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_err, sizeof(g_err), fmt, ap);
+  va_end(ap);
+  return code;
+}
+
+int check_launch(const char* what) {
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return set_error(ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+  return OK;
+}
+
+namespace {
+constexpr int kMaxDevices = 64;
+std::mutex g_mu;
+DeviceInfo g_dev[kMaxDevices];
+bool g_dev_ok[kMaxDevices] = {};
+std::set<std::pair<const void*, int>> g_smem_set;
+struct OccKey {
+  const void* f;
+  int dev, threads;
+  size_t smem;
+  bool operator<(const OccKey& o) const {
+    return f != o.f ? f < o.f : dev != o.dev ? dev < o.dev
+         : threads != o.threads ? threads < o.threads : smem < o.smem;
+  }
+};
+std::map<OccKey, int> g_occ;
+}  // namespace
+
+int current_device_info(DeviceInfo& out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return set_error(ERR_CUDA, "cudaGetDevice: %s", cudaGetErrorString(e));
+  if (dev < 0 || dev >= kMaxDevices) return set_error(ERR_UNSUPPORTED, "device %d", dev);
+  std::lock_guard<std::mutex> lk(g_mu);
+  if (!g_dev_ok[dev]) {
+    DeviceInfo d;
+    d.device = dev;
+    if ((e = cudaDeviceGetAttribute(&d.sms, cudaDevAttrMultiProcessorCount, dev)) ||
+        (e = cudaDeviceGetAttribute(&d.smem_optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev)) ||
+        (e = cudaDeviceGetAttribute(&d.cc_major, cudaDevAttrComputeCapabilityMajor, dev)) ||
+        (e = cudaDeviceGetAttribute(&d.cc_minor, cudaDevAttrComputeCapabilityMinor, dev)) ||
+        (e = cudaDeviceGetAttribute(&d.l2_bytes, cudaDevAttrL2CacheSize, dev)))
+      return set_error(ERR_CUDA, "cudaDeviceGetAttribute: %s", cudaGetErrorString(e));
+    if (d.cc_major != 10 || d.cc_minor != 0)
+      return set_error(ERR_UNSUPPORTED,
+                       "device %d is sm_%d%d; this library is built for sm_100a (B200) only", dev,
+                       d.cc_major, d.cc_minor);
+    g_dev[dev] = d;
+    g_dev_ok[dev] = true;
+  }
+  out = g_dev[dev];
+  return OK;
+}
+
+int allow_max_smem(const void* func, const DeviceInfo& dev) {
+  std::lock_guard<std::mutex> lk(g_mu);
+  auto key = std::make_pair(func, dev.device);
+  if (g_smem_set.count(key)) return OK;
+  const cudaError_t e =
+      cudaFuncSetAttribute(func, cudaFuncAttributeMaxDynamicSharedMemorySize, dev.smem_optin);
+  if (e != cudaSuccess)
+    return set_error(ERR_CUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
+  g_smem_set.insert(key);
+  return OK;
+}
+
+int occupancy(const void* func, const DeviceInfo& dev, int threads, size_t smem, int* out) {
+  const OccKey key{func, dev.device, threads, smem};
+  {
+    std::lock_guard<std::mutex> lk(g_mu);
+    auto it = g_occ.find(key);
+    if (it != g_occ.end()) {
+      *out = it->second;
+      return OK;
+    }
+  }
+  int occ = 0;
+  const cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, func, threads, smem);
+  if (e != cudaSuccess || occ < 1)
+    return set_error(ERR_CUDA, "occupancy query failed (%s, %d blocks)", cudaGetErrorString(e), occ);
+  std::lock_guard<std::mutex> lk(g_mu);
+  g_occ[key] = occ;
+  *out = occ;
+  return OK;
+}
+
+namespace {
+
+constexpr int64_t kMaxDim = (int64_t)1 << 31;
+
+bool misaligned(const void* p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p) % a) != 0; }
+
+int check_fmt(int format) {
+  if (format != 8 && format != 4)
+    return set_error(ERR_ARG, "format must be QGEMV_Q8_0 (8) or QGEMV_Q4_0 (4), got %d", format);
+  return OK;
+}
+
+int check_mk(int64_t M, int64_t K) {
+  if (M < 0 || K < 0) return set_error(ERR_SHAPE, "negative shape M=%lld K=%lld", (long long)M, (long long)K);
+  if (K % QK) return set_error(ERR_SHAPE, "K=%lld is not a multiple of 32", (long long)K);
+  if (M >= kMaxDim || K >= kMaxDim)
+    return set_error(ERR_UNSUPPORTED, "M and K must be below 2^31 (M=%lld K=%lld)", (long long)M,
+                     (long long)K);
+  return OK;
+}
+
+int gemv_entry(int fmt, bool aos, const void* q, const void* d, const float* x, float* y,
+               int64_t M, int64_t K, int32_t ncols, int64_t ldx, int64_t ldy, void* stream) {
+  if (int rc = check_mk(M, K)) return rc;
+  if (ncols < 0) return set_error(ERR_SHAPE, "ncols=%d is negative", ncols);
+  if (M == 0 || ncols == 0) return OK;
+  if (!x || !y) return set_error(ERR_NULL, "x and y must not be NULL");
+  if (K > 0 && (!q || (!aos && !d)))
+    return set_error(ERR_NULL, aos ? "blocks must not be NULL" : "q and d must not be NULL");
+  if (ncols > 1 && ldx < K)
+    return set_error(ERR_SHAPE, "ldx=%lld < K=%lld", (long long)ldx, (long long)K);
+  if (ncols > 1 && ldy < M)
+    return set_error(ERR_SHAPE, "ldy=%lld < M=%lld", (long long)ldy, (long long)M);
+  if (ncols == 1) {
+    ldx = K;
+    ldy = M;
+  }
+  if (K > 0 && misaligned(q, 16))
+    return set_error(ERR_ALIGN, aos ? "blocks must be 16-byte aligned" : "q must be 16-byte aligned");
+  if (!aos && K > 0 && misaligned(d, 2)) return set_error(ERR_ALIGN, "d must be 2-byte aligned");
+  if (misaligned(x, 4) || misaligned(y, 4)) return set_error(ERR_ALIGN, "x and y must be 4-byte aligned");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (K == 0) return fill_zero_rows(y, M, ncols, ldy, st);
+  GemvCall c;
+  c.q = q;
+  c.d = d;
+  c.x = x;
+  c.y = y;
+  c.M = M;
+  c.K = K;
+  c.N = ncols;
+  c.ldx = ldx;
+  c.ldy = ldy;
+  return aos ? gemv_aos(fmt, c, st) : gemv_soa(fmt, c, st);
+}
+
+}  // namespace
+}  // namespace qg
+
+using namespace qg;
+
+extern "C" {
+
+QGEMV_API int qgemv_version(void) { return 100; }
+
+QGEMV_API const char* qgemv_last_error(void) { return g_err; }
+
+QGEMV_API const char* qgemv_status_string(int status) {
+  switch (status) {
+    case QGEMV_OK: return "QGEMV_OK";
+    case QGEMV_ERR_NULL: return "QGEMV_ERR_NULL";
+    case QGEMV_ERR_SHAPE: return "QGEMV_ERR_SHAPE";
+    case QGEMV_ERR_ALIGN: return "QGEMV_ERR_ALIGN";
+    case QGEMV_ERR_CUDA: return "QGEMV_ERR_CUDA";
+    case QGEMV_ERR_UNSUPPORTED: return "QGEMV_ERR_UNSUPPORTED";
+    case QGEMV_ERR_TIMEOUT: return "QGEMV_ERR_TIMEOUT";
+    case QGEMV_ERR_ARG: return "QGEMV_ERR_ARG";
+    default: return "QGEMV_ERR_UNKNOWN";
+  }
+}
+
+QGEMV_API int qgemv_device_info_get(int device, qgemv_device_info* out) {
+  if (!out) return set_error(ERR_NULL, "out must not be NULL");
+  memset(out, 0, sizeof(*out));
+  cudaDeviceProp p;
+  cudaError_t e = cudaGetDeviceProperties(&p, device);
+  if (e != cudaSuccess)
+    return set_error(ERR_CUDA, "cudaGetDeviceProperties(%d): %s", device, cudaGetErrorString(e));
+  snprintf(out->name, sizeof(out->name), "%s", p.name);
+  out->device = device;
+  out->cc_major = p.major;
+  out->cc_minor = p.minor;
+  out->sms = p.multiProcessorCount;
+  out->l2_bytes = p.l2CacheSize;
+  cudaDeviceGetAttribute(&out->mem_clock_khz, cudaDevAttrMemoryClockRate, device);
+  cudaDeviceGetAttribute(&out->bus_width_bits, cudaDevAttrGlobalMemoryBusWidth, device);
+  cudaDeviceGetAttribute(&out->sm_clock_khz, cudaDevAttrClockRate, device);
+  cudaDeviceGetAttribute(&out->smem_per_block_optin, cudaDevAttrMaxSharedMemoryPerBlockOptin,
+                         device);
+  out->datasheet_gbps = 2.0 * out->mem_clock_khz * 1e3 * (out->bus_width_bits / 8.0) / 1e9;
+  return OK;
+}
+
+QGEMV_API int qgemv_q8_0_soa(const void* q, const void* d, const float* x, float* y, int64_t M,
+                             int64_t K, int32_t ncols, int64_t ldx, int64_t ldy, void* stream) {
+  return gemv_entry(8, false, q, d, x, y, M, K, ncols, ldx, ldy, stream);
+}
+
+QGEMV_API int qgemv_q4_0_soa(const void* q, const void* d, const float* x, float* y, int64_t M,
+                             int64_t K, int32_t ncols, int64_t ldx, int64_t ldy, void* stream) {
+  return gemv_entry(4, false, q, d, x, y, M, K, ncols, ldx, ldy, stream);
+}
+
+QGEMV_API int qgemv_soa_variant_count(void) { return soa_variant_count(); }
+
+QGEMV_API const char* qgemv_soa_variant_name(int variant) { return soa_variant_name(variant); }
+
+QGEMV_API int qgemv_soa_variant(int format, int variant, int32_t grid, const void* q,
+                                const void* d, const float* x, float* y, int64_t M, int64_t K,
+                                void* stream) {
+  if (int rc = check_fmt(format)) return rc;
+  if (int rc = check_mk(M, K)) return rc;
+  if (grid < 0) return set_error(ERR_ARG, "grid must be >= 0");
+  if (M == 0 || K == 0) return set_error(ERR_SHAPE, "variants need M > 0 and K > 0");
+  if (!q || !d || !x || !y) return set_error(ERR_NULL, "q, d, x and y must not be NULL");
+  if (misaligned(q, 16) || misaligned(d, 2) || misaligned(x, 4) || misaligned(y, 4))
+    return set_error(ERR_ALIGN, "q must be 16-byte, d 2-byte, x and y 4-byte aligned");
+  GemvCall c;
+  c.q = q;
+  c.d = d;
+  c.x = x;
+  c.y = y;
+  c.M = M;
+  c.K = K;
+  c.N = 1;
+  c.ldx = K;
+  c.ldy = M;
+  c.grid_override = grid;
+  return gemv_soa_variant(format, variant, c, static_cast<cudaStream_t>(stream));
+}
+
+QGEMV_API int qgemv_q8_0_aos(const void* blocks, const float* x, float* y, int64_t M, int64_t K,
+                             int32_t ncols, int64_t ldx, int64_t ldy, void* stream) {
+  return gemv_entry(8, true, blocks, nullptr, x, y, M, K, ncols, ldx, ldy, stream);
+}
+
+QGEMV_API int qgemv_q4_0_aos(const void* blocks, const float* x, float* y, int64_t M, int64_t K,
+                             int32_t ncols, int64_t ldx, int64_t ldy, void* stream) {
+  return gemv_entry(4, true, blocks, nullptr, x, y, M, K, ncols, ldx, ldy, stream);
+}
+
+QGEMV_API int qgemv_quantize_soa(int format, const float* w, int64_t M, int64_t K, int64_t ldw,
+                                 void* q, void* d, void* stream) {
+  if (int rc = check_fmt(format)) return rc;
+  if (int rc = check_mk(M, K)) return rc;
+  if (M == 0 || K == 0) return OK;
+  if (!w || !q || !d) return set_error(ERR_NULL, "w, q and d must not be NULL");
+  if (ldw < K) return set_error(ERR_SHAPE, "ldw=%lld < K=%lld", (long long)ldw, (long long)K);
+  if (misaligned(w, 4) || misaligned(d, 2))
+    return set_error(ERR_ALIGN, "w must be 4-byte and d 2-byte aligned");
+  return quantize(format, w, M, K, ldw, q, d, nullptr, static_cast<cudaStream_t>(stream));
+}
+
+QGEMV_API int qgemv_quantize_aos(int format, const float* w, int64_t M, int64_t K, int64_t ldw,
+                                 void* blocks, void* stream) {
+  if (int rc = check_fmt(format)) return rc;
+  if (int rc = check_mk(M, K)) return rc;
+  if (M == 0 || K == 0) return OK;
+  if (!w || !blocks) return set_error(ERR_NULL, "w and blocks must not be NULL");
+  if (ldw < K) return set_error(ERR_SHAPE, "ldw=%lld < K=%lld", (long long)ldw, (long long)K);
+  if (misaligned(w, 4)) return set_error(ERR_ALIGN, "w must be 4-byte aligned");
+  return quantize(format, w, M, K, ldw, nullptr, nullptr, blocks,
+                  static_cast<cudaStream_t>(stream));
+}
+
+QGEMV_API int qgemv_dequant_soa(int format, const void* q, const void* d, float* w, int64_t M,
+                                int64_t K, void* stream) {
+  if (int rc = check_fmt(format)) return rc;
+  if (int rc = check_mk(M, K)) return rc;
+  if (M == 0 || K == 0) return OK;
+  if (!q || !d || !w) return set_error(ERR_NULL, "q, d and w must not be NULL");
+  if (misaligned(w, 4) || misaligned(d, 2))
+    return set_error(ERR_ALIGN, "w must be 4-byte and d 2-byte aligned");
+  return dequant(format, q, d, w, M, K, static_cast<cudaStream_t>(stream));
+}
+
+QGEMV_API int qgemv_repack(int format, int to_soa, void* blocks, void* q, void* d, int64_t M,
+                           int64_t K, void* stream) {
+  if (int rc = check_fmt(format)) return rc;
+  if (to_soa != 0 && to_soa != 1) return set_error(ERR_ARG, "to_soa must be 0 or 1");
+  if (int rc = check_mk(M, K)) return rc;
+  if (M == 0 || K == 0) return OK;
+  if (!blocks || !q || !d) return set_error(ERR_NULL, "blocks, q and d must not be NULL");
+  if (misaligned(d, 2)) return set_error(ERR_ALIGN, "d must be 2-byte aligned");
+  return repack(format, to_soa, blocks, q, d, M, K, static_cast<cudaStream_t>(stream));
+}
+
+QGEMV_API int qgemv_roof_stream_read(const void* buf, size_t bytes, uint32_t* sink,
+                                     int32_t blocks_per_sm, void* stream) {
+  if (!buf || !sink) return set_error(ERR_NULL, "buf and sink must not be NULL");
+  if (bytes % 16) return set_error(ERR_SHAPE, "bytes must be a multiple of 16");
+  if (misaligned(buf, 16) || misaligned(sink, 4))
+    return set_error(ERR_ALIGN, "buf must be 16-byte and sink 4-byte aligned");
+  if (blocks_per_sm < 1 || blocks_per_sm > 64)
+    return set_error(ERR_ARG, "blocks_per_sm must be in [1, 64]");
+  return roof_stream_read(buf, bytes, sink, blocks_per_sm, static_cast<cudaStream_t>(stream));
+}
+
+QGEMV_API int qgemv_roof_bulk_read(const void* buf, size_t bytes, uint32_t* sink, int* status,
+                                   void* stream) {
+  if (!buf || !sink || !status) return set_error(ERR_NULL, "buf, sink and status must not be NULL");
+  if (bytes % 16) return set_error(ERR_SHAPE, "bytes must be a multiple of 16");
+  if (misaligned(buf, 16) || misaligned(sink, 4) || misaligned(status, 4))
+    return set_error(ERR_ALIGN, "buf must be 16-byte aligned; sink and status 4-byte");
+  return roof_bulk_read(buf, bytes, sink, status, static_cast<cudaStream_t>(stream));
+}
+
+QGEMV_API int qgemv_roof_d2d(void* dst, const void* src, size_t bytes, void* stream) {
+  if (!dst || !src) return set_error(ERR_NULL, "dst and src must not be NULL");
+  const cudaError_t e =
+      cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDeviceToDevice, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return set_error(ERR_CUDA, "cudaMemcpyAsync: %s", cudaGetErrorString(e));
+  return OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,64 @@
+// Internal (C++) interfaces between the kernel files and the C ABI in capi.cu.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+namespace qg {
+
+// Shared-memory budget for the staged activation tile of the GEMV kernels.
+// A whole x of K <= 16384 floats (or N*K floats up to this size) is staged
+// once per CTA; larger batches are staged in K tiles.
+constexpr size_t kXStageBytes = 64 * 1024;
+
+struct DeviceInfo {
+  int device = 0;
+  int sms = 0;
+  int smem_optin = 0;  // max dynamic shared memory per block (opt-in)
+  int cc_major = 0, cc_minor = 0;
+  int l2_bytes = 0;
+};
+
+// Cached per device; fills `out` for the current device.
+int current_device_info(DeviceInfo& out);
+
+// Lets `func` use the device's opt-in shared-memory maximum (once per device).
+int allow_max_smem(const void* func, const DeviceInfo& dev);
+
+// Resident blocks per SM of `func` (cached per device, block size and smem).
+int occupancy(const void* func, const DeviceInfo& dev, int threads, size_t smem, int* out);
+
+struct GemvCall {
+  const void* q = nullptr;  // SoA quant plane, or AoS blocks
+  const void* d = nullptr;  // SoA scale plane (fp16 bits); unused for AoS
+  const float* x = nullptr;
+  float* y = nullptr;
+  int64_t M = 0, K = 0;
+  int N = 1;
+  int64_t ldx = 0, ldy = 0;
+  int grid_override = 0;  // >0: force the grid size (tuning / tests)
+};
+
+int gemv_soa(int fmt, const GemvCall& c, cudaStream_t st);
+int gemv_soa_variant(int fmt, int variant, const GemvCall& c, cudaStream_t st);
+int soa_variant_count();
+const char* soa_variant_name(int v);
+int gemv_aos(int fmt, const GemvCall& c, cudaStream_t st);
+int fill_zero_rows(float* y, int64_t M, int N, int64_t ldy, cudaStream_t st);
+
+// Quantizers: W fp32 [M][ldw] -> SoA planes (q, d) or AoS blocks.
+int quantize(int fmt, const float* w, int64_t M, int64_t K, int64_t ldw, void* q, void* d,
+             void* aos, cudaStream_t st);
+int dequant(int fmt, const void* q, const void* d, float* w, int64_t M, int64_t K,
+            cudaStream_t st);
+int repack(int fmt, int to_soa, const void* aos, void* q, void* d, int64_t M, int64_t K,
+           cudaStream_t st);
+
+// Roof probes.
+int roof_stream_read(const void* buf, size_t bytes, uint32_t* sink, int blocks_per_sm,
+                     cudaStream_t st);
+int roof_bulk_read(const void* buf, size_t bytes, uint32_t* sink, int* status,
+                   cudaStream_t st);
+
+}  // namespace qg

@@ -1,0 +1,149 @@
+"""Quantized GEMV entry points: ``y = W x`` and ``Y = X W^T`` for N <= 16 columns.
+
+The reference's kernels took ``(Q, D, x, y, M, K)`` for one fp32 column
+(src/qgemv_kernels.cuh); these wrappers take torch tensors, validate them,
+and call the C ABI (include/qgemv_b200.h) with their device pointers on the
+current CUDA stream.  ``x`` is ``[K]`` (returns ``[M]``) or ``[N, K]`` (returns
+``[N, M]``; row n of X is activation vector n).  Tensors must already be on
+the GPU: this is the hot path and it does no implicit copies.
+"""
+
+from __future__ import annotations
+
+from dataclasses import dataclass
+
+import torch
+
+from . import _lib
+from .qformats import BLOCK_BYTES, QK
+
+_SOA_FN = {"q8_0": "qgemv_q8_0_soa", "q4_0": "qgemv_q4_0_soa"}
+_AOS_FN = {"q8_0": "qgemv_q8_0_aos", "q4_0": "qgemv_q4_0_aos"}
+
+
+def _check_fmt(fmt: str):
+    if fmt not in _SOA_FN:
+        raise ValueError(f"format must be 'q8_0' or 'q4_0', got {fmt!r}")
+
+
+def _xy(x: torch.Tensor, M: int, K: int, y: torch.Tensor | None, device):
+    if not x.is_cuda or x.device != device:
+        raise ValueError(f"x must be a CUDA tensor on {device}")
+    if x.dtype != torch.float32:
+        raise TypeError(f"x must be float32, got {x.dtype}")
+    vec = x.dim() == 1
+    X = x.unsqueeze(0) if vec else x
+    if X.dim() != 2 or X.shape[1] != K:
+        raise ValueError(f"x must be [K={K}] or [N, K={K}], got {tuple(x.shape)}")
+    if X.stride(1) != 1:
+        X = X.contiguous()
+    N = X.shape[0]
+    if y is None:
+        Y = torch.empty((N, M), dtype=torch.float32, device=device)
+        y = Y[0] if vec else Y
+    else:
+        if y.dtype != torch.float32 or y.device != device:
+            raise ValueError("y must be a float32 tensor on the weights' device")
+        Y = y.unsqueeze(0) if y.dim() == 1 else y
+        if tuple(Y.shape) != (N, M) or Y.stride(1) != 1:
+            raise ValueError(f"y must be [{M}] or [N, {M}] with unit last stride")
+    ldx = X.stride(0) if N > 1 else K
+    ldy = Y.stride(0) if N > 1 else M
+    return X, Y, y, N, ldx, ldy
+
+
+def qgemv(fmt: str, q: torch.Tensor, d: torch.Tensor, x: torch.Tensor,
+          y: torch.Tensor | None = None, stream: int | None = None) -> torch.Tensor:
+    """SoA GEMV: q (int8 [M, K] | uint8 [M, K/2]), d fp16 [M, K/32], x [K] or [N, K]."""
+    _check_fmt(fmt)
+    if not q.is_cuda:
+        raise ValueError("q must be a CUDA tensor (weights stay resident on the GPU)")
+    M = q.shape[0]
+    K = q.shape[1] if fmt == "q8_0" else q.shape[1] * 2
+    if q.dim() != 2 or not q.is_contiguous() or q.element_size() != 1:
+        raise ValueError("q must be a contiguous 1-byte 2-D tensor")
+    if d.dtype != torch.float16 or tuple(d.shape) != (M, K // QK) or not d.is_contiguous():
+        raise ValueError(f"d must be contiguous float16 [{M}, {K // QK}]")
+    X, Y, y, N, ldx, ldy = _xy(x, M, K, y, q.device)
+    st = torch.cuda.current_stream(q.device).cuda_stream if stream is None else stream
+    _lib.call(_SOA_FN[fmt], q.data_ptr(), d.data_ptr(), X.data_ptr(), Y.data_ptr(),
+              M, K, N, ldx, ldy, st)
+    return y
+
+
+def qgemv_aos(fmt: str, blocks: torch.Tensor, x: torch.Tensor,
+              y: torch.Tensor | None = None, stream: int | None = None) -> torch.Tensor:
+    """GEMV over ggml blocks uint8 [M, K/32, 34|18] (GGUF layout, no repack)."""
+    _check_fmt(fmt)
+    if not blocks.is_cuda:
+        raise ValueError("blocks must be a CUDA tensor")
+    if (blocks.dim() != 3 or blocks.shape[2] != BLOCK_BYTES[fmt] or blocks.dtype != torch.uint8
+            or not blocks.is_contiguous()):
+        raise ValueError(f"blocks must be contiguous uint8 [M, K/32, {BLOCK_BYTES[fmt]}]")
+    M, nb, _ = blocks.shape
+    K = nb * QK
+    X, Y, y, N, ldx, ldy = _xy(x, M, K, y, blocks.device)
+    st = torch.cuda.current_stream(blocks.device).cuda_stream if stream is None else stream
+    _lib.call(_AOS_FN[fmt], blocks.data_ptr(), X.data_ptr(), Y.data_ptr(), M, K, N, ldx, ldy, st)
+    return y
+
+
+@dataclass
+class QuantizedMatrix:
+    """A quantized [M, K] weight matrix resident on one GPU.
+
+    ``layout`` is "soa" (planes ``q``, ``d``) or "aos" (ggml ``blocks``).
+    """
+
+    fmt: str
+    M: int
+    K: int
+    layout: str = "soa"
+    q: torch.Tensor | None = None
+    d: torch.Tensor | None = None
+    blocks: torch.Tensor | None = None
+
+    @classmethod
+    def from_float(cls, W: torch.Tensor, fmt: str, layout: str = "soa") -> "QuantizedMatrix":
+        from . import qformats
+        M, K = W.shape
+        if layout == "soa":
+            q, d = (qformats.quantize_q8_0 if fmt == "q8_0" else qformats.quantize_q4_0)(W)
+            return cls(fmt, M, K, "soa", q=q, d=d)
+        blocks = (qformats.quantize_q8_0_aos if fmt == "q8_0" else qformats.quantize_q4_0_aos)(W)
+        return cls(fmt, M, K, "aos", blocks=blocks)
+
+    @property
+    def nbytes(self) -> int:
+        return self.M * (self.K // QK) * BLOCK_BYTES[self.fmt]
+
+    @property
+    def device(self):
+        return (self.q if self.layout == "soa" else self.blocks).device
+
+    def matvec(self, x: torch.Tensor, y: torch.Tensor | None = None,
+               stream: int | None = None) -> torch.Tensor:
+        if self.layout == "soa":
+            return qgemv(self.fmt, self.q, self.d, x, y, stream)
+        return qgemv_aos(self.fmt, self.blocks, x, y, stream)
+
+    __call__ = matvec
+
+    def rows(self, r0: int, r1: int) -> "QuantizedMatrix":
+        """Row slice [r0, r1) as a new matrix (copies; used for row sharding)."""
+        if self.layout == "soa":
+            return QuantizedMatrix(self.fmt, r1 - r0, self.K, "soa",
+                                   q=self.q[r0:r1].contiguous(), d=self.d[r0:r1].contiguous())
+        return QuantizedMatrix(self.fmt, r1 - r0, self.K, "aos",
+                               blocks=self.blocks[r0:r1].contiguous())
+
+    def to(self, device) -> "QuantizedMatrix":
+        if self.layout == "soa":
+            return QuantizedMatrix(self.fmt, self.M, self.K, "soa", q=self.q.to(device),
+                                   d=self.d.to(device))
+        return QuantizedMatrix(self.fmt, self.M, self.K, "aos", blocks=self.blocks.to(device))
+
+
+def algorithmic_bytes(fmt: str, M: int, K: int, N: int = 1) -> int:
+    """Bytes a call must move: weights M*K*(34|18)/32 + x 4*K*N + y 4*M*N."""
+    return M * (K // QK) * BLOCK_BYTES[fmt] + 4 * K * N + 4 * M * N

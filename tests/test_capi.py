@@ -1,0 +1,103 @@
+"""The C ABI library without a GPU: it loads, exports every symbol the header
+declares, and rejects bad arguments before touching the device."""
+
+import ctypes
+import re
+
+import pytest
+
+from qgemv_roofline_b200 import _lib
+
+
+def declared_symbols():
+    text = open(_lib.HEADER).read()
+    return re.findall(r"QGEMV_API\s+[\w\s\*]+?\b(qgemv_\w+)\s*\(", text)
+
+
+def test_library_loads_and_exports_every_declared_symbol():
+    lib = _lib.lib()
+    names = declared_symbols()
+    assert len(names) >= 15
+    for n in names:
+        assert hasattr(lib, n), n
+    # the ctypes signature table covers the whole header
+    assert set(names) == set(_lib.SIGNATURES)
+
+
+def test_version_and_status_strings():
+    lib = _lib.lib()
+    assert lib.qgemv_version() == 100
+    for code, name in _lib.STATUS_NAMES.items():
+        assert lib.qgemv_status_string(code).decode() == name
+
+
+FAKE = 0x100000  # 16-byte aligned, never dereferenced: validation fails first
+
+
+def rc(name, *args):
+    return getattr(_lib.lib(), name)(*args)
+
+
+@pytest.mark.parametrize("fn", ["qgemv_q8_0_soa", "qgemv_q4_0_soa"])
+def test_soa_validation(fn):
+    E = _lib
+    assert rc(fn, FAKE, FAKE, FAKE, FAKE, 64, 100, 1, 100, 64, None) == 2  # K % 32
+    assert "multiple of 32" in E.last_error()
+    assert rc(fn, FAKE, FAKE, FAKE, FAKE, -1, 64, 1, 64, 1, None) == 2
+    assert rc(fn, FAKE, FAKE, FAKE, FAKE, 64, 64, -1, 64, 64, None) == 2
+    assert rc(fn, None, FAKE, FAKE, FAKE, 64, 64, 1, 64, 64, None) == 1
+    assert rc(fn, FAKE, FAKE, None, FAKE, 64, 64, 1, 64, 64, None) == 1
+    assert rc(fn, FAKE + 8, FAKE, FAKE, FAKE, 64, 64, 1, 64, 64, None) == 3  # q not 16-B
+    assert rc(fn, FAKE, FAKE + 1, FAKE, FAKE, 64, 64, 1, 64, 64, None) == 3  # d not 2-B
+    assert rc(fn, FAKE, FAKE, FAKE + 2, FAKE, 64, 64, 1, 64, 64, None) == 3  # x not 4-B
+    assert rc(fn, FAKE, FAKE, FAKE, FAKE, 64, 64, 2, 32, 64, None) == 2  # ldx < K
+    assert rc(fn, FAKE, FAKE, FAKE, FAKE, 64, 64, 2, 64, 32, None) == 2  # ldy < M
+    assert rc(fn, FAKE, FAKE, FAKE, FAKE, 1 << 31, 64, 1, 64, 1, None) == 5
+    # empty work is a no-op that needs no device
+    assert rc(fn, None, None, None, None, 0, 64, 1, 64, 0, None) == 0
+    assert rc(fn, None, None, None, None, 64, 64, 0, 64, 64, None) == 0
+
+
+@pytest.mark.parametrize("fn", ["qgemv_q8_0_aos", "qgemv_q4_0_aos"])
+def test_aos_validation(fn):
+    assert rc(fn, FAKE, FAKE, FAKE, 64, 48, 1, 48, 64, None) == 2
+    assert rc(fn, None, FAKE, FAKE, 64, 64, 1, 64, 64, None) == 1
+    assert rc(fn, FAKE + 2, FAKE, FAKE, 64, 64, 1, 64, 64, None) == 3
+
+
+def test_quantize_repack_roof_validation():
+    assert rc("qgemv_quantize_soa", 5, FAKE, 4, 64, 64, FAKE, FAKE, None) == 7  # format
+    assert rc("qgemv_quantize_soa", 8, FAKE, 4, 40, 40, FAKE, FAKE, None) == 2
+    assert rc("qgemv_quantize_soa", 4, FAKE, 4, 64, 32, FAKE, FAKE, None) == 2  # ldw < K
+    assert rc("qgemv_quantize_soa", 4, None, 4, 64, 64, FAKE, FAKE, None) == 1
+    assert rc("qgemv_quantize_aos", 8, FAKE + 1, 4, 64, 64, FAKE, None) == 3
+    assert rc("qgemv_dequant_soa", 4, FAKE, FAKE + 1, FAKE, 4, 64, None) == 3
+    assert rc("qgemv_repack", 8, 2, FAKE, FAKE, FAKE, 4, 64, None) == 7
+    assert rc("qgemv_repack", 8, 1, None, FAKE, FAKE, 4, 64, None) == 1
+    assert rc("qgemv_roof_stream_read", FAKE, 100, FAKE, 4, None) == 2
+    assert rc("qgemv_roof_stream_read", FAKE + 4, 128, FAKE, 4, None) == 3
+    assert rc("qgemv_roof_stream_read", FAKE, 128, FAKE, 0, None) == 7
+    assert rc("qgemv_roof_bulk_read", FAKE, 128, FAKE, None, None) == 1
+    assert rc("qgemv_roof_d2d", None, FAKE, 16, None) == 1
+    assert rc("qgemv_device_info_get", 0, None) == 1
+
+
+def test_errors_are_per_thread_messages():
+    import threading
+    rc("qgemv_q8_0_soa", FAKE, FAKE, FAKE, FAKE, 64, 100, 1, 100, 64, None)
+    seen = {}
+
+    def other():
+        seen["msg"] = _lib.last_error()
+
+    t = threading.Thread(target=other)
+    t.start()
+    t.join()
+    assert seen["msg"] == ""
+    assert "multiple of 32" in _lib.last_error()
+
+
+def test_python_raises_typed_error():
+    with pytest.raises(_lib.QGemvError) as ei:
+        _lib.call("qgemv_q8_0_soa", FAKE, FAKE, FAKE, FAKE, 64, 100, 1, 100, 64, None)
+    assert ei.value.status == 2 and "QGEMV_ERR_SHAPE" in str(ei.value)

@@ -1,0 +1,171 @@
+"""GEMV parity on the GPU: the sm_100a kernels through the C ABI against the
+float64 oracle, within the north-star bound |y - y_ref| <= 1e-5 ||w_row|| ||x||
+per row and the reference gate max|err| / max|y_ref| <= 1e-5
+(tests/test_correctness.py:21 of the reference)."""
+
+import numpy as np
+import pytest
+import torch
+
+import qgemv_roofline_b200 as qg
+from oracle import qformats_oracle as o
+
+pytestmark = pytest.mark.gpu
+TOL = 1e-5
+DEV = "cuda"
+
+
+def assert_parity(fmt, q, d, X, Y, tol=TOL):
+    """q, d: numpy planes; X: [N, K] numpy; Y: result, [N, M] (or [M])."""
+    Y = np.asarray(Y, dtype=np.float64).reshape(X.shape[0], -1)
+    y_ref = o.matvec_ref(fmt, q, d, X)
+    wn = o.row_norms(fmt, q, d)
+    ok, worst = o.check_rowwise(Y, y_ref, wn, X, tol)
+    assert ok, f"row-wise bound exceeded: worst ratio {worst:.3g}"
+    ok, max_abs, max_rel = o.check_gate(Y, y_ref, tol)
+    assert ok, f"reference gate exceeded: max_rel {max_rel:.3g}"
+    return max_rel
+
+
+def to_gpu_planes(fmt, q, d):
+    return (torch.from_numpy(np.ascontiguousarray(q)).to(DEV),
+            torch.from_numpy(np.ascontiguousarray(d.view(np.float16))).to(DEV))
+
+
+def make(fmt, M, K, N, seed, scale=0.02):
+    rng = np.random.default_rng(seed)
+    W = (rng.standard_normal((M, K)) * scale).astype(np.float32)
+    X = rng.standard_normal((N, K)).astype(np.float32)
+    q, d = o.quantize(fmt, W)
+    return q, d, X
+
+
+@pytest.mark.parametrize("fmt", ["q8_0", "q4_0"])
+def test_golden_soa(golden, fmt):
+    k = "8" if fmt == "q8_0" else "4"
+    for name, g in golden.items():
+        q, d = to_gpu_planes(fmt, g["q" + k], g["d" + k])
+        X = torch.from_numpy(g["X"]).to(DEV)
+        Y = qg.qgemv(fmt, q, d, X).cpu().numpy()
+        assert_parity(fmt, g["q" + k], g["d" + k].view(np.float16), g["X"], Y)
+        ok, _, rel = o.check_gate(Y, g["y%s_f64" % k])
+        assert ok, (name, rel)
+
+
+@pytest.mark.parametrize("fmt", ["q8_0", "q4_0"])
+def test_golden_aos(golden, fmt):
+    k = "8" if fmt == "q8_0" else "4"
+    for name, g in golden.items():
+        blocks = torch.from_numpy(o.to_aos(fmt, g["q" + k], g["d" + k].view(np.float16))).to(DEV)
+        X = torch.from_numpy(g["X"]).to(DEV)
+        Y = qg.qgemv_aos(fmt, blocks, X).cpu().numpy()
+        ok, _, rel = o.check_gate(Y, g["y%s_f64" % k])
+        assert ok, (name, rel)
+
+
+SHAPES = [
+    (4096, 4096, 1), (11008, 4096, 1), (2048, 1024, 1),   # reference test shapes
+    (1, 32, 1), (3, 96, 2), (7, 96, 3), (257, 1024, 1),   # ragged / tiny
+    (1000, 11008, 1), (100, 8192, 1),                      # K not a multiple of 512
+    (512, 8192, 2), (384, 8192, 4), (320, 8192, 8), (300, 8192, 16),  # batch, K tiles
+    (200, 4096, 5), (130, 2048, 20),                        # N rounded up / > 16
+]
+
+
+@pytest.mark.parametrize("fmt", ["q8_0", "q4_0"])
+@pytest.mark.parametrize("M,K,N", SHAPES)
+def test_soa_shapes(fmt, M, K, N):
+    q, d, X = make(fmt, M, K, N, seed=M * 7 + K + N)
+    qt, dt = to_gpu_planes(fmt, q, d)
+    Y = qg.qgemv(fmt, qt, dt, torch.from_numpy(X).to(DEV)).cpu().numpy()
+    assert_parity(fmt, q, d, X, Y)
+
+
+@pytest.mark.parametrize("fmt", ["q8_0", "q4_0"])
+@pytest.mark.parametrize("M,K,N", [(4096, 4096, 1), (1000, 11008, 1), (5, 96, 3),
+                                   (300, 8192, 16), (257, 1024, 2), (130, 2048, 20)])
+def test_aos_shapes(fmt, M, K, N):
+    q, d, X = make(fmt, M, K, N, seed=M + 3 * K + N)
+    blocks = torch.from_numpy(o.to_aos(fmt, q, d)).to(DEV)
+    Y = qg.qgemv_aos(fmt, blocks, torch.from_numpy(X).to(DEV)).cpu().numpy()
+    assert_parity(fmt, q, d, X, Y)
+
+
+@pytest.mark.parametrize("fmt", ["q8_0", "q4_0"])
+def test_reference_distribution_error(fmt):
+    """U(-1, 1) weights and x, the reference's own inputs: the error is of the
+    order the reference reports (worst 5.6e-7 relative)."""
+    rng = np.random.default_rng(1234)
+    W = (rng.random((4096, 4096)) * 2 - 1).astype(np.float32)
+    X = (rng.random((1, 4096)) * 2 - 1).astype(np.float32)
+    q, d = o.quantize(fmt, W)
+    qt, dt = to_gpu_planes(fmt, q, d)
+    Y = qg.qgemv(fmt, qt, dt, torch.from_numpy(X).to(DEV)).cpu().numpy()
+    rel = assert_parity(fmt, q, d, X, Y)
+    assert rel < 2e-6
+
+
+@pytest.mark.parametrize("fmt", ["q8_0", "q4_0"])
+def test_strided_x_y_and_guard_bands(fmt):
+    M, K, N = 333, 2048, 3
+    q, d, X = make(fmt, M, K, N, seed=9)
+    qt, dt = to_gpu_planes(fmt, q, d)
+    Xbig = torch.full((N, K + 64), float("nan"), device=DEV)
+    Xbig[:, :K] = torch.from_numpy(X).to(DEV)
+    canary = -12345.0
+    Ybuf = torch.full((N + 2, M + 40), canary, device=DEV)
+    Yv = Ybuf[1:N + 1, 8:8 + M]
+    qg.qgemv(fmt, qt, dt, Xbig[:, :K], y=Yv)
+    torch.cuda.synchronize()
+    Yh = Ybuf.cpu().numpy()
+    assert_parity(fmt, q, d, X, Yh[1:N + 1, 8:8 + M])
+    mask = np.ones_like(Yh, dtype=bool)
+    mask[1:N + 1, 8:8 + M] = False
+    assert (Yh[mask] == canary).all(), "a write landed outside y"
+
+
+@pytest.mark.parametrize("fmt", ["q8_0", "q4_0"])
+def test_deterministic_and_stream(fmt):
+    q, d, X = make(fmt, 5000, 4096, 1, seed=5)
+    qt, dt = to_gpu_planes(fmt, q, d)
+    x = torch.from_numpy(X[0]).to(DEV)
+    s = torch.cuda.Stream()
+    with torch.cuda.stream(s):
+        y1 = qg.qgemv(fmt, qt, dt, x)
+        y2 = qg.qgemv(fmt, qt, dt, x)
+    s.synchronize()
+    assert torch.equal(y1, y2)
+    assert_parity(fmt, q, d, X, y1.cpu().numpy())
+
+
+def test_k_zero_gives_zeros():
+    q = torch.empty((10, 0), dtype=torch.int8, device=DEV)
+    d = torch.empty((10, 0), dtype=torch.float16, device=DEV)
+    y = torch.full((10,), 7.0, device=DEV)
+    qg.qgemv("q8_0", q, d, torch.empty(0, device=DEV), y=y)
+    assert torch.count_nonzero(y).item() == 0
+
+
+@pytest.mark.parametrize("fmt", ["q8_0", "q4_0"])
+def test_full_size_spot_rows_and_linearity(fmt):
+    """98304 x 4096 (the large config): quantize on the GPU, then check rows at
+    the start, middle and end against the oracle (on those rows' bytes), and
+    linearity y(a x1 + b x2) = a y(x1) + b y(x2) over all rows."""
+    M, K = 98304, 4096
+    g = torch.Generator(device=DEV).manual_seed(2024)
+    W = torch.randn(M, K, generator=g, device=DEV) * 0.02
+    x1 = torch.randn(K, generator=g, device=DEV)
+    x2 = torch.randn(K, generator=g, device=DEV)
+    q, d = (qg.quantize_q8_0 if fmt == "q8_0" else qg.quantize_q4_0)(W)
+    y1 = qg.qgemv(fmt, q, d, x1)
+    y2 = qg.qgemv(fmt, q, d, x2)
+    y12 = qg.qgemv(fmt, q, d, 0.5 * x1 + 2.0 * x2)
+    lin = (y12 - (0.5 * y1 + 2.0 * y2)).abs().max().item()
+    assert lin <= 1e-5 * (0.5 * y1.abs().max().item() + 2.0 * y2.abs().max().item()) * 10
+    rows = np.r_[0:64, M // 2 - 32:M // 2 + 32, M - 64:M]
+    Wh = W[torch.from_numpy(rows).to(DEV)].cpu().numpy()
+    qo, do = o.quantize(fmt, Wh)
+    qh, dh = q[torch.from_numpy(rows).to(DEV)].cpu().numpy(), d[torch.from_numpy(rows).to(DEV)].cpu().numpy()
+    assert np.array_equal(qh, qo) and np.array_equal(dh.view(np.uint16), do.view(np.uint16))
+    X = x1.cpu().numpy()[None, :]
+    assert_parity(fmt, qo, do, X, y1.cpu().numpy()[rows][None, :])
