@@ -120,6 +120,13 @@ QGEMV_API int qgemv_soa_variant(int format, int variant, int32_t grid, const voi
                                 const void* d, const float* x, float* y, int64_t M, int64_t K,
                                 void* stream);
 
+/* Device-side error word of the current device: kernels whose waits are
+ * bounded (the TMA-fed GEMV, whose mbarrier waits give up after ~1 s) record
+ * QGEMV_ERR_TIMEOUT there instead of hanging.  Returns QGEMV_OK when it is
+ * clear, else the recorded status; clear = 1 resets it.  Synchronises
+ * `stream`. */
+QGEMV_API int qgemv_check_device_error(int clear, void* stream);
+
 /* ------------------------------------------------------- quantize / repack --- */
 
 /* GPU quantizer, byte-identical to quantize_q8_0 / quantize_q4_0 of the

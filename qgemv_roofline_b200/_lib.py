@@ -81,6 +81,7 @@ SIGNATURES = {
     "qgemv_soa_variant_name": ([ctypes.c_int], ctypes.c_char_p),
     "qgemv_soa_variant": ([ctypes.c_int, ctypes.c_int, _i32, _vp, _vp, _vp, _vp, _i64, _i64, _vp],
                           ctypes.c_int),
+    "qgemv_check_device_error": ([ctypes.c_int, _vp], ctypes.c_int),
     "qgemv_quantize_soa": ([ctypes.c_int, _vp, _i64, _i64, _i64, _vp, _vp, _vp], ctypes.c_int),
     "qgemv_quantize_aos": ([ctypes.c_int, _vp, _i64, _i64, _i64, _vp, _vp], ctypes.c_int),
     "qgemv_dequant_soa": ([ctypes.c_int, _vp, _vp, _vp, _i64, _i64, _vp], ctypes.c_int),

@@ -84,8 +84,13 @@ int allow_max_smem(const void* func, const DeviceInfo& dev) {
   std::lock_guard<std::mutex> lk(g_mu);
   auto key = std::make_pair(func, dev.device);
   if (g_smem_set.count(key)) return OK;
-  const cudaError_t e =
-      cudaFuncSetAttribute(func, cudaFuncAttributeMaxDynamicSharedMemorySize, dev.smem_optin);
+  // dynamic + static shared memory must stay within the opt-in maximum
+  cudaFuncAttributes fa;
+  cudaError_t e = cudaFuncGetAttributes(&fa, func);
+  if (e != cudaSuccess)
+    return set_error(ERR_CUDA, "cudaFuncGetAttributes: %s", cudaGetErrorString(e));
+  e = cudaFuncSetAttribute(func, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           dev.smem_optin - (int)fa.sharedSizeBytes);
   if (e != cudaSuccess)
     return set_error(ERR_CUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
   g_smem_set.insert(key);
@@ -138,7 +143,7 @@ int gemv_entry(int fmt, bool aos, const void* q, const void* d, const float* x, 
   if (int rc = check_mk(M, K)) return rc;
   if (ncols < 0) return set_error(ERR_SHAPE, "ncols=%d is negative", ncols);
   if (M == 0 || ncols == 0) return OK;
-  if (!x || !y) return set_error(ERR_NULL, "x and y must not be NULL");
+  if (!y || (K > 0 && !x)) return set_error(ERR_NULL, "x and y must not be NULL");
   if (K > 0 && (!q || (!aos && !d)))
     return set_error(ERR_NULL, aos ? "blocks must not be NULL" : "q and d must not be NULL");
   if (ncols > 1 && ldx < K)
@@ -152,7 +157,8 @@ int gemv_entry(int fmt, bool aos, const void* q, const void* d, const float* x, 
   if (K > 0 && misaligned(q, 16))
     return set_error(ERR_ALIGN, aos ? "blocks must be 16-byte aligned" : "q must be 16-byte aligned");
   if (!aos && K > 0 && misaligned(d, 2)) return set_error(ERR_ALIGN, "d must be 2-byte aligned");
-  if (misaligned(x, 4) || misaligned(y, 4)) return set_error(ERR_ALIGN, "x and y must be 4-byte aligned");
+  if (misaligned(x, 4) || misaligned(y, 4))
+    return set_error(ERR_ALIGN, "x and y must be 4-byte aligned");
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (K == 0) return fill_zero_rows(y, M, ncols, ldy, st);
   GemvCall c;
@@ -251,6 +257,13 @@ QGEMV_API int qgemv_soa_variant(int format, int variant, int32_t grid, const voi
   c.ldy = M;
   c.grid_override = grid;
   return gemv_soa_variant(format, variant, c, static_cast<cudaStream_t>(stream));
+}
+
+QGEMV_API int qgemv_check_device_error(int clear, void* stream) {
+  int v = 0;
+  if (int rc = read_device_error(clear, static_cast<cudaStream_t>(stream), &v)) return rc;
+  if (v) return set_error(v, "a kernel reported %s on the device", qgemv_status_string(v));
+  return OK;
 }
 
 QGEMV_API int qgemv_q8_0_aos(const void* blocks, const float* x, float* y, int64_t M, int64_t K,

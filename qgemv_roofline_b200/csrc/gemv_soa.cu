@@ -176,7 +176,11 @@ int launch_soa(const GemvCall& c, const DeviceInfo& dev, cudaStream_t st) {
 // of accumulators grows.
 template <int FMT>
 int dispatch_soa(const GemvCall& c, const DeviceInfo& dev, cudaStream_t st) {
-  if (c.N <= 1) return launch_soa<FMT, 1, 4, 2>(c, dev, st);
+  if (c.N <= 1) {
+    const int rc = gemv_soa_tma(FMT, c, st);  // the TMA-fed kernel when the shape allows
+    if (rc != -1) return rc;
+    return FMT == 8 ? launch_soa<FMT, 1, 4, 1>(c, dev, st) : launch_soa<FMT, 1, 8, 1>(c, dev, st);
+  }
   if (c.N <= 2) return launch_soa<FMT, 2, 4, 2>(c, dev, st);
   if (c.N <= 4) return launch_soa<FMT, 4, 2, 2>(c, dev, st);
   if (c.N <= 8) return launch_soa<FMT, 8, 2, 1>(c, dev, st);
@@ -192,6 +196,7 @@ struct Variant {
 constexpr Variant kVariants[] = {
     {"soa_r1u4", 1, 4}, {"soa_r2u2", 2, 2}, {"soa_r2u4", 2, 4}, {"soa_r4u1", 4, 1},
     {"soa_r4u2", 4, 2}, {"soa_r4u4", 4, 4}, {"soa_r8u1", 8, 1}, {"soa_r8u2", 8, 2},
+    {"soa_tma", 0, 0},
 };
 constexpr int kNumVariants = sizeof(kVariants) / sizeof(kVariants[0]);
 
@@ -205,7 +210,11 @@ int launch_variant(int v, const GemvCall& c, const DeviceInfo& dev, cudaStream_t
     case 4: return launch_soa<FMT, 1, 4, 2>(c, dev, st);
     case 5: return launch_soa<FMT, 1, 4, 4>(c, dev, st);
     case 6: return launch_soa<FMT, 1, 8, 1>(c, dev, st);
-    default: return launch_soa<FMT, 1, 8, 2>(c, dev, st);
+    case 7: return launch_soa<FMT, 1, 8, 2>(c, dev, st);
+    default: {
+      const int rc = gemv_soa_tma(FMT, c, st);
+      return rc == -1 ? set_error(ERR_UNSUPPORTED, "shape not handled by the TMA kernel") : rc;
+    }
   }
 }
 

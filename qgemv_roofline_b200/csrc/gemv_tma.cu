@@ -1,0 +1,358 @@
+// TMA-fed single-column q8_0 / q4_0 SoA GEMV for sm_100a (the hot path).
+//
+// Same computation as the reference's qgemv_q8_v5_soa_smem /
+// qgemv_q4_v5_soa_smem (src/qgemv_kernels.cuh:264-291, 323-352), built
+// around the B200 memory engine instead of per-thread loads:
+//
+//  * One CTA per SM, 17 warps.  Warp 0 is the producer: one lane streams
+//    tiles of TR consecutive rows (quant bytes and fp16 scales, each tile
+//    two contiguous 1-D bulk copies, cp.async.bulk) into an S-stage
+//    shared-memory ring; completion is tracked by per-stage "full" mbarriers
+//    (expect_tx) and stages are recycled through "empty" mbarriers.  Each CTA
+//    owns a contiguous row range, so it streams one contiguous region.
+//  * Warps 1..16 consume.  Consumer warp w owns K slice (w % KS) and row
+//    group (w / KS): its lanes keep the x values of their chunks of that
+//    slice in registers for the whole kernel (x is never re-read), read the
+//    quants of R rows at a time from shared memory, convert them exactly
+//    (gemv_core.cuh) and accumulate with packed f32x2 FMAs.  The R partial
+//    dots are reduced across the warp with a transposing butterfly (about
+//    R + 4 shuffles for R rows) and stored per (row, slice) in shared memory.
+//  * When a stage is released, the producer warp sums the KS slice partials
+//    of each row in a fixed order (deterministic) and writes y.
+//  * Every mbarrier wait is bounded (~1 s).  On a timeout the CTA raises a
+//    shared abort flag so no thread waits further, the producer waits
+//    (bounded) for the copies it issued, the kernel returns, and a device
+//    error word (read by qgemv_check_device_error) records QGEMV_ERR_TIMEOUT.
+//
+// Requirements (checked on the host, otherwise the caller uses the
+// register-streaming kernel): one column, K % 256 == 0 (so scale rows are
+// 16-byte multiples), K <= 16384.
+#include "gemv_core.cuh"
+#include "qgemv_internal.h"
+
+#include <algorithm>
+
+namespace qg {
+
+__device__ int g_device_error = 0;
+
+namespace {
+
+constexpr int CONSUMERS = 16;
+constexpr int TMA_THREADS = 32 * (CONSUMERS + 1);
+constexpr int MAX_STAGES = 8;
+constexpr long long SPIN_LIMIT = 2000000000LL;  // clock64 cycles, ~1 s
+
+__device__ __forceinline__ uint32_t saddr(const void* p) {
+  return (uint32_t)__cvta_generic_to_shared(p);
+}
+
+__device__ __forceinline__ bool mbar_try(uint32_t bar, uint32_t parity) {
+  uint32_t done;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
+      " selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(done)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return done != 0;
+}
+
+// Bounded wait; gives up early when another thread raised the abort flag.
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort_flag) {
+  const long long t0 = clock64();
+  while (!mbar_try(bar, parity)) {
+    if (*abort_flag) return false;
+    if (clock64() - t0 > SPIN_LIMIT) {
+      *abort_flag = 1;
+      atomicExch(&g_device_error, (int)ERR_TIMEOUT);
+      return false;
+    }
+  }
+  return true;
+}
+
+__device__ __forceinline__ void mbar_wait_drain(uint32_t bar, uint32_t parity) {
+  const long long t0 = clock64();
+  while (!mbar_try(bar, parity) && clock64() - t0 < SPIN_LIMIT) {
+  }
+}
+
+__device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t bytes,
+                                         uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::
+          "r"(dst),
+      "l"(src), "r"(bytes), "r"(bar)
+      : "memory");
+}
+
+// Sums v[0..R) across the 32 lanes.  Afterwards lane L holds the total of row
+// row_of_lane<R>(L); lanes with (L & (32 / R - 1)) == 0 are the owners.
+template <int R>
+__device__ __forceinline__ float reduce_rows(float (&v)[R], int lane) {
+  if (R == 1) return warp_sum(v[0]);
+  // Halve the set of rows at each step: lanes with the bit set keep the upper
+  // half and receive their partner's copy of it.
+#pragma unroll
+  for (int h = R / 2, bit = 16; h >= 1; h /= 2, bit /= 2) {
+    const bool up = (lane & bit) != 0;
+#pragma unroll
+    for (int i = 0; i < h; ++i) {
+      const float keep = up ? v[i + h] : v[i];
+      const float send = up ? v[i] : v[i + h];
+      v[i] = keep + __shfl_xor_sync(0xffffffffu, send, bit);
+    }
+  }
+  float s = v[0];
+#pragma unroll
+  for (int bit = 32 / R / 2; bit >= 1; bit /= 2) s += __shfl_xor_sync(0xffffffffu, s, bit);
+  return s;
+}
+
+template <int R>
+__device__ __forceinline__ int row_of_lane(int lane) {
+  // bits 4, 3, ... of the lane (most significant first) select the row
+  int r = 0;
+#pragma unroll
+  for (int h = R / 2, bit = 16; h >= 1; h /= 2, bit /= 2) r += (lane & bit) ? h : 0;
+  return r;
+}
+
+struct TmaArgs {
+  const uint8_t* q;
+  const unsigned short* d;
+  const float* x;
+  float* y;
+  int M, K, TR, S, KS;
+};
+
+template <int FMT, int CPL, int R>
+__global__ void __launch_bounds__(TMA_THREADS, 1) k_gemv_tma(const TmaArgs p) {
+  using F = Fmt<FMT>;
+  constexpr int EPC = F::ELEMS_PER_CHUNK;
+  extern __shared__ __align__(128) uint8_t sm[];
+  __shared__ __align__(8) unsigned long long full[MAX_STAGES];
+  __shared__ __align__(8) unsigned long long empty[MAX_STAGES];
+  __shared__ int abort_flag;
+
+  const int K = p.K, TR = p.TR, S = p.S, KS = p.KS;
+  const int QB = K / F::ROW_DIV;  // quant bytes per row
+  const int DB = K / 16;          // scale bytes per row
+  const int STG = TR * (QB + DB);
+  float* part = reinterpret_cast<float*>(sm + (size_t)S * STG);  // [S][TR][KS]
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int a = (int)((int64_t)p.M * blockIdx.x / gridDim.x);
+  const int nrows = (int)((int64_t)p.M * (blockIdx.x + 1) / gridDim.x) - a;
+  const int ntiles = (nrows + TR - 1) / TR;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S; ++s) {
+      asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(saddr(&full[s])));
+      asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(saddr(&empty[s])),
+                   "r"(CONSUMERS));
+    }
+    abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  __syncthreads();
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    int last_issued[MAX_STAGES];
+    for (int s = 0; s < MAX_STAGES; ++s) last_issued[s] = -1;
+    bool ok = true;
+    for (int t = 0; t < ntiles + S && ok; ++t) {
+      const int s = t % S;
+      if (t >= S) {
+        const int tt = t - S;  // tile whose stage is recycled now
+        // every lane waits (acquire), since every lane reads the partials
+        ok = __all_sync(0xffffffffu,
+                        mbar_wait(saddr(&empty[s]), (uint32_t)((tt / S) & 1), &abort_flag));
+        if (!ok) break;
+        const int r0 = tt * TR, nr = min(TR, nrows - r0);
+        const float* ps = part + (size_t)s * TR * KS;
+        for (int i = lane; i < nr; i += 32) {
+          float v = 0.0f;
+          for (int k = 0; k < KS; ++k) v += ps[i * KS + k];
+          p.y[a + r0 + i] = v;
+        }
+        __syncwarp();
+      }
+      if (t < ntiles) {
+        if (lane == 0) {
+          const int r0 = t * TR, nr = min(TR, nrows - r0);
+          const uint32_t qb = (uint32_t)nr * QB, db = (uint32_t)nr * DB;
+          const uint32_t bar = saddr(&full[s]);
+          uint8_t* st = sm + (size_t)s * STG;
+          asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar),
+                       "r"(qb + db)
+                       : "memory");
+          bulk_g2s(saddr(st), p.q + (int64_t)(a + r0) * QB, qb, bar);
+          bulk_g2s(saddr(st + (size_t)TR * QB),
+                   reinterpret_cast<const uint8_t*>(p.d) + (int64_t)(a + r0) * DB, db, bar);
+        }
+        last_issued[s] = t;
+      }
+    }
+    if (!ok && lane == 0) {
+      // aborted: wait (bounded) for every copy still in flight into our smem
+      for (int s = 0; s < S; ++s)
+        if (last_issued[s] >= 0)
+          mbar_wait_drain(saddr(&full[s]), (uint32_t)((last_issued[s] / S) & 1));
+    }
+    return;
+  }
+
+  // -------------------------------------------------------------- consumers
+  const int cw = warp - 1;
+  const int ks = cw % KS, rg = cw / KS, RG = CONSUMERS / KS;
+  const int nch = K / EPC;
+  int cidx[CPL];
+  bool cval[CPL];
+  float xr[CPL][EPC];
+#pragma unroll
+  for (int j = 0; j < CPL; ++j) {
+    const int c = ks * 32 * CPL + lane + 32 * j;
+    cval[j] = c < nch;
+    cidx[j] = cval[j] ? c : 0;
+#pragma unroll
+    for (int e = 0; e < EPC; ++e) {
+      if (FMT == 8) {
+        xr[j][e] = cval[j] ? p.x[c * 16 + e] : 0.0f;
+      } else {
+        // e = 8t + pos: nibble order of cvt_q4_word, divided by 2^shift
+        const int t = e >> 3, pp = e & 7;
+        const int jj = 4 * t + (pp >> 1) + 16 * (pp & 1);
+        xr[j][e] = cval[j] ? p.x[c * 32 + jj] * __int_as_float((127 - q4_shift(pp)) << 23) : 0.0f;
+      }
+    }
+  }
+
+  for (int t = 0; t < ntiles; ++t) {
+    const int s = t % S;
+    // every lane waits on the barrier, so the bulk-copied bytes are visible to it
+    if (!__all_sync(0xffffffffu, mbar_wait(saddr(&full[s]), (uint32_t)((t / S) & 1), &abort_flag)))
+      break;
+    const int nr = min(TR, nrows - t * TR);
+    const uint8_t* st = sm + (size_t)s * STG;
+    const uint8_t* sd = st + (size_t)TR * QB;
+    float* ps = part + (size_t)s * TR * KS;
+    for (int r0 = rg * R; r0 < nr; r0 += RG * R) {
+      float acc[R];
+#pragma unroll
+      for (int r = 0; r < R; ++r) acc[r] = 0.0f;
+#pragma unroll
+      for (int j = 0; j < CPL; ++j) {
+        if (!cval[j]) continue;
+        uint4 wv[R];
+        float dv[R];
+#pragma unroll
+        for (int r = 0; r < R; ++r) {
+          const int rr = min(r0 + r, nr - 1);
+          wv[r] = *reinterpret_cast<const uint4*>(st + (size_t)rr * QB + cidx[j] * 16);
+          const unsigned short db = *reinterpret_cast<const unsigned short*>(
+              sd + (size_t)rr * DB + (FMT == 8 ? (cidx[j] >> 1) : cidx[j]) * 2);
+          dv[r] = r0 + r < nr ? half_bits_to_float(db) : 0.0f;
+        }
+        float2 s2[R];
+#pragma unroll
+        for (int r = 0; r < R; ++r) s2[r] = make_float2(0.0f, 0.0f);
+#pragma unroll
+        for (int tw = 0; tw < 4; ++tw) {
+          if (FMT == 8) {
+            const float2 xa = make_float2(xr[j][4 * tw], xr[j][4 * tw + 1]);
+            const float2 xb = make_float2(xr[j][4 * tw + 2], xr[j][4 * tw + 3]);
+#pragma unroll
+            for (int r = 0; r < R; ++r) {
+              float2 ca, cb;
+              cvt_q8_word(word_of(wv[r], tw), ca, cb);
+              s2[r] = __ffma2_rn(ca, xa, s2[r]);
+              s2[r] = __ffma2_rn(cb, xb, s2[r]);
+            }
+          } else {
+#pragma unroll
+            for (int r = 0; r < R; ++r) {
+              float2 cv[4];
+              cvt_q4_word(word_of(wv[r], tw), cv);
+#pragma unroll
+              for (int i = 0; i < 4; ++i)
+                s2[r] = __ffma2_rn(cv[i], make_float2(xr[j][8 * tw + 2 * i], xr[j][8 * tw + 2 * i + 1]),
+                                   s2[r]);
+            }
+          }
+        }
+#pragma unroll
+        for (int r = 0; r < R; ++r) acc[r] = fmaf(dv[r], s2[r].x + s2[r].y, acc[r]);
+      }
+      const float v = reduce_rows<R>(acc, lane);
+      const int r = row_of_lane<R>(lane);
+      if ((lane & (32 / R - 1)) == 0 && r0 + r < nr) ps[(r0 + r) * KS + ks] = v;
+    }
+    __syncwarp();
+    if (lane == 0)
+      asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(saddr(&empty[s])) : "memory");
+  }
+}
+
+template <int FMT, int CPL, int R>
+int launch_tma(const GemvCall& c, const DeviceInfo& dev, cudaStream_t st) {
+  using F = Fmt<FMT>;
+  constexpr int EPC = F::ELEMS_PER_CHUNK;
+  auto kern = k_gemv_tma<FMT, CPL, R>;
+  const int K = (int)c.K, M = (int)c.M;
+  const int nch = K / EPC;
+  int KS = 1;
+  while (KS * 32 * CPL < nch) KS *= 2;
+  if (KS > CONSUMERS) return -1;
+  const int RG = CONSUMERS / KS;
+  const int row_bytes = K / F::ROW_DIV + K / 16;
+  const int unit = RG * R;
+  const int TR = unit * std::max(1, (32 * 1024) / (unit * row_bytes));
+  const int STG = TR * row_bytes;
+  if (int rc = allow_max_smem(reinterpret_cast<const void*>(kern), dev)) return rc;
+  cudaFuncAttributes fa;
+  if (cudaFuncGetAttributes(&fa, kern) != cudaSuccess) return check_launch("cudaFuncGetAttributes");
+  const int avail = dev.smem_optin - (int)fa.sharedSizeBytes;
+  const int S = std::min(MAX_STAGES, avail / (STG + TR * KS * 4));
+  if (S < 2) return -1;
+  const size_t smem = (size_t)S * (STG + TR * KS * 4);
+  int grid = std::min(dev.sms, (M + TR - 1) / TR);
+  if (c.grid_override > 0) grid = c.grid_override;
+  TmaArgs a{static_cast<const uint8_t*>(c.q), static_cast<const unsigned short*>(c.d), c.x, c.y,
+            M, K, TR, S, KS};
+  kern<<<grid, TMA_THREADS, smem, st>>>(a);
+  return check_launch("k_gemv_tma");
+}
+
+}  // namespace
+
+bool tma_eligible(const GemvCall& c) {
+  return c.N == 1 && c.K >= 256 && c.K % 256 == 0 && c.K <= 16384 && c.M >= 1;
+}
+
+// Returns OK, an error status, or -1 when the shape is not handled here.
+int gemv_soa_tma(int fmt, const GemvCall& c, cudaStream_t st) {
+  if (!tma_eligible(c)) return -1;
+  DeviceInfo dev;
+  if (int rc = current_device_info(dev)) return rc;
+  return fmt == 8 ? launch_tma<8, 2, 2>(c, dev, st) : launch_tma<4, 1, 4>(c, dev, st);
+}
+
+int read_device_error(int clear, cudaStream_t st, int* out) {
+  int v = 0;
+  cudaError_t e = cudaMemcpyFromSymbolAsync(&v, g_device_error, sizeof(int), 0,
+                                            cudaMemcpyDeviceToHost, st);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+  if (e != cudaSuccess) return set_error(ERR_CUDA, "reading the device error word: %s", cudaGetErrorString(e));
+  if (clear && v) {
+    const int zero = 0;
+    e = cudaMemcpyToSymbolAsync(g_device_error, &zero, sizeof(int), 0, cudaMemcpyHostToDevice, st);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+    if (e != cudaSuccess) return set_error(ERR_CUDA, "clearing the device error word: %s", cudaGetErrorString(e));
+  }
+  *out = v;
+  return OK;
+}
+
+}  // namespace qg

@@ -42,6 +42,10 @@ struct GemvCall {
 
 int gemv_soa(int fmt, const GemvCall& c, cudaStream_t st);
 int gemv_soa_variant(int fmt, int variant, const GemvCall& c, cudaStream_t st);
+// TMA-fed single-column kernel; returns -1 when the shape is not eligible.
+int gemv_soa_tma(int fmt, const GemvCall& c, cudaStream_t st);
+bool tma_eligible(const GemvCall& c);
+int read_device_error(int clear, cudaStream_t st, int* out);
 int soa_variant_count();
 const char* soa_variant_name(int v);
 int gemv_aos(int fmt, const GemvCall& c, cudaStream_t st);

@@ -169,3 +169,37 @@ def test_full_size_spot_rows_and_linearity(fmt):
     assert np.array_equal(qh, qo) and np.array_equal(dh.view(np.uint16), do.view(np.uint16))
     X = x1.cpu().numpy()[None, :]
     assert_parity(fmt, qo, do, X, y1.cpu().numpy()[rows][None, :])
+
+
+@pytest.mark.parametrize("fmt", ["q8_0", "q4_0"])
+@pytest.mark.parametrize("M,K", [(1, 256), (5, 4096), (149, 512), (300, 16384), (7, 16384),
+                                 (2000, 11008), (1500, 8192), (3001, 4096)])
+def test_single_column_tma_shapes(fmt, M, K):
+    """Shapes of the TMA-fed kernel (K % 256 == 0): tiny, ragged tiles, the
+    largest K, K = 11008 (idle slices), fewer tiles than SMs."""
+    q, d, X = make(fmt, M, K, 1, seed=M + K)
+    qt, dt = to_gpu_planes(fmt, q, d)
+    y = qg.qgemv(fmt, qt, dt, torch.from_numpy(X[0]).to(DEV)).cpu().numpy()
+    assert_parity(fmt, q, d, X, y[None, :])
+    qg._lib.call("qgemv_check_device_error", 1, None)
+
+
+@pytest.mark.parametrize("fmt", ["q8_0", "q4_0"])
+def test_kernel_ladder_variants(fmt):
+    """Every selectable single-column configuration (the --only ladder)."""
+    lib = qg._lib.lib()
+    M, K = 777, 4096
+    q, d, X = make(fmt, M, K, 1, seed=31)
+    qt, dt = to_gpu_planes(fmt, q, d)
+    x = torch.from_numpy(X[0]).to(DEV)
+    for v in range(lib.qgemv_soa_variant_count()):
+        for grid in (0, 3):
+            y = torch.full((M,), float("nan"), device=DEV)
+            qg._lib.call("qgemv_soa_variant", qg._lib.FORMAT_CODE[fmt], v, grid, qt.data_ptr(),
+                         dt.data_ptr(), x.data_ptr(), y.data_ptr(), M, K, None)
+            assert_parity(fmt, q, d, X, y.cpu().numpy()[None, :])
+    qg._lib.call("qgemv_check_device_error", 1, None)
+
+
+def test_device_error_word_is_clear():
+    qg._lib.call("qgemv_check_device_error", 0, None)
