@@ -119,6 +119,77 @@ __device__ __forceinline__ int row_of_lane(int lane) {
   return r;
 }
 
+// --- integer dot products -------------------------------------------------
+// a: four quants (signed int8 for q8_0, unsigned bytes for q4_0 nibbles);
+// b: four signed bytes of one plane of the fixed-point activations.
+__device__ __forceinline__ int dp4a_ss(uint32_t a, uint32_t b, int c) {
+  int d;
+  asm("dp4a.s32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+  return d;
+}
+__device__ __forceinline__ int dp4a_us(uint32_t a, uint32_t b, int c) {
+  int d;
+  asm("dp4a.u32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+  return d;
+}
+
+// One 32-element block of x in block fixed point: X_j = rint(x_j * 2^(30-e))
+// with |x_j| < 2^e, so |X_j| < 2^30, split into four balanced signed byte
+// planes X_j = sum_p D_p,j 2^(8p), D in [-128, 127].  pl[w][p] packs
+// D_p of elements 4w..4w+3.  The block's dot with integer quants q is then
+// sum_p 2^(8p) * sum_w dp4a(q_w, pl[w][p]): exact in int32 per plane.
+struct XPlanes {
+  uint32_t pl[8][4];
+  int e;        // block exponent (|x| < 2^e), -149 for an all-zero block
+  float bias;   // 128 * sum_j X_j, for the q4_0 offset (see consumer)
+  bool finite;
+};
+
+__device__ __forceinline__ void make_planes(const float* __restrict__ xb, XPlanes& o) {
+  float v[32];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const float4 f = *reinterpret_cast<const float4*>(xb + 4 * i);
+    v[4 * i] = f.x; v[4 * i + 1] = f.y; v[4 * i + 2] = f.z; v[4 * i + 3] = f.w;
+  }
+  float amax = 0.0f;
+  bool finite = true;
+#pragma unroll
+  for (int j = 0; j < 32; ++j) {
+    finite = finite && isfinite(v[j]);
+    amax = fmaxf(amax, fabsf(v[j]));
+  }
+  int e = -149;
+  if (amax > 0.0f && finite) frexpf(amax, &e);  // amax = m 2^e, m in [0.5, 1)
+  o.e = e;
+  o.finite = finite;
+  long long sum = 0;
+  int X[32];
+#pragma unroll
+  for (int j = 0; j < 32; ++j) {
+    X[j] = finite ? __float2int_rn(ldexpf(v[j], 30 - e)) : 0;
+    sum += X[j];
+  }
+  o.bias = 128.0f * (float)sum;
+#pragma unroll
+  for (int w = 0; w < 8; ++w) {
+    uint32_t pk[4] = {0u, 0u, 0u, 0u};
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      int r = X[4 * w + u];
+#pragma unroll
+      for (int pl = 0; pl < 3; ++pl) {
+        const int dgt = (int)(signed char)(r & 0xFF);  // balanced digit
+        pk[pl] |= (uint32_t)(dgt & 0xFF) << (8 * u);
+        r = (r - dgt) >> 8;                             // exact
+      }
+      pk[3] |= (uint32_t)(r & 0xFF) << (8 * u);         // |r| <= 64
+    }
+#pragma unroll
+    for (int pl = 0; pl < 4; ++pl) o.pl[w][pl] = pk[pl];
+  }
+}
+
 struct TmaArgs {
   const uint8_t* q;
   const unsigned short* d;
@@ -127,7 +198,11 @@ struct TmaArgs {
   int M, K, TR, S, KS;
 };
 
-template <int FMT, int CPL, int R>
+// MODE 0: quants converted to fp32 with the magic-number trick and FFMA2
+//         accumulation (x as fp32).
+// MODE 1: x in block fixed point (four byte planes) and exact dp4a integer
+//         dot products per 32-weight block, fp32 across blocks.
+template <int FMT, int MODE, int R>
 __global__ void __launch_bounds__(TMA_THREADS, 1) k_gemv_tma(const TmaArgs p) {
   using F = Fmt<FMT>;
   constexpr int EPC = F::ELEMS_PER_CHUNK;
@@ -135,6 +210,7 @@ __global__ void __launch_bounds__(TMA_THREADS, 1) k_gemv_tma(const TmaArgs p) {
   __shared__ __align__(8) unsigned long long full[MAX_STAGES];
   __shared__ __align__(8) unsigned long long empty[MAX_STAGES];
   __shared__ int abort_flag;
+  __shared__ int xexp_max;  // MODE 1: max block exponent of x
 
   const int K = p.K, TR = p.TR, S = p.S, KS = p.KS;
   const int QB = K / F::ROW_DIV;  // quant bytes per row
@@ -153,6 +229,7 @@ __global__ void __launch_bounds__(TMA_THREADS, 1) k_gemv_tma(const TmaArgs p) {
                    "r"(CONSUMERS));
     }
     abort_flag = 0;
+    xexp_max = -149;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   __syncthreads();
@@ -172,10 +249,11 @@ __global__ void __launch_bounds__(TMA_THREADS, 1) k_gemv_tma(const TmaArgs p) {
         if (!ok) break;
         const int r0 = tt * TR, nr = min(TR, nrows - r0);
         const float* ps = part + (size_t)s * TR * KS;
+        const int yexp = MODE == 1 ? xexp_max - 30 : 0;
         for (int i = lane; i < nr; i += 32) {
           float v = 0.0f;
           for (int k = 0; k < KS; ++k) v += ps[i * KS + k];
-          p.y[a + r0 + i] = v;
+          p.y[a + r0 + i] = MODE == 1 ? ldexpf(v, yexp) : v;
         }
         __syncwarp();
       }
@@ -208,25 +286,43 @@ __global__ void __launch_bounds__(TMA_THREADS, 1) k_gemv_tma(const TmaArgs p) {
   const int cw = warp - 1;
   const int ks = cw % KS, rg = cw / KS, RG = CONSUMERS / KS;
   const int nch = K / EPC;
-  int cidx[CPL];
-  bool cval[CPL];
-  float xr[CPL][EPC];
+  // MODE 0: a lane owns 16-byte chunk c (16 q8_0 / 32 q4_0 weights).
+  // MODE 1: a lane owns 32-weight block c (32 bytes q8_0, 16 bytes q4_0).
+  const int nunits = MODE == 0 ? nch : K / QK;
+  const int c = ks * 32 + lane;
+  const bool cval = c < nunits;
+  const int cidx = cval ? c : 0;
+
+  float xr[MODE == 0 ? EPC : 1];
+  XPlanes xp;
+  float xsc = 0.0f;
+  if (MODE == 0) {
 #pragma unroll
-  for (int j = 0; j < CPL; ++j) {
-    const int c = ks * 32 * CPL + lane + 32 * j;
-    cval[j] = c < nch;
-    cidx[j] = cval[j] ? c : 0;
-#pragma unroll
-    for (int e = 0; e < EPC; ++e) {
+    for (int e = 0; e < (MODE == 0 ? EPC : 1); ++e) {
       if (FMT == 8) {
-        xr[j][e] = cval[j] ? p.x[c * 16 + e] : 0.0f;
+        xr[e] = cval ? p.x[cidx * 16 + e] : 0.0f;
       } else {
         // e = 8t + pos: nibble order of cvt_q4_word, divided by 2^shift
         const int t = e >> 3, pp = e & 7;
         const int jj = 4 * t + (pp >> 1) + 16 * (pp & 1);
-        xr[j][e] = cval[j] ? p.x[c * 32 + jj] * __int_as_float((127 - q4_shift(pp)) << 23) : 0.0f;
+        xr[e] = cval ? p.x[cidx * 32 + jj] * __int_as_float((127 - q4_shift(pp)) << 23) : 0.0f;
       }
     }
+  } else {
+    if (cval) {
+      make_planes(p.x + cidx * 32, xp);
+    } else {
+      for (int w = 0; w < 8; ++w)
+        for (int pl = 0; pl < 4; ++pl) xp.pl[w][pl] = 0u;
+      xp.e = -149;
+      xp.bias = 0.0f;
+      xp.finite = true;
+    }
+    atomicMax(&xexp_max, xp.e);
+    asm volatile("bar.sync 1, %0;" ::"r"(CONSUMERS * 32) : "memory");  // consumers only
+    // per-block scale 2^(e - max e) (q4_0: / 16, see below); NaN for a
+    // non-finite block so that y is NaN, as a float dot product would be
+    xsc = xp.finite ? ldexpf(1.0f, xp.e - xexp_max - (FMT == 4 ? 4 : 0)) : __int_as_float(0x7FC00000);
   }
 
   for (int t = 0; t < ntiles; ++t) {
@@ -242,48 +338,97 @@ __global__ void __launch_bounds__(TMA_THREADS, 1) k_gemv_tma(const TmaArgs p) {
       float acc[R];
 #pragma unroll
       for (int r = 0; r < R; ++r) acc[r] = 0.0f;
-#pragma unroll
-      for (int j = 0; j < CPL; ++j) {
-        if (!cval[j]) continue;
-        uint4 wv[R];
+      if (cval) {
         float dv[R];
 #pragma unroll
         for (int r = 0; r < R; ++r) {
           const int rr = min(r0 + r, nr - 1);
-          wv[r] = *reinterpret_cast<const uint4*>(st + (size_t)rr * QB + cidx[j] * 16);
           const unsigned short db = *reinterpret_cast<const unsigned short*>(
-              sd + (size_t)rr * DB + (FMT == 8 ? (cidx[j] >> 1) : cidx[j]) * 2);
+              sd + (size_t)rr * DB + (MODE == 0 && FMT == 8 ? (cidx >> 1) : cidx) * 2);
           dv[r] = r0 + r < nr ? half_bits_to_float(db) : 0.0f;
         }
-        float2 s2[R];
+        if (MODE == 0) {
+          uint4 wv[R];
 #pragma unroll
-        for (int r = 0; r < R; ++r) s2[r] = make_float2(0.0f, 0.0f);
+          for (int r = 0; r < R; ++r)
+            wv[r] = *reinterpret_cast<const uint4*>(st + (size_t)min(r0 + r, nr - 1) * QB + cidx * 16);
+          float2 s2[R];
 #pragma unroll
-        for (int tw = 0; tw < 4; ++tw) {
-          if (FMT == 8) {
-            const float2 xa = make_float2(xr[j][4 * tw], xr[j][4 * tw + 1]);
-            const float2 xb = make_float2(xr[j][4 * tw + 2], xr[j][4 * tw + 3]);
+          for (int r = 0; r < R; ++r) s2[r] = make_float2(0.0f, 0.0f);
 #pragma unroll
-            for (int r = 0; r < R; ++r) {
-              float2 ca, cb;
-              cvt_q8_word(word_of(wv[r], tw), ca, cb);
-              s2[r] = __ffma2_rn(ca, xa, s2[r]);
-              s2[r] = __ffma2_rn(cb, xb, s2[r]);
-            }
-          } else {
+          for (int tw = 0; tw < 4; ++tw) {
+            if (FMT == 8) {
+              const float2 xa = make_float2(xr[(4 * tw) % EPC], xr[(4 * tw + 1) % EPC]);
+              const float2 xb = make_float2(xr[(4 * tw + 2) % EPC], xr[(4 * tw + 3) % EPC]);
 #pragma unroll
-            for (int r = 0; r < R; ++r) {
-              float2 cv[4];
-              cvt_q4_word(word_of(wv[r], tw), cv);
+              for (int r = 0; r < R; ++r) {
+                float2 ca, cb;
+                cvt_q8_word(word_of(wv[r], tw), ca, cb);
+                s2[r] = __ffma2_rn(ca, xa, s2[r]);
+                s2[r] = __ffma2_rn(cb, xb, s2[r]);
+              }
+            } else {
 #pragma unroll
-              for (int i = 0; i < 4; ++i)
-                s2[r] = __ffma2_rn(cv[i], make_float2(xr[j][8 * tw + 2 * i], xr[j][8 * tw + 2 * i + 1]),
-                                   s2[r]);
+              for (int r = 0; r < R; ++r) {
+                float2 cv[4];
+                cvt_q4_word(word_of(wv[r], tw), cv);
+#pragma unroll
+                for (int i = 0; i < 4; ++i)
+                  s2[r] = __ffma2_rn(cv[i], make_float2(xr[(8 * tw + 2 * i) % EPC],
+                                                        xr[(8 * tw + 2 * i + 1) % EPC]), s2[r]);
+              }
             }
           }
-        }
 #pragma unroll
-        for (int r = 0; r < R; ++r) acc[r] = fmaf(dv[r], s2[r].x + s2[r].y, acc[r]);
+          for (int r = 0; r < R; ++r) acc[r] = dv[r] * (s2[r].x + s2[r].y);
+        } else {
+#pragma unroll
+          for (int r = 0; r < R; ++r) {
+            const uint8_t* rowp = st + (size_t)min(r0 + r, nr - 1) * QB;
+            int S0 = 0, S1 = 0, S2 = 0, S3 = 0;
+            if (FMT == 8) {
+              // 32 signed quants: words w = 0..7 hold elements 4w..4w+3
+              const uint4 u0 = *reinterpret_cast<const uint4*>(rowp + cidx * 32);
+              const uint4 u1 = *reinterpret_cast<const uint4*>(rowp + cidx * 32 + 16);
+              const uint32_t wq[8] = {u0.x, u0.y, u0.z, u0.w, u1.x, u1.y, u1.z, u1.w};
+#pragma unroll
+              for (int w = 0; w < 8; ++w) {
+                S0 = dp4a_ss(wq[w], xp.pl[w][0], S0);
+                S1 = dp4a_ss(wq[w], xp.pl[w][1], S1);
+                S2 = dp4a_ss(wq[w], xp.pl[w][2], S2);
+                S3 = dp4a_ss(wq[w], xp.pl[w][3], S3);
+              }
+            } else {
+              // 16 bytes: word t holds elements 4t..4t+3 (low nibbles) and
+              // 16+4t..16+4t+3 (high nibbles, taken in place as 16 * n)
+              const uint4 u = *reinterpret_cast<const uint4*>(rowp + cidx * 16);
+              const uint32_t wq[4] = {u.x, u.y, u.z, u.w};
+              int H0 = 0, H1 = 0, H2 = 0, H3 = 0;
+#pragma unroll
+              for (int t4 = 0; t4 < 4; ++t4) {
+                const uint32_t lo = wq[t4] & 0x0F0F0F0Fu, hi = wq[t4] & 0xF0F0F0F0u;
+                S0 = dp4a_us(lo, xp.pl[t4][0], S0);
+                S1 = dp4a_us(lo, xp.pl[t4][1], S1);
+                S2 = dp4a_us(lo, xp.pl[t4][2], S2);
+                S3 = dp4a_us(lo, xp.pl[t4][3], S3);
+                H0 = dp4a_us(hi, xp.pl[t4 + 4][0], H0);
+                H1 = dp4a_us(hi, xp.pl[t4 + 4][1], H1);
+                H2 = dp4a_us(hi, xp.pl[t4 + 4][2], H2);
+                H3 = dp4a_us(hi, xp.pl[t4 + 4][3], H3);
+              }
+              // 16 * sum n X per plane
+              S0 = (S0 << 4) + H0; S1 = (S1 << 4) + H1;
+              S2 = (S2 << 4) + H2; S3 = (S3 << 4) + H3;
+            }
+            float Fv = (float)S3;
+            Fv = fmaf(Fv, 256.0f, (float)S2);
+            Fv = fmaf(Fv, 256.0f, (float)S1);
+            Fv = fmaf(Fv, 256.0f, (float)S0);
+            // q4_0: 16 * sum (n - 8) X = 16 sum n X - 128 sum X; the 1/16 is in xsc
+            if (FMT == 4) Fv -= xp.bias;
+            acc[r] = (dv[r] * xsc) * Fv;
+          }
+        }
       }
       const float v = reduce_rows<R>(acc, lane);
       const int r = row_of_lane<R>(lane);
@@ -295,15 +440,14 @@ __global__ void __launch_bounds__(TMA_THREADS, 1) k_gemv_tma(const TmaArgs p) {
   }
 }
 
-template <int FMT, int CPL, int R>
+template <int FMT, int MODE, int R>
 int launch_tma(const GemvCall& c, const DeviceInfo& dev, cudaStream_t st) {
   using F = Fmt<FMT>;
-  constexpr int EPC = F::ELEMS_PER_CHUNK;
-  auto kern = k_gemv_tma<FMT, CPL, R>;
+  auto kern = k_gemv_tma<FMT, MODE, R>;
   const int K = (int)c.K, M = (int)c.M;
-  const int nch = K / EPC;
+  const int nunits = MODE == 0 ? K / F::ELEMS_PER_CHUNK : K / QK;
   int KS = 1;
-  while (KS * 32 * CPL < nch) KS *= 2;
+  while (KS * 32 < nunits) KS *= 2;
   if (KS > CONSUMERS) return -1;
   const int RG = CONSUMERS / KS;
   const int row_bytes = K / F::ROW_DIV + K / 16;
@@ -336,7 +480,15 @@ int gemv_soa_tma(int fmt, const GemvCall& c, cudaStream_t st) {
   if (!tma_eligible(c)) return -1;
   DeviceInfo dev;
   if (int rc = current_device_info(dev)) return rc;
-  return fmt == 8 ? launch_tma<8, 2, 2>(c, dev, st) : launch_tma<4, 1, 4>(c, dev, st);
+  return fmt == 8 ? launch_tma<8, 1, 4>(c, dev, st) : launch_tma<4, 1, 4>(c, dev, st);
+}
+
+int gemv_soa_tma_mode(int fmt, int mode, const GemvCall& c, cudaStream_t st) {
+  if (!tma_eligible(c)) return -1;
+  DeviceInfo dev;
+  if (int rc = current_device_info(dev)) return rc;
+  if (mode == 0) return fmt == 8 ? launch_tma<8, 0, 2>(c, dev, st) : launch_tma<4, 0, 4>(c, dev, st);
+  return fmt == 8 ? launch_tma<8, 1, 4>(c, dev, st) : launch_tma<4, 1, 4>(c, dev, st);
 }
 
 int read_device_error(int clear, cudaStream_t st, int* out) {
