@@ -12,9 +12,13 @@ HBM; x is replicated; the step needs no collective (an NCCL all-gather of y is
 timed separately and reported beside it).  Total work is fixed as N grows
 ("strong" scaling).
 
-Every rank keeps C copies of its weight slices and step i reads copy i % C,
-with C chosen so that the bytes streamed between two reads of the same copy
-are >= 4x the 126 MB L2 (the weights are never timed from L2).
+Every rank keeps C_f copies of each format's weight slice and call i of that
+format reads copy i % C_f, with C_f chosen so that the bytes streamed between
+two reads of the same copy are >= 4x the 126 MB L2 (the weights are never
+timed from L2).  The K timed steps are issued as K q8_0 calls back to back,
+then K q4_0 calls back to back (events only at the start, between the two
+groups and at the end), so each group's launches overlap the previous
+launch's tail the way a caller's stream of GEMVs does.
 
 Printed (rank 0, one JSON line): the whole-job algorithmic GB/s (weights
 M*K*(34|18)/32 + x 4*K + y 4*M per call) over the max-over-ranks device time
@@ -78,8 +82,9 @@ def workload_config(args, world, rows, copies=None):
     }
     if copies is not None:
         cfg["weight_copies_rotated"] = copies
-        cfg["l2"] = (f"inputs larger than L2: {copies} rotated weight copies, >= 4x the "
+        cfg["l2"] = ("inputs larger than L2: rotated weight copies per format, >= 4x the "
                      "126 MB L2 streamed between reads of one copy; no flush")
+        cfg["timed_order"] = "K q8_0 calls back to back, then K q4_0 calls"
     return cfg
 
 
@@ -268,7 +273,7 @@ def main():
     r0, r1 = M * rank // world, M * (rank + 1) // world
     rows = r1 - r0
     step_bytes_rank = alg_bytes("q8_0", rows, K) + alg_bytes("q4_0", rows, K)
-    copies = max(2, math.ceil(4 * L2_BYTES / (wbytes("q8_0", rows, K) + wbytes("q4_0", rows, K))))
+    ncopies = {f: max(2, math.ceil(4 * L2_BYTES / wbytes(f, rows, K))) for f in ("q8_0", "q4_0")}
 
     # weights: this rank's rows of W, generated and quantized on the GPU
     g = torch.Generator(device=dev).manual_seed(SEED + 7919 * rank)
@@ -276,12 +281,13 @@ def main():
     x = torch.randn(K, generator=torch.Generator(device=dev).manual_seed(SEED), device=dev)
     mats = {}
     for fmt in ("q8_0", "q4_0"):
+        c = ncopies[fmt]
         if args.layout == "soa":
             q, d = (qg.quantize_q8_0 if fmt == "q8_0" else qg.quantize_q4_0)(W)
-            mats[fmt] = [(q, d)] + [(q.clone(), d.clone()) for _ in range(copies - 1)]
+            mats[fmt] = [(q, d)] + [(q.clone(), d.clone()) for _ in range(c - 1)]
         else:
             b = (qg.quantize_q8_0_aos if fmt == "q8_0" else qg.quantize_q4_0_aos)(W)
-            mats[fmt] = [b] + [b.clone() for _ in range(copies - 1)]
+            mats[fmt] = [b] + [b.clone() for _ in range(c - 1)]
     del W
     ys = {f: torch.empty(rows, device=dev) for f in mats}
     calls = [{"fmt": f, "layout": args.layout, "copies": mats[f], "M": rows, "K": K,
@@ -306,7 +312,7 @@ def main():
         pass
     barrier()
     with ClockSampler(uuid) as sampler:
-        total_ms, per_ms = time_steps(calls, args.warmup, args.steps)
+        total_ms, per_ms = time_steps(calls, args.warmup, args.steps, grouped=True)
         barrier()
     clocks = sampler.summary()
     total_ms, q8_ms, q4_ms = max_over_ranks([total_ms, per_ms[0], per_ms[1]])
@@ -362,7 +368,7 @@ def main():
               for f in mats}
         mq = {f: [m] for f, m in mq.items()}
         for f in mats:
-            for c in range(1, copies):
+            for c in range(1, ncopies[f]):
                 if args.layout == "soa":
                     mq[f].append(qg.QuantizedMatrix(f, rows, K, "soa", q=mats[f][c][0],
                                                     d=mats[f][c][1]))
@@ -377,7 +383,7 @@ def main():
         def e2e_step(i):
             xd.copy_(xh, non_blocking=True)
             for f in ("q8_0", "q4_0"):
-                y = mq[f][i % copies].matvec(xd, ys[f])
+                y = mq[f][i % ncopies[f]].matvec(xd, ys[f])
                 yh[f].copy_(y, non_blocking=True)
             st.synchronize()
 
@@ -409,7 +415,7 @@ def main():
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": total_ms / K_steps,
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
             "dtype": "fp32", "data": "synthetic (seeded N(0, 0.02) weights, N(0, 1) x)",
-            "config": workload_config(args, world, rows, copies),
+            "config": workload_config(args, world, rows, ncopies),
             "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e,
             "gpu_launches": 2 * K_steps * world, "clocks": clocks,
             "per_format": per_format, **extras,

@@ -185,13 +185,17 @@ typedef struct qgemv_call_desc {
 } qgemv_call_desc;
 
 /* Timing harness (replaces time_kernel, src/bench.cu:134-156): issues
- * `warmup` untimed steps, then `steps` steps back to back on `stream`; a step
- * runs every call of `calls` once.  A CUDA event is recorded before the first
- * timed step and after every call.  ms_out[0] = total device time of the timed
- * steps; ms_out[1 + j] = summed device time of call j (ncalls + 1 floats).
- * Synchronises `stream` before returning. */
+ * `warmup` untimed steps, then `steps` timed steps on `stream`; a step runs
+ * every call of `calls` once (call j on copy step % ncopies).
+ * grouped = 0: steps in order, a CUDA event before the first step and after
+ *              every call; ms_out[1 + j] = summed device time of call j.
+ * grouped = 1: all `steps` launches of call 0 back to back, then of call 1,
+ *              ...; events only between groups; ms_out[1 + j] = device time
+ *              of group j.
+ * ms_out[0] = total device time (ncalls + 1 floats).  Synchronises `stream`
+ * before returning. */
 QGEMV_API int qgemv_time_steps(const qgemv_call_desc* calls, int32_t ncalls, int32_t warmup,
-                               int32_t steps, void* stream, float* ms_out);
+                               int32_t steps, int32_t grouped, void* stream, float* ms_out);
 
 #ifdef __cplusplus
 }

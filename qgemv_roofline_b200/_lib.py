@@ -89,7 +89,7 @@ SIGNATURES = {
     "qgemv_roof_stream_read": ([_vp, _sz, _vp, _i32, _vp], ctypes.c_int),
     "qgemv_roof_bulk_read": ([_vp, _sz, _vp, _vp, _vp], ctypes.c_int),
     "qgemv_roof_d2d": ([_vp, _vp, _sz, _vp], ctypes.c_int),
-    "qgemv_time_steps": ([ctypes.POINTER(CallDesc), _i32, _i32, _i32, _vp,
+    "qgemv_time_steps": ([ctypes.POINTER(CallDesc), _i32, _i32, _i32, _i32, _vp,
                           ctypes.POINTER(ctypes.c_float)], ctypes.c_int),
 }
 

@@ -58,10 +58,24 @@ __device__ __forceinline__ bool mbar_try(uint32_t bar, uint32_t parity) {
   return done != 0;
 }
 
+// try_wait with a suspend-time hint: the thread sleeps in hardware until the
+// phase completes (or about 0.5 ms pass), instead of spinning on the barrier.
+__device__ __forceinline__ bool mbar_try_sleep(uint32_t bar, uint32_t parity) {
+  uint32_t done;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n"
+      " selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(done)
+      : "r"(bar), "r"(parity), "r"(500000u)
+      : "memory");
+  return done != 0;
+}
+
 // Bounded wait; gives up early when another thread raised the abort flag.
 __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort_flag) {
+  if (mbar_try_sleep(bar, parity)) return true;
   const long long t0 = clock64();
-  while (!mbar_try(bar, parity)) {
+  while (!mbar_try_sleep(bar, parity)) {
     if (*abort_flag) return false;
     if (clock64() - t0 > SPIN_LIMIT) {
       *abort_flag = 1;
@@ -121,10 +135,21 @@ __device__ __forceinline__ int row_of_lane(int lane) {
 
 // --- integer dot products -------------------------------------------------
 // a: four quants (signed int8 for q8_0, unsigned bytes for q4_0 nibbles);
-// b: four signed bytes of one plane of the fixed-point activations.
+// b: four bytes of one plane of the fixed-point activations (planes 0-2 are
+// unsigned, plane 3 is signed).
+__device__ __forceinline__ int dp4a_su(uint32_t a, uint32_t b, int c) {
+  int d;
+  asm("dp4a.s32.u32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+  return d;
+}
 __device__ __forceinline__ int dp4a_ss(uint32_t a, uint32_t b, int c) {
   int d;
   asm("dp4a.s32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+  return d;
+}
+__device__ __forceinline__ uint32_t dp4a_uu(uint32_t a, uint32_t b, uint32_t c) {
+  uint32_t d;
+  asm("dp4a.u32.u32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
   return d;
 }
 __device__ __forceinline__ int dp4a_us(uint32_t a, uint32_t b, int c) {
@@ -134,9 +159,10 @@ __device__ __forceinline__ int dp4a_us(uint32_t a, uint32_t b, int c) {
 }
 
 // One 32-element block of x in block fixed point: X_j = rint(x_j * 2^(30-e))
-// with |x_j| < 2^e, so |X_j| < 2^30, split into four balanced signed byte
-// planes X_j = sum_p D_p,j 2^(8p), D in [-128, 127].  pl[w][p] packs
-// D_p of elements 4w..4w+3.  The block's dot with integer quants q is then
+// with |x_j| < 2^e, so |X_j| < 2^30.  X_j = X3 2^24 + X2 2^16 + X1 2^8 + X0
+// with X0..X2 the unsigned low bytes of X_j and X3 its (signed) top byte, so
+// the planes are just the bytes of the two's-complement X_j.  pl[w][p] packs
+// byte p of elements 4w..4w+3.  A block's dot with integer quants q is
 // sum_p 2^(8p) * sum_w dp4a(q_w, pl[w][p]): exact in int32 per plane.
 struct XPlanes {
   uint32_t pl[8][4];
@@ -152,41 +178,36 @@ __device__ __forceinline__ void make_planes(const float* __restrict__ xb, XPlane
     const float4 f = *reinterpret_cast<const float4*>(xb + 4 * i);
     v[4 * i] = f.x; v[4 * i + 1] = f.y; v[4 * i + 2] = f.z; v[4 * i + 3] = f.w;
   }
-  float amax = 0.0f;
-  bool finite = true;
+  uint32_t amax = 0u;  // bits of max |x| (ordered like the values for non-NaN)
 #pragma unroll
-  for (int j = 0; j < 32; ++j) {
-    finite = finite && isfinite(v[j]);
-    amax = fmaxf(amax, fabsf(v[j]));
-  }
+  for (int j = 0; j < 32; ++j) amax = max(amax, __float_as_uint(v[j]) & 0x7FFFFFFFu);
+  o.finite = amax < 0x7F800000u;
   int e = -149;
-  if (amax > 0.0f && finite) frexpf(amax, &e);  // amax = m 2^e, m in [0.5, 1)
+  if (amax >= 0x00800000u) e = (int)(amax >> 23) - 126;  // normal: amax = 0.1m * 2^e
+  else if (amax != 0u) frexpf(__uint_as_float(amax), &e);  // subnormal block maximum
+  if (!o.finite) e = 0;
   o.e = e;
-  o.finite = finite;
-  long long sum = 0;
   int X[32];
+  float sum = 0.0f;
+  if (e >= -97) {
+    const float sc = __uint_as_float((uint32_t)(157 - e) << 23);  // 2^(30 - e), exact
 #pragma unroll
-  for (int j = 0; j < 32; ++j) {
-    X[j] = finite ? __float2int_rn(ldexpf(v[j], 30 - e)) : 0;
-    sum += X[j];
+    for (int j = 0; j < 32; ++j) X[j] = o.finite ? __float2int_rn(v[j] * sc) : 0;
+  } else {
+#pragma unroll
+    for (int j = 0; j < 32; ++j) X[j] = __float2int_rn(ldexpf(v[j], 30 - e));
   }
-  o.bias = 128.0f * (float)sum;
+#pragma unroll
+  for (int j = 0; j < 32; ++j) sum += (float)X[j];
+  o.bias = 128.0f * sum;
 #pragma unroll
   for (int w = 0; w < 8; ++w) {
-    uint32_t pk[4] = {0u, 0u, 0u, 0u};
 #pragma unroll
-    for (int u = 0; u < 4; ++u) {
-      int r = X[4 * w + u];
-#pragma unroll
-      for (int pl = 0; pl < 3; ++pl) {
-        const int dgt = (int)(signed char)(r & 0xFF);  // balanced digit
-        pk[pl] |= (uint32_t)(dgt & 0xFF) << (8 * u);
-        r = (r - dgt) >> 8;                             // exact
-      }
-      pk[3] |= (uint32_t)(r & 0xFF) << (8 * u);         // |r| <= 64
+    for (int pl = 0; pl < 4; ++pl) {
+      const uint32_t sel = (uint32_t)pl | ((uint32_t)(pl + 4) << 4);
+      o.pl[w][pl] = __byte_perm(__byte_perm(X[4 * w], X[4 * w + 1], sel),
+                                __byte_perm(X[4 * w + 2], X[4 * w + 3], sel), 0x5410);
     }
-#pragma unroll
-    for (int pl = 0; pl < 4; ++pl) o.pl[w][pl] = pk[pl];
   }
 }
 
@@ -233,6 +254,12 @@ __global__ void __launch_bounds__(TMA_THREADS, 1) k_gemv_tma(const TmaArgs p) {
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   __syncthreads();
+  // Programmatic dependent launch: the next kernel on the stream may be
+  // scheduled now.  It only prefetches weights before its own
+  // griddepcontrol.wait, and this kernel never writes weights; x and y are
+  // touched only after this kernel's own wait (below), which returns once the
+  // previous kernel has completed and its writes are visible.
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
@@ -241,6 +268,8 @@ __global__ void __launch_bounds__(TMA_THREADS, 1) k_gemv_tma(const TmaArgs p) {
     bool ok = true;
     for (int t = 0; t < ntiles + S && ok; ++t) {
       const int s = t % S;
+      // the first S tiles (weights only) are prefetched before the dependency
+      if (t == S) asm volatile("griddepcontrol.wait;" ::: "memory");
       if (t >= S) {
         const int tt = t - S;  // tile whose stage is recycled now
         // every lane waits (acquire), since every lane reads the partials
@@ -249,11 +278,18 @@ __global__ void __launch_bounds__(TMA_THREADS, 1) k_gemv_tma(const TmaArgs p) {
         if (!ok) break;
         const int r0 = tt * TR, nr = min(TR, nrows - r0);
         const float* ps = part + (size_t)s * TR * KS;
-        const int yexp = MODE == 1 ? xexp_max - 30 : 0;
+        // MODE 1: y = v * 2^(max e - 30), applied as two exact power-of-two
+        // factors so neither constant over- or underflows
+        float f1 = 1.0f, f2 = 1.0f;
+        if (MODE == 1) {
+          const int yexp = xexp_max - 30, h1 = yexp / 2;
+          f1 = ldexpf(1.0f, h1);
+          f2 = ldexpf(1.0f, yexp - h1);
+        }
         for (int i = lane; i < nr; i += 32) {
           float v = 0.0f;
           for (int k = 0; k < KS; ++k) v += ps[i * KS + k];
-          p.y[a + r0 + i] = MODE == 1 ? ldexpf(v, yexp) : v;
+          p.y[a + r0 + i] = (v * f1) * f2;
         }
         __syncwarp();
       }
@@ -297,6 +333,7 @@ __global__ void __launch_bounds__(TMA_THREADS, 1) k_gemv_tma(const TmaArgs p) {
   XPlanes xp;
   float xsc = 0.0f;
   if (MODE == 0) {
+    asm volatile("griddepcontrol.wait;" ::: "memory");
 #pragma unroll
     for (int e = 0; e < (MODE == 0 ? EPC : 1); ++e) {
       if (FMT == 8) {
@@ -309,6 +346,7 @@ __global__ void __launch_bounds__(TMA_THREADS, 1) k_gemv_tma(const TmaArgs p) {
       }
     }
   } else {
+    asm volatile("griddepcontrol.wait;" ::: "memory");  // x may be the previous kernel's y
     if (cval) {
       make_planes(p.x + cidx * 32, xp);
     } else {
@@ -393,9 +431,9 @@ __global__ void __launch_bounds__(TMA_THREADS, 1) k_gemv_tma(const TmaArgs p) {
               const uint32_t wq[8] = {u0.x, u0.y, u0.z, u0.w, u1.x, u1.y, u1.z, u1.w};
 #pragma unroll
               for (int w = 0; w < 8; ++w) {
-                S0 = dp4a_ss(wq[w], xp.pl[w][0], S0);
-                S1 = dp4a_ss(wq[w], xp.pl[w][1], S1);
-                S2 = dp4a_ss(wq[w], xp.pl[w][2], S2);
+                S0 = dp4a_su(wq[w], xp.pl[w][0], S0);
+                S1 = dp4a_su(wq[w], xp.pl[w][1], S1);
+                S2 = dp4a_su(wq[w], xp.pl[w][2], S2);
                 S3 = dp4a_ss(wq[w], xp.pl[w][3], S3);
               }
             } else {
@@ -403,27 +441,28 @@ __global__ void __launch_bounds__(TMA_THREADS, 1) k_gemv_tma(const TmaArgs p) {
               // 16+4t..16+4t+3 (high nibbles, taken in place as 16 * n)
               const uint4 u = *reinterpret_cast<const uint4*>(rowp + cidx * 16);
               const uint32_t wq[4] = {u.x, u.y, u.z, u.w};
-              int H0 = 0, H1 = 0, H2 = 0, H3 = 0;
+              uint32_t L0 = 0u, L1 = 0u, L2 = 0u, H0 = 0u, H1 = 0u, H2 = 0u;
+              int H3 = 0;
 #pragma unroll
               for (int t4 = 0; t4 < 4; ++t4) {
                 const uint32_t lo = wq[t4] & 0x0F0F0F0Fu, hi = wq[t4] & 0xF0F0F0F0u;
-                S0 = dp4a_us(lo, xp.pl[t4][0], S0);
-                S1 = dp4a_us(lo, xp.pl[t4][1], S1);
-                S2 = dp4a_us(lo, xp.pl[t4][2], S2);
+                L0 = dp4a_uu(lo, xp.pl[t4][0], L0);
+                L1 = dp4a_uu(lo, xp.pl[t4][1], L1);
+                L2 = dp4a_uu(lo, xp.pl[t4][2], L2);
                 S3 = dp4a_us(lo, xp.pl[t4][3], S3);
-                H0 = dp4a_us(hi, xp.pl[t4 + 4][0], H0);
-                H1 = dp4a_us(hi, xp.pl[t4 + 4][1], H1);
-                H2 = dp4a_us(hi, xp.pl[t4 + 4][2], H2);
+                H0 = dp4a_uu(hi, xp.pl[t4 + 4][0], H0);
+                H1 = dp4a_uu(hi, xp.pl[t4 + 4][1], H1);
+                H2 = dp4a_uu(hi, xp.pl[t4 + 4][2], H2);
                 H3 = dp4a_us(hi, xp.pl[t4 + 4][3], H3);
               }
-              // 16 * sum n X per plane
-              S0 = (S0 << 4) + H0; S1 = (S1 << 4) + H1;
-              S2 = (S2 << 4) + H2; S3 = (S3 << 4) + H3;
+              // 16 * sum n X per plane (all below 2^21 in magnitude)
+              S0 = (int)((L0 << 4) + H0); S1 = (int)((L1 << 4) + H1);
+              S2 = (int)((L2 << 4) + H2); S3 = (S3 << 4) + H3;
             }
-            float Fv = (float)S3;
-            Fv = fmaf(Fv, 256.0f, (float)S2);
-            Fv = fmaf(Fv, 256.0f, (float)S1);
-            Fv = fmaf(Fv, 256.0f, (float)S0);
+            // fold the planes pairwise in int32 (|S3 * 256 + S2| < 2^30), then
+            // one fp32 combination: F = hi * 2^16 + lo
+            const int hi = (S3 << 8) + S2, lo = (S1 << 8) + S0;
+            float Fv = fmaf((float)hi, 65536.0f, (float)lo);
             // q4_0: 16 * sum (n - 8) X = 16 sum n X - 128 sum X; the 1/16 is in xsc
             if (FMT == 4) Fv -= xp.bias;
             acc[r] = (dv[r] * xsc) * Fv;
@@ -465,14 +504,26 @@ int launch_tma(const GemvCall& c, const DeviceInfo& dev, cudaStream_t st) {
   if (c.grid_override > 0) grid = c.grid_override;
   TmaArgs a{static_cast<const uint8_t*>(c.q), static_cast<const unsigned short*>(c.d), c.x, c.y,
             M, K, TR, S, KS};
-  kern<<<grid, TMA_THREADS, smem, st>>>(a);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(TMA_THREADS);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, a);
+  if (e != cudaSuccess) return set_error(ERR_CUDA, "k_gemv_tma launch: %s", cudaGetErrorString(e));
   return check_launch("k_gemv_tma");
 }
 
 }  // namespace
 
 bool tma_eligible(const GemvCall& c) {
-  return c.N == 1 && c.K >= 256 && c.K % 256 == 0 && c.K <= 16384 && c.M >= 1;
+  return c.N == 1 && c.K >= 256 && c.K % 256 == 0 && c.K <= 16384 && c.M >= 1 &&
+         (reinterpret_cast<uintptr_t>(c.x) & 15) == 0;
 }
 
 // Returns OK, an error status, or -1 when the shape is not handled here.

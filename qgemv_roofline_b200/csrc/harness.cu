@@ -4,11 +4,14 @@
 // The reference bracketed every launch with its own event pair and a
 // synchronize, and re-read one weight buffer, so any matrix smaller than L2
 // was timed from L2.  Here a run is `warmup` untimed steps and then `steps`
-// timed steps issued back to back from C++ (no per-step host round trip).
-// Step i issues, for every call descriptor j, one GEMV on weight copy
-// (i % ncopies_j); a CUDA event is recorded before the first timed step and
-// after every call, so each call's device time is the gap between
-// consecutive events and the total is first-to-last.
+// timed steps issued back to back from C++ (no per-step host round trip),
+// and step i of call descriptor j uses weight copy (i % ncopies_j).
+//  * Interleaved mode: step i runs every call once, with a CUDA event after
+//    each call; a call's device time is the gap between consecutive events
+//    (exact, but an event between two launches prevents their overlap).
+//  * Grouped mode: call j's launches run back to back as one group with
+//    events only between groups, the way a caller streams many GEMVs; each
+//    launch may then overlap its start with the previous launch's tail.
 #include "qgemv_b200.h"
 
 #include <vector>
@@ -46,8 +49,8 @@ struct Events {
 using namespace qg;
 
 extern "C" QGEMV_API int qgemv_time_steps(const qgemv_call_desc* calls, int32_t ncalls,
-                                          int32_t warmup, int32_t steps, void* stream,
-                                          float* ms_out) {
+                                          int32_t warmup, int32_t steps, int32_t grouped,
+                                          void* stream, float* ms_out) {
   if (!calls || !ms_out) return set_error(ERR_NULL, "calls and ms_out must not be NULL");
   if (ncalls < 1 || ncalls > 64) return set_error(ERR_ARG, "ncalls must be in [1, 64]");
   if (warmup < 0 || steps < 1) return set_error(ERR_ARG, "need warmup >= 0 and steps >= 1");
@@ -76,6 +79,32 @@ extern "C" QGEMV_API int qgemv_time_steps(const qgemv_call_desc* calls, int32_t 
     for (int j = 0; j < ncalls; ++j)
       if (int rc = issue(calls[j], i % calls[j].ncopies, st)) return rc;
 
+  if (grouped) {
+    // Call j's `steps` launches run back to back as one group (copies still
+    // rotate); events only at group boundaries, so consecutive launches of a
+    // group can overlap their launch and prologue with the previous tail.
+    Events E;
+    E.ev.resize(ncalls + 1);
+    for (int j = 0; j <= ncalls; ++j) {
+      const cudaError_t e = cudaEventCreate(&E.ev[j]);
+      if (e != cudaSuccess) {
+        E.ev.resize(j);
+        return set_error(ERR_CUDA, "cudaEventCreate: %s", cudaGetErrorString(e));
+      }
+    }
+    if (cudaStreamSynchronize(st) != cudaSuccess) return check_launch("warm-up");
+    cudaEventRecord(E.ev[0], st);
+    for (int j = 0; j < ncalls; ++j) {
+      for (int i = 0; i < steps; ++i)
+        if (int rc = issue(calls[j], i % calls[j].ncopies, st)) return rc;
+      cudaEventRecord(E.ev[j + 1], st);
+    }
+    const cudaError_t e = cudaEventSynchronize(E.ev[ncalls]);
+    if (e != cudaSuccess) return set_error(ERR_CUDA, "timed steps: %s", cudaGetErrorString(e));
+    cudaEventElapsedTime(&ms_out[0], E.ev[0], E.ev[ncalls]);
+    for (int j = 0; j < ncalls; ++j) cudaEventElapsedTime(&ms_out[1 + j], E.ev[j], E.ev[j + 1]);
+    return check_launch("qgemv_time_steps");
+  }
   Events E;
   E.ev.resize(nev);
   for (int64_t i = 0; i < nev; ++i) {

@@ -56,13 +56,16 @@ def time_calls(fn: Callable[[int], None], calls_per_batch: int, batches: int,
     return out
 
 
-def time_steps(calls, warmup: int, steps: int, stream: int | None = None):
+def time_steps(calls, warmup: int, steps: int, stream: int | None = None,
+               grouped: bool = False):
     """Native timed loop (qgemv_time_steps in include/qgemv_b200.h).
 
     ``calls``: list of dicts with keys fmt ("q8_0"/"q4_0"), layout ("soa"/"aos"),
     copies (list of (q, d) tensor pairs for SoA, or block tensors for AoS),
     M, K, x [N, K] or [K], y.  Step i runs every call once on copy
-    i % len(copies).  Returns (total_ms, [ms per call j summed over steps]).
+    i % len(copies).  grouped=False: steps in order, an event after every
+    call; grouped=True: each call's launches back to back as one group, events
+    only between groups.  Returns (total_ms, [ms of call j summed over steps]).
     """
     import ctypes
 
@@ -95,5 +98,5 @@ def time_steps(calls, warmup: int, steps: int, stream: int | None = None):
         descs[j].x, descs[j].y = x.data_ptr(), y.data_ptr()
     out = (ctypes.c_float * (len(calls) + 1))()
     st = torch.cuda.current_stream().cuda_stream if stream is None else stream
-    _lib.call("qgemv_time_steps", descs, len(calls), warmup, steps, st, out)
+    _lib.call("qgemv_time_steps", descs, len(calls), warmup, steps, int(grouped), st, out)
     return float(out[0]), [float(out[1 + j]) for j in range(len(calls))]

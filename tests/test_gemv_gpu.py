@@ -203,3 +203,63 @@ def test_kernel_ladder_variants(fmt):
 
 def test_device_error_word_is_clear():
     qg._lib.call("qgemv_check_device_error", 0, None)
+
+
+@pytest.mark.parametrize("fmt", ["q8_0", "q4_0"])
+def test_back_to_back_dependent_calls(fmt):
+    """Six GEMVs in a row on one stream, each reading the previous output and
+    overwriting the buffer the previous one read (ping-pong), with no other
+    kernel in between: checks the ordering of overlapped launches."""
+    K = 2048
+    q, d, X = make(fmt, K, K, 1, seed=7, scale=0.02)
+    qt, dt = to_gpu_planes(fmt, q, d)
+    a = torch.from_numpy(X[0]).to(DEV)
+    b = torch.empty_like(a)
+    snaps = [a.cpu().numpy()]
+    for i in range(6):
+        src, dst = (a, b) if i % 2 == 0 else (b, a)
+        qg.qgemv(fmt, qt, dt, src, y=dst)
+    torch.cuda.synchronize()
+    # replay the chain step by step against the oracle
+    cur = snaps[0]
+    a2 = torch.from_numpy(X[0]).to(DEV)
+    b2 = torch.empty_like(a2)
+    for i in range(6):
+        src, dst = (a2, b2) if i % 2 == 0 else (b2, a2)
+        qg.qgemv(fmt, qt, dt, src, y=dst)
+        torch.cuda.synchronize()
+        out = dst.cpu().numpy()
+        assert_parity(fmt, q, d, cur[None, :], out[None, :])
+        cur = out
+    final = (b if 6 % 2 == 1 else a).cpu().numpy()
+    assert np.array_equal(final, cur), "overlapped chain differs from the synchronised one"
+
+
+@pytest.mark.parametrize("fmt", ["q8_0", "q4_0"])
+def test_unaligned_x_and_extreme_scales(fmt):
+    M, K = 300, 4096
+    q, d, X = make(fmt, M, K, 1, seed=13)
+    qt, dt = to_gpu_planes(fmt, q, d)
+    buf = torch.zeros(K + 8, device=DEV)
+    # (a smaller scale would make y subnormal: no fp32 result could then meet
+    # the bound, whose scale is far below the subnormal spacing)
+    for scale in (1.0, 1e-35, 3e30):
+        xs = (X[0].astype(np.float64) * scale).astype(np.float32)
+        buf[1:K + 1] = torch.from_numpy(xs).to(DEV)      # 4-byte aligned only
+        y1 = qg.qgemv(fmt, qt, dt, buf[1:K + 1]).cpu().numpy()
+        y2 = qg.qgemv(fmt, qt, dt, torch.from_numpy(xs).to(DEV)).cpu().numpy()  # aligned
+        for y in (y1, y2):
+            assert np.isfinite(y).all()
+            assert_parity(fmt, q, d, xs[None, :], y[None, :])
+
+
+@pytest.mark.parametrize("fmt", ["q8_0", "q4_0"])
+def test_non_finite_x_gives_non_finite_y(fmt):
+    M, K = 64, 4096
+    q, d, X = make(fmt, M, K, 1, seed=17)
+    qt, dt = to_gpu_planes(fmt, q, d)
+    for bad in (float("inf"), float("nan")):
+        xs = X[0].copy()
+        xs[100] = bad
+        y = qg.qgemv(fmt, qt, dt, torch.from_numpy(xs).to(DEV)).cpu().numpy()
+        assert not np.isfinite(y).any()
