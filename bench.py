@@ -334,7 +334,7 @@ def main():
         for f in per_format:
             per_format[f]["frac_of_stream_read_roof"] = per_format[f]["gbps_per_gpu"] / sr
     dom = "q8_0" if q8_ms >= q4_ms else "q4_0"
-    kname = f"k_gemv_{args.layout}<{8 if dom == 'q8_0' else 4}>"
+    kname = (f"k_gemv_tma<{8 if dom == 'q8_0' else 4},1,4>" if args.layout == "soa" else f"k_gemv_aos<{8 if dom == 'q8_0' else 4},1,4>")
     ach = per_format[dom]["gbps_per_gpu"]
     traffic = dram_traffic(f"{dom}_{args.layout}_{rows}x{K}")
     roofline = {"bound": "hbm", "achieved": ach, "peak": peak, "unit": "GB/s",
