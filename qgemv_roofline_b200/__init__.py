@@ -11,7 +11,7 @@ Public API (torch tensors as buffers; compute in libqgemv_b200.so):
 * multi-GPU row sharding: ``shard.ShardedQGemv``.
 """
 
-from . import _lib, gemv, qformats, roof, timing  # noqa: F401
+from . import _lib, gemv, qformats, roof, shard, timing  # noqa: F401
 from ._lib import QGemvError, device_info  # noqa: F401
 from .gemv import QuantizedMatrix, algorithmic_bytes, qgemv, qgemv_aos  # noqa: F401
 from .qformats import (QK, dequant_q4_0, dequant_q8_0, from_aos, quantize_q4_0,  # noqa: F401

@@ -1,0 +1,95 @@
+"""Row-sharded quantized GEMV across the GPUs of one node (one process per GPU).
+
+The reference is single-GPU.  For the large shapes the rows of W are split
+over the ranks of a ``torch.distributed`` process group: rank g owns rows
+``[row_range(M, g, P)]`` of W, resident in its own HBM as SoA planes (or
+ggml blocks); x is replicated (it is the caller's input, or the all-gathered
+y of the previous layer).  Each rank computes its y slice with no
+communication; an NCCL all-gather assembles the full y only when the caller
+asks for it.
+
+``local_gemv`` is the per-rank kernel call (default: the sm_100a C-ABI through
+``QuantizedMatrix.matvec``); it is a parameter so the host-side partition and
+gather logic can be exercised without a GPU.
+"""
+
+from __future__ import annotations
+
+from typing import Callable
+
+import torch
+import torch.distributed as dist
+
+from .gemv import QuantizedMatrix
+
+
+def row_range(M: int, rank: int, world: int) -> tuple[int, int]:
+    """Rows [r0, r1) of rank ``rank``: contiguous, sizes differ by at most one."""
+    if world < 1 or not 0 <= rank < world:
+        raise ValueError(f"rank {rank} out of range for world size {world}")
+    return M * rank // world, M * (rank + 1) // world
+
+
+class ShardedQGemv:
+    """This rank's row slice of a quantized [M, K] matrix.
+
+    ``forward(x, gather=False)`` returns this rank's y slice ``[rows]`` (or
+    ``[N, rows]``); ``gather=True`` returns the full ``[M]`` (``[N, M]``) y on
+    every rank, assembled with one all-gather (rank-major, padded to equal
+    slice sizes when M is not a multiple of the world size).
+    """
+
+    def __init__(self, local: QuantizedMatrix | None, M: int, K: int, fmt: str,
+                 group=None, local_gemv: Callable | None = None):
+        self.group = group
+        self.world = dist.get_world_size(group) if dist.is_initialized() else 1
+        self.rank = dist.get_rank(group) if dist.is_initialized() else 0
+        self.M, self.K, self.fmt = M, K, fmt
+        self.r0, self.r1 = row_range(M, self.rank, self.world)
+        self.local = local
+        if local is not None and (local.M != self.r1 - self.r0 or local.K != K):
+            raise ValueError(f"local slice is [{local.M}, {local.K}], expected "
+                             f"[{self.r1 - self.r0}, {K}]")
+        self.local_gemv = local_gemv or (lambda x, y=None: self.local.matvec(x, y))
+        self.slice_max = -(-M // self.world)  # ceil: padded slice for the gather
+
+    @classmethod
+    def from_full(cls, full: QuantizedMatrix, device=None, group=None) -> "ShardedQGemv":
+        """Takes this rank's rows of a full matrix (held on any device) to ``device``."""
+        world = dist.get_world_size(group) if dist.is_initialized() else 1
+        rank = dist.get_rank(group) if dist.is_initialized() else 0
+        r0, r1 = row_range(full.M, rank, world)
+        part = full.rows(r0, r1)
+        if device is not None:
+            part = part.to(device)
+        return cls(part, full.M, full.K, full.fmt, group=group)
+
+    def forward(self, x: torch.Tensor, gather: bool = False) -> torch.Tensor:
+        y = self.local_gemv(x)
+        if not gather or self.world == 1:
+            return y
+        return self.all_gather(y)
+
+    __call__ = forward
+
+    def all_gather(self, y_local: torch.Tensor) -> torch.Tensor:
+        """[rows] or [N, rows] slices of every rank -> full [M] or [N, M]."""
+        vec = y_local.dim() == 1
+        Y = y_local.unsqueeze(0) if vec else y_local
+        N, rows = Y.shape
+        P, S = self.world, self.slice_max
+        pad = torch.zeros((N, S), dtype=Y.dtype, device=Y.device)
+        pad[:, :rows] = Y
+        send = pad.t().contiguous()  # [S, N]: rank-major after the gather
+        if dist.get_backend(self.group) == "nccl":
+            out = torch.empty((P * S, N), dtype=Y.dtype, device=Y.device)
+            dist.all_gather_into_tensor(out, send, group=self.group)
+            parts = out.view(P, S, N)
+        else:
+            bufs = [torch.empty_like(send) for _ in range(P)]
+            dist.all_gather(bufs, send, group=self.group)
+            parts = torch.stack(bufs)
+        cols = [parts[g, : row_range(self.M, g, P)[1] - row_range(self.M, g, P)[0]]
+                for g in range(P)]
+        full = torch.cat(cols, dim=0).t().contiguous()  # [N, M]
+        return full[0] if vec else full

@@ -263,3 +263,15 @@ def test_non_finite_x_gives_non_finite_y(fmt):
         xs[100] = bad
         y = qg.qgemv(fmt, qt, dt, torch.from_numpy(xs).to(DEV)).cpu().numpy()
         assert not np.isfinite(y).any()
+
+
+def test_sharded_wrapper_single_process():
+    """ShardedQGemv without a process group: one shard holding every row."""
+    from qgemv_roofline_b200.shard import ShardedQGemv
+    M, K = 513, 2048
+    q, d, X = make("q8_0", M, K, 2, seed=23)
+    qt, dt = to_gpu_planes("q8_0", q, d)
+    full = qg.QuantizedMatrix("q8_0", M, K, "soa", q=qt, d=dt)
+    sh = ShardedQGemv.from_full(full, device=DEV)
+    Y = sh(torch.from_numpy(X).to(DEV), gather=True).cpu().numpy()
+    assert_parity("q8_0", q, d, X, Y)
