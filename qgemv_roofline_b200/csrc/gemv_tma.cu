@@ -11,12 +11,19 @@
 //    (expect_tx) and stages are recycled through "empty" mbarriers.  Each CTA
 //    owns a contiguous row range, so it streams one contiguous region.
 //  * Warps 1..16 consume.  Consumer warp w owns K slice (w % KS) and row
-//    group (w / KS): its lanes keep the x values of their chunks of that
-//    slice in registers for the whole kernel (x is never re-read), read the
-//    quants of R rows at a time from shared memory, convert them exactly
-//    (gemv_core.cuh) and accumulate with packed f32x2 FMAs.  The R partial
-//    dots are reduced across the warp with a transposing butterfly (about
-//    R + 4 shuffles for R rows) and stored per (row, slice) in shared memory.
+//    group (w / KS); lane l of it owns one 32-weight block of that slice.
+//    In the default mode (MODE 1) the lane converts its 32 x values once per
+//    kernel into block fixed point, X_j = rint(x_j 2^(30-e)), kept as four
+//    byte planes in registers; each block's dot with the integer quants is
+//    then exact dp4a arithmetic (q8_0: the raw int8 quants; q4_0: two masks
+//    per 8 nibbles and a per-block bias for the -8 offset), folded in int32
+//    and scaled into an fp32 accumulator.  MODE 0 (kept for the kernel
+//    ladder) unpacks quants to fp32 instead and accumulates with FFMA2.
+//    R rows are processed at a time; the R partial dots are reduced across
+//    the warp with a transposing butterfly (about R + 4 shuffles for R rows)
+//    and stored per (row, slice) in shared memory.
+//  * Programmatic dependent launch: the next launch may start once this one
+//    has set up; it prefetches only weights before griddepcontrol.wait.
 //  * When a stage is released, the producer warp sums the KS slice partials
 //    of each row in a fixed order (deterministic) and writes y.
 //  * Every mbarrier wait is bounded (~1 s).  On a timeout the CTA raises a
