@@ -38,6 +38,8 @@
 #include "qgemv_internal.h"
 
 #include <algorithm>
+#include <map>
+#include <mutex>
 
 namespace qg {
 
@@ -45,8 +47,10 @@ __device__ int g_device_error = 0;
 
 namespace {
 
-constexpr int CONSUMERS = 16;
-constexpr int TMA_THREADS = 32 * (CONSUMERS + 1);
+// Consumer warps per CTA: 16 with one CTA per SM, or 8 with two CTAs per SM
+// (each with half the shared-memory ring), which lets the next launch's CTA
+// start streaming on an SM while this launch's CTA there drains.
+constexpr int tma_threads(int cw) { return 32 * (cw + 1); }
 constexpr int MAX_STAGES = 8;
 constexpr long long SPIN_LIMIT = 2000000000LL;  // clock64 cycles, ~1 s
 
@@ -67,15 +71,24 @@ __device__ __forceinline__ bool mbar_try(uint32_t bar, uint32_t parity) {
 
 // try_wait with a suspend-time hint: the thread sleeps in hardware until the
 // phase completes (or about 0.5 ms pass), instead of spinning on the barrier.
+// Suspend-time hint of the mbarrier waits, in ns (0: plain try_wait, which the
+// measurements favoured slightly; the hint changed no timing by more than 1 %).
+#ifndef QG_MBAR_SUSPEND_NS
+#define QG_MBAR_SUSPEND_NS 0u
+#endif
 __device__ __forceinline__ bool mbar_try_sleep(uint32_t bar, uint32_t parity) {
+#if QG_MBAR_SUSPEND_NS == 0
+  return mbar_try(bar, parity);
+#else
   uint32_t done;
   asm volatile(
       "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n"
       " selp.u32 %0, 1, 0, p;\n}\n"
       : "=r"(done)
-      : "r"(bar), "r"(parity), "r"(500000u)
+      : "r"(bar), "r"(parity), "r"(QG_MBAR_SUSPEND_NS)
       : "memory");
   return done != 0;
+#endif
 }
 
 // Bounded wait; gives up early when another thread raised the abort flag.
@@ -230,15 +243,15 @@ struct TmaArgs {
 //         accumulation (x as fp32).
 // MODE 1: x in block fixed point (four byte planes) and exact dp4a integer
 //         dot products per 32-weight block, fp32 across blocks.
-template <int FMT, int MODE, int R>
-__global__ void __launch_bounds__(TMA_THREADS, 1) k_gemv_tma(const TmaArgs p) {
+template <int FMT, int MODE, int R, int CONSUMERS>
+__global__ void __launch_bounds__(tma_threads(CONSUMERS), 16 / CONSUMERS)
+k_gemv_tma(const TmaArgs p) {
   using F = Fmt<FMT>;
   constexpr int EPC = F::ELEMS_PER_CHUNK;
   extern __shared__ __align__(128) uint8_t sm[];
   __shared__ __align__(8) unsigned long long full[MAX_STAGES];
   __shared__ __align__(8) unsigned long long empty[MAX_STAGES];
   __shared__ int abort_flag;
-  __shared__ int xexp_max;  // MODE 1: max block exponent of x
 
   const int K = p.K, TR = p.TR, S = p.S, KS = p.KS;
   const int QB = K / F::ROW_DIV;  // quant bytes per row
@@ -257,7 +270,6 @@ __global__ void __launch_bounds__(TMA_THREADS, 1) k_gemv_tma(const TmaArgs p) {
                    "r"(CONSUMERS));
     }
     abort_flag = 0;
-    xexp_max = -149;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   __syncthreads();
@@ -285,18 +297,10 @@ __global__ void __launch_bounds__(TMA_THREADS, 1) k_gemv_tma(const TmaArgs p) {
         if (!ok) break;
         const int r0 = tt * TR, nr = min(TR, nrows - r0);
         const float* ps = part + (size_t)s * TR * KS;
-        // MODE 1: y = v * 2^(max e - 30), applied as two exact power-of-two
-        // factors so neither constant over- or underflows
-        float f1 = 1.0f, f2 = 1.0f;
-        if (MODE == 1) {
-          const int yexp = xexp_max - 30, h1 = yexp / 2;
-          f1 = ldexpf(1.0f, h1);
-          f2 = ldexpf(1.0f, yexp - h1);
-        }
         for (int i = lane; i < nr; i += 32) {
           float v = 0.0f;
           for (int k = 0; k < KS; ++k) v += ps[i * KS + k];
-          p.y[a + r0 + i] = (v * f1) * f2;
+          p.y[a + r0 + i] = v;
         }
         __syncwarp();
       }
@@ -338,7 +342,7 @@ __global__ void __launch_bounds__(TMA_THREADS, 1) k_gemv_tma(const TmaArgs p) {
 
   float xr[MODE == 0 ? EPC : 1];
   XPlanes xp;
-  float xsc = 0.0f;
+  float xs1 = 0.0f, xs2 = 0.0f;  // MODE 1: the block's scale 2^(e-30), as two factors
   if (MODE == 0) {
     asm volatile("griddepcontrol.wait;" ::: "memory");
 #pragma unroll
@@ -363,11 +367,14 @@ __global__ void __launch_bounds__(TMA_THREADS, 1) k_gemv_tma(const TmaArgs p) {
       xp.bias = 0.0f;
       xp.finite = true;
     }
-    atomicMax(&xexp_max, xp.e);
-    asm volatile("bar.sync 1, %0;" ::"r"(CONSUMERS * 32) : "memory");  // consumers only
-    // per-block scale 2^(e - max e) (q4_0: / 16, see below); NaN for a
-    // non-finite block so that y is NaN, as a float dot product would be
-    xsc = xp.finite ? ldexpf(1.0f, xp.e - xexp_max - (FMT == 4 ? 4 : 0)) : __int_as_float(0x7FC00000);
+    // X_j = x_j 2^(30-e): the block's dot is its integer dot times 2^(e-30)
+    // (q4_0: times 2^-4 more, see below).  Split in two exact power-of-two
+    // factors, each a normal float for every e, so the product only rounds
+    // where the true value itself under- or overflows.  NaN for a non-finite
+    // block so that y is NaN, as a float dot product would be.
+    const int t = xp.e - 30 - (FMT == 4 ? 4 : 0), h = t / 2;
+    xs1 = xp.finite ? __int_as_float((127 + h) << 23) : __int_as_float(0x7FC00000);
+    xs2 = __int_as_float((127 + t - h) << 23);
   }
 
   for (int t = 0; t < ntiles; ++t) {
@@ -470,9 +477,9 @@ __global__ void __launch_bounds__(TMA_THREADS, 1) k_gemv_tma(const TmaArgs p) {
             // one fp32 combination: F = hi * 2^16 + lo
             const int hi = (S3 << 8) + S2, lo = (S1 << 8) + S0;
             float Fv = fmaf((float)hi, 65536.0f, (float)lo);
-            // q4_0: 16 * sum (n - 8) X = 16 sum n X - 128 sum X; the 1/16 is in xsc
+            // q4_0: 16 * sum (n - 8) X = 16 sum n X - 128 sum X; the 1/16 is in xs1 xs2
             if (FMT == 4) Fv -= xp.bias;
-            acc[r] = (dv[r] * xsc) * Fv;
+            acc[r] = ((dv[r] * Fv) * xs1) * xs2;
           }
         }
       }
@@ -486,11 +493,35 @@ __global__ void __launch_bounds__(TMA_THREADS, 1) k_gemv_tma(const TmaArgs p) {
   }
 }
 
-template <int FMT, int MODE, int R>
-int launch_tma(const GemvCall& c, const DeviceInfo& dev, cudaStream_t st) {
+struct TmaPlan {
+  int grid, TR, S, KS;
+  size_t smem;
+};
+
+struct PlanKey {
+  const void* f;
+  int dev, M, K;
+  bool operator<(const PlanKey& o) const {
+    return f != o.f ? f < o.f : dev != o.dev ? dev < o.dev : M != o.M ? M < o.M : K < o.K;
+  }
+};
+std::mutex g_plan_mu;
+std::map<PlanKey, TmaPlan> g_plans;
+
+// Tile rows, stages and grid for one (kernel, device, M, K); cached, so a
+// launch costs one map lookup besides the launch itself.
+template <int FMT, int MODE, int R, int CONSUMERS>
+int plan_tma(const void* kern, int M, int K, const DeviceInfo& dev, TmaPlan* out) {
+  const PlanKey key{kern, dev.device, M, K};
+  {
+    std::lock_guard<std::mutex> lk(g_plan_mu);
+    auto it = g_plans.find(key);
+    if (it != g_plans.end()) {
+      *out = it->second;
+      return OK;
+    }
+  }
   using F = Fmt<FMT>;
-  auto kern = k_gemv_tma<FMT, MODE, R>;
-  const int K = (int)c.K, M = (int)c.M;
   const int nunits = MODE == 0 ? K / F::ELEMS_PER_CHUNK : K / QK;
   int KS = 1;
   while (KS * 32 < nunits) KS *= 2;
@@ -498,23 +529,49 @@ int launch_tma(const GemvCall& c, const DeviceInfo& dev, cudaStream_t st) {
   const int RG = CONSUMERS / KS;
   const int row_bytes = K / F::ROW_DIV + K / 16;
   const int unit = RG * R;
-  const int TR = unit * std::max(1, (32 * 1024) / (unit * row_bytes));
-  const int STG = TR * row_bytes;
-  if (int rc = allow_max_smem(reinterpret_cast<const void*>(kern), dev)) return rc;
+  const int ctas_per_sm = 16 / CONSUMERS;
+  if (int rc = allow_max_smem(kern, dev)) return rc;
   cudaFuncAttributes fa;
   if (cudaFuncGetAttributes(&fa, kern) != cudaSuccess) return check_launch("cudaFuncGetAttributes");
-  const int avail = dev.smem_optin - (int)fa.sharedSizeBytes;
-  const int S = std::min(MAX_STAGES, avail / (STG + TR * KS * 4));
+  // shared memory of one CTA when `ctas_per_sm` must fit on an SM (1 KB of
+  // each CTA's share is reserved by the hardware)
+  const int avail = (ctas_per_sm == 1 ? dev.smem_optin : (228 * 1024) / ctas_per_sm - 1024) -
+                    (int)fa.sharedSizeBytes;
+  const int tile_target = ctas_per_sm == 1 ? 32 * 1024 : 36 * 1024;
+  int TR = unit * std::max(1, tile_target / (unit * row_bytes));
+  int S = std::min(MAX_STAGES, avail / (TR * row_bytes + TR * KS * 4));
+  while (S < 2 && TR > unit) {  // very long rows: fewer rows per tile
+    TR -= unit;
+    S = std::min(MAX_STAGES, avail / (TR * row_bytes + TR * KS * 4));
+  }
   if (S < 2) return -1;
-  const size_t smem = (size_t)S * (STG + TR * KS * 4);
-  int grid = std::min(dev.sms, (M + TR - 1) / TR);
-  if (c.grid_override > 0) grid = c.grid_override;
+  TmaPlan pl;
+  pl.TR = TR;
+  pl.S = S;
+  pl.KS = KS;
+  pl.smem = (size_t)S * (TR * row_bytes + TR * KS * 4);
+  pl.grid = std::max(1, std::min(dev.sms * ctas_per_sm, (M + TR - 1) / TR));
+  std::lock_guard<std::mutex> lk(g_plan_mu);
+  g_plans[key] = pl;
+  *out = pl;
+  return OK;
+}
+
+template <int FMT, int MODE, int R, int CONSUMERS>
+int launch_tma(const GemvCall& c, const DeviceInfo& dev, cudaStream_t st) {
+  auto kern = k_gemv_tma<FMT, MODE, R, CONSUMERS>;
+  const int K = (int)c.K, M = (int)c.M;
+  TmaPlan pl;
+  if (int rc = plan_tma<FMT, MODE, R, CONSUMERS>(reinterpret_cast<const void*>(kern), M, K, dev,
+                                                  &pl))
+    return rc;
+  const int grid = c.grid_override > 0 ? c.grid_override : pl.grid;
   TmaArgs a{static_cast<const uint8_t*>(c.q), static_cast<const unsigned short*>(c.d), c.x, c.y,
-            M, K, TR, S, KS};
+            M, K, pl.TR, pl.S, pl.KS};
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(grid);
-  cfg.blockDim = dim3(TMA_THREADS);
-  cfg.dynamicSmemBytes = smem;
+  cfg.blockDim = dim3(tma_threads(CONSUMERS));
+  cfg.dynamicSmemBytes = pl.smem;
   cfg.stream = st;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
@@ -538,15 +595,24 @@ int gemv_soa_tma(int fmt, const GemvCall& c, cudaStream_t st) {
   if (!tma_eligible(c)) return -1;
   DeviceInfo dev;
   if (int rc = current_device_info(dev)) return rc;
-  return fmt == 8 ? launch_tma<8, 1, 4>(c, dev, st) : launch_tma<4, 1, 4>(c, dev, st);
+  // Two CTAs of 8 consumer warps per SM overlap one CTA's drain with the
+  // next CTA's fill; measured faster for q4_0 at every size and for q8_0 up
+  // to ~200 MB of weights.  Beyond that q8_0 streams best with one CTA of 16.
+  if (fmt == 4) return launch_tma<4, 1, 4, 8>(c, dev, st);
+  if (c.M * (c.K + c.K / 16) >= ((int64_t)256 << 20)) return launch_tma<8, 1, 4, 16>(c, dev, st);
+  return launch_tma<8, 1, 4, 8>(c, dev, st);
 }
 
 int gemv_soa_tma_mode(int fmt, int mode, const GemvCall& c, cudaStream_t st) {
   if (!tma_eligible(c)) return -1;
   DeviceInfo dev;
   if (int rc = current_device_info(dev)) return rc;
-  if (mode == 0) return fmt == 8 ? launch_tma<8, 0, 2>(c, dev, st) : launch_tma<4, 0, 4>(c, dev, st);
-  return fmt == 8 ? launch_tma<8, 1, 4>(c, dev, st) : launch_tma<4, 1, 4>(c, dev, st);
+  switch (mode) {
+    case 0: return fmt == 8 ? launch_tma<8, 0, 2, 16>(c, dev, st) : launch_tma<4, 0, 4, 16>(c, dev, st);
+    case 2: return fmt == 8 ? launch_tma<8, 1, 4, 8>(c, dev, st) : launch_tma<4, 1, 4, 8>(c, dev, st);
+    case 3: return fmt == 8 ? launch_tma<8, 1, 2, 8>(c, dev, st) : launch_tma<4, 1, 2, 8>(c, dev, st);
+    default: return fmt == 8 ? launch_tma<8, 1, 4, 16>(c, dev, st) : launch_tma<4, 1, 4, 16>(c, dev, st);
+  }
 }
 
 int read_device_error(int clear, cudaStream_t st, int* out) {
