@@ -13,7 +13,7 @@
 //  * Warps 1..16 consume.  Consumer warp w owns K slice (w % KS) and row
 //    group (w / KS); lane l of it owns one 32-weight block of that slice.
 //    In the default mode (MODE 1) the lane converts its 32 x values once per
-//    kernel into block fixed point, X_j = rint(x_j 2^(30-e)), kept as four
+//    kernel into block fixed point, X_j = rint(x_j 2^(22-e)), kept as three
 //    byte planes in registers; each block's dot with the integer quants is
 //    then exact dp4a arithmetic (q8_0: the raw int8 quants; q4_0: two masks
 //    per 8 nibbles and a per-block bias for the -8 offset), folded in int32
@@ -178,14 +178,20 @@ __device__ __forceinline__ int dp4a_us(uint32_t a, uint32_t b, int c) {
   return d;
 }
 
-// One 32-element block of x in block fixed point: X_j = rint(x_j * 2^(30-e))
-// with |x_j| < 2^e, so |X_j| < 2^30.  X_j = X3 2^24 + X2 2^16 + X1 2^8 + X0
-// with X0..X2 the unsigned low bytes of X_j and X3 its (signed) top byte, so
-// the planes are just the bytes of the two's-complement X_j.  pl[w][p] packs
-// byte p of elements 4w..4w+3.  A block's dot with integer quants q is
+// One 32-element block of x in block fixed point: X_j = rint(x_j * 2^(22-e))
+// with |x_j| < 2^e, so |X_j| < 2^22.  X_j = X2 2^16 + X1 2^8 + X0 with X0, X1
+// the unsigned low bytes of X_j and X2 its (signed) third byte, so the three
+// planes are just bytes 0-2 of the two's-complement X_j.  pl[w][p] packs byte
+// p of elements 4w..4w+3.  A block's dot with integer quants q is
 // sum_p 2^(8p) * sum_w dp4a(q_w, pl[w][p]): exact in int32 per plane.
+// Rounding x_j to the 2^(e-22) grid moves it by at most 2^(e-23) <=
+// 2^-22 ||x_block||, so the dot of a row moves by at most
+// 2^-22 * sqrt(32) * ||w|| * ||x|| ~ 1.35e-6 ||w|| ||x|| (Cauchy-Schwarz per
+// block and across blocks), for any K.
+constexpr int NPL = 3;
+
 struct XPlanes {
-  uint32_t pl[8][4];
+  uint32_t pl[8][NPL];
   int e;        // block exponent (|x| < 2^e), -149 for an all-zero block
   float bias;   // 128 * sum_j X_j, for the q4_0 offset (see consumer)
   bool finite;
@@ -209,13 +215,13 @@ __device__ __forceinline__ void make_planes(const float* __restrict__ xb, XPlane
   o.e = e;
   int X[32];
   float sum = 0.0f;
-  if (e >= -97) {
-    const float sc = __uint_as_float((uint32_t)(157 - e) << 23);  // 2^(30 - e), exact
+  if (e >= -105) {
+    const float sc = __uint_as_float((uint32_t)(149 - e) << 23);  // 2^(22 - e), exact
 #pragma unroll
     for (int j = 0; j < 32; ++j) X[j] = o.finite ? __float2int_rn(v[j] * sc) : 0;
   } else {
 #pragma unroll
-    for (int j = 0; j < 32; ++j) X[j] = __float2int_rn(ldexpf(v[j], 30 - e));
+    for (int j = 0; j < 32; ++j) X[j] = __float2int_rn(ldexpf(v[j], 22 - e));
   }
 #pragma unroll
   for (int j = 0; j < 32; ++j) sum += (float)X[j];
@@ -223,7 +229,7 @@ __device__ __forceinline__ void make_planes(const float* __restrict__ xb, XPlane
 #pragma unroll
   for (int w = 0; w < 8; ++w) {
 #pragma unroll
-    for (int pl = 0; pl < 4; ++pl) {
+    for (int pl = 0; pl < NPL; ++pl) {
       const uint32_t sel = (uint32_t)pl | ((uint32_t)(pl + 4) << 4);
       o.pl[w][pl] = __byte_perm(__byte_perm(X[4 * w], X[4 * w + 1], sel),
                                 __byte_perm(X[4 * w + 2], X[4 * w + 3], sel), 0x5410);
@@ -362,17 +368,17 @@ k_gemv_tma(const TmaArgs p) {
       make_planes(p.x + cidx * 32, xp);
     } else {
       for (int w = 0; w < 8; ++w)
-        for (int pl = 0; pl < 4; ++pl) xp.pl[w][pl] = 0u;
+        for (int pl = 0; pl < NPL; ++pl) xp.pl[w][pl] = 0u;
       xp.e = -149;
       xp.bias = 0.0f;
       xp.finite = true;
     }
-    // X_j = x_j 2^(30-e): the block's dot is its integer dot times 2^(e-30)
+    // X_j = x_j 2^(22-e): the block's dot is its integer dot times 2^(e-22)
     // (q4_0: times 2^-4 more, see below).  Split in two exact power-of-two
     // factors, each a normal float for every e, so the product only rounds
     // where the true value itself under- or overflows.  NaN for a non-finite
     // block so that y is NaN, as a float dot product would be.
-    const int t = xp.e - 30 - (FMT == 4 ? 4 : 0), h = t / 2;
+    const int t = xp.e - 22 - (FMT == 4 ? 4 : 0), h = t / 2;
     xs1 = xp.finite ? __int_as_float((127 + h) << 23) : __int_as_float(0x7FC00000);
     xs2 = __int_as_float((127 + t - h) << 23);
   }
@@ -437,7 +443,7 @@ k_gemv_tma(const TmaArgs p) {
 #pragma unroll
           for (int r = 0; r < R; ++r) {
             const uint8_t* rowp = st + (size_t)min(r0 + r, nr - 1) * QB;
-            int S0 = 0, S1 = 0, S2 = 0, S3 = 0;
+            int S0 = 0, S1 = 0, S2 = 0;
             if (FMT == 8) {
               // 32 signed quants: words w = 0..7 hold elements 4w..4w+3
               const uint4 u0 = *reinterpret_cast<const uint4*>(rowp + cidx * 32);
@@ -447,36 +453,34 @@ k_gemv_tma(const TmaArgs p) {
               for (int w = 0; w < 8; ++w) {
                 S0 = dp4a_su(wq[w], xp.pl[w][0], S0);
                 S1 = dp4a_su(wq[w], xp.pl[w][1], S1);
-                S2 = dp4a_su(wq[w], xp.pl[w][2], S2);
-                S3 = dp4a_ss(wq[w], xp.pl[w][3], S3);
+                S2 = dp4a_ss(wq[w], xp.pl[w][2], S2);
               }
             } else {
               // 16 bytes: word t holds elements 4t..4t+3 (low nibbles) and
               // 16+4t..16+4t+3 (high nibbles, taken in place as 16 * n)
               const uint4 u = *reinterpret_cast<const uint4*>(rowp + cidx * 16);
               const uint32_t wq[4] = {u.x, u.y, u.z, u.w};
-              uint32_t L0 = 0u, L1 = 0u, L2 = 0u, H0 = 0u, H1 = 0u, H2 = 0u;
-              int H3 = 0;
+              uint32_t L0 = 0u, L1 = 0u, H0 = 0u, H1 = 0u;
+              int H2 = 0;
 #pragma unroll
               for (int t4 = 0; t4 < 4; ++t4) {
                 const uint32_t lo = wq[t4] & 0x0F0F0F0Fu, hi = wq[t4] & 0xF0F0F0F0u;
                 L0 = dp4a_uu(lo, xp.pl[t4][0], L0);
                 L1 = dp4a_uu(lo, xp.pl[t4][1], L1);
-                L2 = dp4a_uu(lo, xp.pl[t4][2], L2);
-                S3 = dp4a_us(lo, xp.pl[t4][3], S3);
+                S2 = dp4a_us(lo, xp.pl[t4][2], S2);
                 H0 = dp4a_uu(hi, xp.pl[t4 + 4][0], H0);
                 H1 = dp4a_uu(hi, xp.pl[t4 + 4][1], H1);
-                H2 = dp4a_uu(hi, xp.pl[t4 + 4][2], H2);
-                H3 = dp4a_us(hi, xp.pl[t4 + 4][3], H3);
+                H2 = dp4a_us(hi, xp.pl[t4 + 4][2], H2);
               }
               // 16 * sum n X per plane (all below 2^21 in magnitude)
-              S0 = (int)((L0 << 4) + H0); S1 = (int)((L1 << 4) + H1);
-              S2 = (int)((L2 << 4) + H2); S3 = (S3 << 4) + H3;
+              S0 = (int)((L0 << 4) + H0);
+              S1 = (int)((L1 << 4) + H1);
+              S2 = (S2 << 4) + H2;
             }
-            // fold the planes pairwise in int32 (|S3 * 256 + S2| < 2^30), then
-            // one fp32 combination: F = hi * 2^16 + lo
-            const int hi = (S3 << 8) + S2, lo = (S1 << 8) + S0;
-            float Fv = fmaf((float)hi, 65536.0f, (float)lo);
+            // fold the two low planes in int32 (< 2^30), then one fp32
+            // combination: F = S2 * 2^16 + (S1 * 2^8 + S0)
+            const int lo = (S1 << 8) + S0;
+            float Fv = fmaf((float)S2, 65536.0f, (float)lo);
             // q4_0: 16 * sum (n - 8) X = 16 sum n X - 128 sum X; the 1/16 is in xs1 xs2
             if (FMT == 4) Fv -= xp.bias;
             acc[r] = ((dv[r] * Fv) * xs1) * xs2;
