@@ -197,7 +197,7 @@ constexpr Variant kVariants[] = {
     {"soa_r1u4", 1, 4}, {"soa_r2u2", 2, 2}, {"soa_r2u4", 2, 4}, {"soa_r4u1", 4, 1},
     {"soa_r4u2", 4, 2}, {"soa_r4u4", 4, 4}, {"soa_r8u1", 8, 1}, {"soa_r8u2", 8, 2},
     {"soa_tma_dp4a", 0, 0}, {"soa_tma_f32", 0, 0}, {"soa_tma_dp4a_2cta_r4", 0, 0},
-    {"soa_tma_dp4a_2cta_r2", 0, 0},
+    {"soa_tma_dp4a_2cta_r2", 0, 0}, {"soa_tma_dp4a_2cta_r8", 0, 0},
 };
 constexpr int kNumVariants = sizeof(kVariants) / sizeof(kVariants[0]);
 
@@ -213,7 +213,7 @@ int launch_variant(int v, const GemvCall& c, const DeviceInfo& dev, cudaStream_t
     case 6: return launch_soa<FMT, 1, 8, 1>(c, dev, st);
     case 7: return launch_soa<FMT, 1, 8, 2>(c, dev, st);
     default: {
-      const int mode = v == 8 ? 1 : v == 9 ? 0 : v == 10 ? 2 : 3;
+      const int mode = v == 8 ? 1 : v == 9 ? 0 : v == 10 ? 2 : v == 11 ? 3 : 4;
       const int rc = gemv_soa_tma_mode(FMT, mode, c, st);
       return rc == -1 ? set_error(ERR_UNSUPPORTED, "shape not handled by the TMA kernel") : rc;
     }

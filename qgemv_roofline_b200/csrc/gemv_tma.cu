@@ -609,9 +609,18 @@ int gemv_soa_tma(int fmt, const GemvCall& c, cudaStream_t st) {
   // Two CTAs of 8 consumer warps per SM overlap one CTA's drain with the
   // next CTA's fill; measured faster for q4_0 at every size and for q8_0 up
   // to ~200 MB of weights.  Beyond that q8_0 streams best with one CTA of 16.
-  if (fmt == 4) return launch_tma<4, 1, 4, 8>(c, dev, st);
-  if (c.M * (c.K + c.K / 16) >= ((int64_t)256 << 20)) return launch_tma<8, 1, 4, 16>(c, dev, st);
-  return launch_tma<8, 1, 4, 8>(c, dev, st);
+  // q4_0 is issue-bound: 8 rows per pass amortize the per-pass reduction
+  // (falls back to 4 rows, then to one CTA of 16, when the tile does not fit).
+  int rc = -1;
+  if (fmt == 4) {
+    rc = launch_tma<4, 1, 8, 8>(c, dev, st);
+    if (rc == -1) rc = launch_tma<4, 1, 4, 8>(c, dev, st);
+    if (rc == -1) rc = launch_tma<4, 1, 4, 16>(c, dev, st);
+    return rc;
+  }
+  if (c.M * (c.K + c.K / 16) < ((int64_t)256 << 20)) rc = launch_tma<8, 1, 4, 8>(c, dev, st);
+  if (rc == -1) rc = launch_tma<8, 1, 4, 16>(c, dev, st);
+  return rc;
 }
 
 int gemv_soa_tma_mode(int fmt, int mode, const GemvCall& c, cudaStream_t st) {
@@ -622,6 +631,7 @@ int gemv_soa_tma_mode(int fmt, int mode, const GemvCall& c, cudaStream_t st) {
     case 0: return fmt == 8 ? launch_tma<8, 0, 2, 16>(c, dev, st) : launch_tma<4, 0, 4, 16>(c, dev, st);
     case 2: return fmt == 8 ? launch_tma<8, 1, 4, 8>(c, dev, st) : launch_tma<4, 1, 4, 8>(c, dev, st);
     case 3: return fmt == 8 ? launch_tma<8, 1, 2, 8>(c, dev, st) : launch_tma<4, 1, 2, 8>(c, dev, st);
+    case 4: return fmt == 8 ? launch_tma<8, 1, 8, 8>(c, dev, st) : launch_tma<4, 1, 8, 8>(c, dev, st);
     default: return fmt == 8 ? launch_tma<8, 1, 4, 16>(c, dev, st) : launch_tma<4, 1, 4, 16>(c, dev, st);
   }
 }
