@@ -203,7 +203,11 @@ int launch_aos(const GemvCall& c, const DeviceInfo& dev, cudaStream_t st) {
 
 template <int FMT>
 int dispatch_aos(const GemvCall& c, const DeviceInfo& dev, cudaStream_t st) {
-  if (c.N <= 1) return launch_aos<FMT, 1, 4>(c, dev, st);
+  if (c.N <= 1) {
+    const int rc = gemv_aos_tma(FMT, c, st);  // TMA-fed kernel when the shape allows
+    if (rc != -1) return rc;
+    return launch_aos<FMT, 1, 4>(c, dev, st);
+  }
   if (c.N <= 2) return launch_aos<FMT, 2, 4>(c, dev, st);
   if (c.N <= 4) return launch_aos<FMT, 4, 2>(c, dev, st);
   if (c.N <= 8) return launch_aos<FMT, 8, 2>(c, dev, st);

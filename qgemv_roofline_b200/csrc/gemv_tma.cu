@@ -249,7 +249,10 @@ struct TmaArgs {
 //         accumulation (x as fp32).
 // MODE 1: x in block fixed point (four byte planes) and exact dp4a integer
 //         dot products per 32-weight block, fp32 across blocks.
-template <int FMT, int MODE, int R, int CONSUMERS>
+// AOS: the weights are ggml blocks [M][K/32] (34 / 18 bytes, d first); a tile
+// of rows is then one contiguous range and each lane realigns its block from
+// shared memory (MODE 1 only).
+template <int FMT, int MODE, int R, int CONSUMERS, bool AOS = false>
 __global__ void __launch_bounds__(tma_threads(CONSUMERS), 16 / CONSUMERS)
 k_gemv_tma(const TmaArgs p) {
   using F = Fmt<FMT>;
@@ -260,8 +263,9 @@ k_gemv_tma(const TmaArgs p) {
   __shared__ int abort_flag;
 
   const int K = p.K, TR = p.TR, S = p.S, KS = p.KS;
-  const int QB = K / F::ROW_DIV;  // quant bytes per row
-  const int DB = K / 16;          // scale bytes per row
+  // bytes per row of the quant plane / of the scale plane (AoS: whole blocks, no plane)
+  const int QB = AOS ? (K / QK) * F::BLOCK_BYTES : K / F::ROW_DIV;
+  const int DB = AOS ? 0 : K / 16;
   const int STG = TR * (QB + DB);
   float* part = reinterpret_cast<float*>(sm + (size_t)S * STG);  // [S][TR][KS]
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -320,8 +324,9 @@ k_gemv_tma(const TmaArgs p) {
                        "r"(qb + db)
                        : "memory");
           bulk_g2s(saddr(st), p.q + (int64_t)(a + r0) * QB, qb, bar);
-          bulk_g2s(saddr(st + (size_t)TR * QB),
-                   reinterpret_cast<const uint8_t*>(p.d) + (int64_t)(a + r0) * DB, db, bar);
+          if (!AOS)
+            bulk_g2s(saddr(st + (size_t)TR * QB),
+                     reinterpret_cast<const uint8_t*>(p.d) + (int64_t)(a + r0) * DB, db, bar);
         }
         last_issued[s] = t;
       }
@@ -345,6 +350,11 @@ k_gemv_tma(const TmaArgs p) {
   const int c = ks * 32 + lane;
   const bool cval = c < nunits;
   const int cidx = cval ? c : 0;
+  // AoS block of this lane: aligned word offset, and whether it starts mid-word
+  const int aos_boff = cidx * F::BLOCK_BYTES;
+  const int aos_off = aos_boff & ~3;
+  const bool aos_odd = (aos_boff & 2) != 0;
+  const uint32_t aos_sel = aos_odd ? 0x7654u : 0x5432u;
 
   float xr[MODE == 0 ? EPC : 1];
   XPlanes xp;
@@ -408,10 +418,12 @@ k_gemv_tma(const TmaArgs p) {
         // bytes of the stage; their results are never stored, and rows never
         // mix in the reduction below, so no clamping is needed.
         float dv[R];
-        const uint8_t* dbase = sd + (size_t)r0 * DB + (MODE == 0 && FMT == 8 ? (cidx >> 1) : cidx) * 2;
+        if (!AOS) {
+          const uint8_t* dbase = sd + (size_t)r0 * DB + (MODE == 0 && FMT == 8 ? (cidx >> 1) : cidx) * 2;
 #pragma unroll
-        for (int r = 0; r < R; ++r)
-          dv[r] = half_bits_to_float(*reinterpret_cast<const unsigned short*>(dbase + (size_t)r * DB));
+          for (int r = 0; r < R; ++r)
+            dv[r] = half_bits_to_float(*reinterpret_cast<const unsigned short*>(dbase + (size_t)r * DB));
+        }
         if (MODE == 0) {
           uint4 wv[R];
 #pragma unroll
@@ -451,11 +463,32 @@ k_gemv_tma(const TmaArgs p) {
           for (int r = 0; r < R; ++r) {
             const uint8_t* rowp = st + (size_t)(r0 + r) * QB;
             int S0 = 0, S1 = 0, S2 = 0;
+            // AoS: the lane's block starts at byte cidx * (34|18) of the row
+            // (2-byte aligned; rows start on 16-byte boundaries); read the
+            // aligned words covering it and realign the quants with PRMT.
+            constexpr int QW = FMT == 8 ? 8 : 4;  // quant words per block
+            uint32_t aw[QW];
+            if (AOS) {
+              const uint32_t* src = reinterpret_cast<const uint32_t*>(rowp + aos_off);
+              uint32_t wd[QW + 1];
+#pragma unroll
+              for (int i = 0; i <= QW; ++i) wd[i] = src[i];
+              dv[r] = half_bits_to_float((unsigned short)(aos_odd ? (wd[0] >> 16) : (wd[0] & 0xFFFFu)));
+#pragma unroll
+              for (int i = 0; i < QW; ++i) aw[i] = __byte_perm(wd[i], wd[i + 1], aos_sel);
+            }
             if (FMT == 8) {
               // 32 signed quants: words w = 0..7 hold elements 4w..4w+3
-              const uint4 u0 = *reinterpret_cast<const uint4*>(rowp + cidx * 32);
-              const uint4 u1 = *reinterpret_cast<const uint4*>(rowp + cidx * 32 + 16);
-              const uint32_t wq[8] = {u0.x, u0.y, u0.z, u0.w, u1.x, u1.y, u1.z, u1.w};
+              uint32_t wq[8];
+              if (AOS) {
+#pragma unroll
+                for (int w = 0; w < 8; ++w) wq[w] = aw[w % QW];
+              } else {
+                const uint4 u0 = *reinterpret_cast<const uint4*>(rowp + cidx * 32);
+                const uint4 u1 = *reinterpret_cast<const uint4*>(rowp + cidx * 32 + 16);
+                wq[0] = u0.x; wq[1] = u0.y; wq[2] = u0.z; wq[3] = u0.w;
+                wq[4] = u1.x; wq[5] = u1.y; wq[6] = u1.z; wq[7] = u1.w;
+              }
 #pragma unroll
               for (int w = 0; w < 8; ++w) {
                 S0 = dp4a_su(wq[w], xp.pl[w][0], S0);
@@ -465,8 +498,14 @@ k_gemv_tma(const TmaArgs p) {
             } else {
               // 16 bytes: word t holds elements 4t..4t+3 (low nibbles) and
               // 16+4t..16+4t+3 (high nibbles, taken in place as 16 * n)
-              const uint4 u = *reinterpret_cast<const uint4*>(rowp + cidx * 16);
-              const uint32_t wq[4] = {u.x, u.y, u.z, u.w};
+              uint32_t wq[4];
+              if (AOS) {
+#pragma unroll
+                for (int w = 0; w < 4; ++w) wq[w] = aw[w];
+              } else {
+                const uint4 u = *reinterpret_cast<const uint4*>(rowp + cidx * 16);
+                wq[0] = u.x; wq[1] = u.y; wq[2] = u.z; wq[3] = u.w;
+              }
               uint32_t L0 = 0u, L1 = 0u, H0 = 0u, H1 = 0u;
               int H2 = 0;
 #pragma unroll
@@ -521,7 +560,7 @@ std::map<PlanKey, TmaPlan> g_plans;
 
 // Tile rows, stages and grid for one (kernel, device, M, K); cached, so a
 // launch costs one map lookup besides the launch itself.
-template <int FMT, int MODE, int R, int CONSUMERS>
+template <int FMT, int MODE, int R, int CONSUMERS, bool AOS = false>
 int plan_tma(const void* kern, int M, int K, const DeviceInfo& dev, TmaPlan* out) {
   const PlanKey key{kern, dev.device, M, K};
   {
@@ -538,7 +577,7 @@ int plan_tma(const void* kern, int M, int K, const DeviceInfo& dev, TmaPlan* out
   while (KS * 32 < nunits) KS *= 2;
   if (KS > CONSUMERS) return -1;
   const int RG = CONSUMERS / KS;
-  const int row_bytes = K / F::ROW_DIV + K / 16;
+  const int row_bytes = AOS ? (K / QK) * F::BLOCK_BYTES : K / F::ROW_DIV + K / 16;
   const int unit = RG * R;
   const int ctas_per_sm = 16 / CONSUMERS;
   if (int rc = allow_max_smem(kern, dev)) return rc;
@@ -568,13 +607,13 @@ int plan_tma(const void* kern, int M, int K, const DeviceInfo& dev, TmaPlan* out
   return OK;
 }
 
-template <int FMT, int MODE, int R, int CONSUMERS>
+template <int FMT, int MODE, int R, int CONSUMERS, bool AOS = false>
 int launch_tma(const GemvCall& c, const DeviceInfo& dev, cudaStream_t st) {
-  auto kern = k_gemv_tma<FMT, MODE, R, CONSUMERS>;
+  auto kern = k_gemv_tma<FMT, MODE, R, CONSUMERS, AOS>;
   const int K = (int)c.K, M = (int)c.M;
   TmaPlan pl;
-  if (int rc = plan_tma<FMT, MODE, R, CONSUMERS>(reinterpret_cast<const void*>(kern), M, K, dev,
-                                                  &pl))
+  if (int rc = plan_tma<FMT, MODE, R, CONSUMERS, AOS>(reinterpret_cast<const void*>(kern), M, K,
+                                                       dev, &pl))
     return rc;
   const int grid = c.grid_override > 0 ? c.grid_override : pl.grid;
   TmaArgs a{static_cast<const uint8_t*>(c.q), static_cast<const unsigned short*>(c.d), c.x, c.y,
@@ -620,6 +659,23 @@ int gemv_soa_tma(int fmt, const GemvCall& c, cudaStream_t st) {
   }
   if (c.M * (c.K + c.K / 16) < ((int64_t)256 << 20)) rc = launch_tma<8, 1, 4, 8>(c, dev, st);
   if (rc == -1) rc = launch_tma<8, 1, 4, 16>(c, dev, st);
+  return rc;
+}
+
+// AoS (GGUF layout) single-column GEMV on the TMA path; -1 when not eligible.
+int gemv_aos_tma(int fmt, const GemvCall& c, cudaStream_t st) {
+  if (!tma_eligible(c)) return -1;
+  DeviceInfo dev;
+  if (int rc = current_device_info(dev)) return rc;
+  int rc = -1;
+  if (fmt == 4) {
+    rc = launch_tma<4, 1, 8, 8, true>(c, dev, st);
+    if (rc == -1) rc = launch_tma<4, 1, 4, 8, true>(c, dev, st);
+    if (rc == -1) rc = launch_tma<4, 1, 4, 16, true>(c, dev, st);
+    return rc;
+  }
+  if (c.M * (c.K + c.K / 16) < ((int64_t)256 << 20)) rc = launch_tma<8, 1, 4, 8, true>(c, dev, st);
+  if (rc == -1) rc = launch_tma<8, 1, 4, 16, true>(c, dev, st);
   return rc;
 }
 

@@ -47,6 +47,8 @@ int gemv_soa_tma(int fmt, const GemvCall& c, cudaStream_t st);
 bool tma_eligible(const GemvCall& c);
 // mode 0: fp32 unpack + FFMA2; mode 1: fixed-point x planes + dp4a.
 int gemv_soa_tma_mode(int fmt, int mode, const GemvCall& c, cudaStream_t st);
+// GGUF-layout blocks on the TMA path; -1 when the shape is not eligible.
+int gemv_aos_tma(int fmt, const GemvCall& c, cudaStream_t st);
 int read_device_error(int clear, cudaStream_t st, int* out);
 int soa_variant_count();
 const char* soa_variant_name(int v);
