@@ -98,6 +98,51 @@ QGEMV_API int qgemv_q4_0_soa(const void* q, const void* d, const float* x, float
                              int64_t M, int64_t K, int32_t ncols, int64_t ldx, int64_t ldy,
                              void* stream);
 
+/* Batched SoA calls (ncols >= 2) run on the tensor cores when K % 256 == 0,
+ * K <= 2^20 and q, d are 16-byte aligned; they need a workspace (the
+ * activations re-laid as fp16 hi/lo pairs, about 4 * K * min(ncols, 16)
+ * bytes).  qgemv_q8_0_soa / qgemv_q4_0_soa keep one per (device, stream),
+ * allocated by the first such call on the stream and grown when a later
+ * call needs more; that call must not be inside stream capture
+ * (QGEMV_ERR_UNSUPPORTED).  qgemv_soa_ws takes the workspace from the caller
+ * instead and allocates nothing.  Calls that share a workspace must be
+ * ordered (one stream, or events between them).  The reference had no
+ * batched kernel. */
+
+/* Workspace bytes of a batched SoA call (0 when the call needs none). */
+QGEMV_API size_t qgemv_soa_workspace_bytes(int format, int64_t M, int64_t K, int32_t ncols);
+
+/* qgemv_q8_0_soa / qgemv_q4_0_soa (format QGEMV_Q8_0 or QGEMV_Q4_0) with a
+ * caller-owned device workspace of at least qgemv_soa_workspace_bytes()
+ * bytes, 16-byte aligned (unused, and may be NULL, when that is 0). */
+QGEMV_API int qgemv_soa_ws(int format, const void* q, const void* d, const float* x, float* y,
+                           int64_t M, int64_t K, int32_t ncols, int64_t ldx, int64_t ldy,
+                           void* workspace, size_t workspace_bytes, void* stream);
+
+/* Frees the per-stream workspaces (synchronises their devices). */
+QGEMV_API int qgemv_release_workspaces(void);
+
+/* Batch tiles: the same quantized weights re-laid for the tensor-core batch
+ * kernel, one contiguous block per 16 rows x 512 columns (quants in the
+ * order the kernel reads them, then that block's fp16 scales; rows beyond M
+ * and columns beyond K zero).  A block is then a single bulk copy; the SoA
+ * planes, whose 16 rows lie K bytes apart, need 16 copies per block and
+ * stream at a fraction of the HBM rate on this path.  Made once per weight
+ * matrix (qgemv_tile_weights), from SoA planes (layout 0: q, d) or from
+ * ggml blocks (layout 1: q = blocks, d unused).  No reference counterpart:
+ * the reference had no batched kernel. */
+QGEMV_API size_t qgemv_tiled_bytes(int format, int64_t M, int64_t K);
+QGEMV_API int qgemv_tile_weights(int format, int layout, const void* q, const void* d, int64_t M,
+                                 int64_t K, void* tiled, void* stream);
+
+/* Y = X W^T from batch tiles, any ncols >= 0 (16 per launch), K % 32 == 0,
+ * K <= 2^20.  workspace: qgemv_tiled_workspace_bytes(K, ncols) bytes,
+ * 16-byte aligned, or NULL for the per-stream workspace described above. */
+QGEMV_API size_t qgemv_tiled_workspace_bytes(int64_t K, int32_t ncols);
+QGEMV_API int qgemv_tiled_gemv(int format, const void* tiled, int64_t M, int64_t K,
+                               const float* x, float* y, int32_t ncols, int64_t ldx, int64_t ldy,
+                               void* workspace, size_t workspace_bytes, void* stream);
+
 /* GEMV straight from ggml/GGUF blocks (no repack).  Replaces the AoS kernels
  * qgemv_q8_v0_naive / v1_warp / v2_smem_x and qgemv_q4_v0 / v1 / v2
  * (src/qgemv_kernels.cuh:39-104, 180-224, 294-320; launches

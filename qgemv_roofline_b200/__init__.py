@@ -6,6 +6,7 @@ Public API (torch tensors as buffers; compute in libqgemv_b200.so):
   ``QK``, ``quantize_q8_0``, ``quantize_q4_0``, ``dequant_q8_0``,
   ``dequant_q4_0``, plus ``to_aos`` / ``from_aos`` and ``quantize_*_aos``;
 * GEMV: ``qgemv(fmt, q, d, x)``, ``qgemv_aos(fmt, blocks, x)``,
+  ``qgemv_tiled(fmt, tile_weights(fmt, q, d), M, K, X)`` (batch tiles),
   ``QuantizedMatrix``;
 * roof probes: ``roof.measure``, ``roof.cublas_fp16_mv``;
 * multi-GPU row sharding: ``shard.ShardedQGemv``.
@@ -13,7 +14,8 @@ Public API (torch tensors as buffers; compute in libqgemv_b200.so):
 
 from . import _lib, gemv, qformats, roof, shard, timing  # noqa: F401
 from ._lib import QGemvError, device_info  # noqa: F401
-from .gemv import QuantizedMatrix, algorithmic_bytes, qgemv, qgemv_aos  # noqa: F401
+from .gemv import (QuantizedMatrix, algorithmic_bytes, qgemv, qgemv_aos,  # noqa: F401
+                   qgemv_tiled, tile_weights)
 from .qformats import (QK, dequant_q4_0, dequant_q8_0, from_aos, quantize_q4_0,  # noqa: F401
                        quantize_q4_0_aos, quantize_q8_0, quantize_q8_0_aos, to_aos, weight_bytes)
 

@@ -82,6 +82,16 @@ SIGNATURES = {
     "qgemv_soa_variant": ([ctypes.c_int, ctypes.c_int, _i32, _vp, _vp, _vp, _vp, _i64, _i64, _vp],
                           ctypes.c_int),
     "qgemv_check_device_error": ([ctypes.c_int, _vp], ctypes.c_int),
+    "qgemv_soa_workspace_bytes": ([ctypes.c_int, _i64, _i64, _i32], ctypes.c_size_t),
+    "qgemv_soa_ws": ([ctypes.c_int, _vp, _vp, _vp, _vp, _i64, _i64, _i32, _i64, _i64, _vp,
+                      ctypes.c_size_t, _vp], ctypes.c_int),
+    "qgemv_release_workspaces": ([], ctypes.c_int),
+    "qgemv_tiled_bytes": ([ctypes.c_int, _i64, _i64], ctypes.c_size_t),
+    "qgemv_tile_weights": ([ctypes.c_int, ctypes.c_int, _vp, _vp, _i64, _i64, _vp, _vp],
+                           ctypes.c_int),
+    "qgemv_tiled_workspace_bytes": ([_i64, _i32], ctypes.c_size_t),
+    "qgemv_tiled_gemv": ([ctypes.c_int, _vp, _i64, _i64, _vp, _vp, _i32, _i64, _i64, _vp,
+                          ctypes.c_size_t, _vp], ctypes.c_int),
     "qgemv_quantize_soa": ([ctypes.c_int, _vp, _i64, _i64, _i64, _vp, _vp, _vp], ctypes.c_int),
     "qgemv_quantize_aos": ([ctypes.c_int, _vp, _i64, _i64, _i64, _vp, _vp], ctypes.c_int),
     "qgemv_dequant_soa": ([ctypes.c_int, _vp, _vp, _vp, _i64, _i64, _vp], ctypes.c_int),

@@ -7,6 +7,7 @@
 // status code, keeps a per-thread message, and accepts any K % 32 == 0.
 #include "qgemv_b200.h"
 
+#include <algorithm>
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
@@ -139,7 +140,8 @@ int check_mk(int64_t M, int64_t K) {
 }
 
 int gemv_entry(int fmt, bool aos, const void* q, const void* d, const float* x, float* y,
-               int64_t M, int64_t K, int32_t ncols, int64_t ldx, int64_t ldy, void* stream) {
+               int64_t M, int64_t K, int32_t ncols, int64_t ldx, int64_t ldy, void* stream,
+               void* ws = nullptr, size_t ws_bytes = 0, bool caller_ws = false) {
   if (int rc = check_mk(M, K)) return rc;
   if (ncols < 0) return set_error(ERR_SHAPE, "ncols=%d is negative", ncols);
   if (M == 0 || ncols == 0) return OK;
@@ -171,8 +173,89 @@ int gemv_entry(int fmt, bool aos, const void* q, const void* d, const float* x, 
   c.N = ncols;
   c.ldx = ldx;
   c.ldy = ldy;
+  if (!aos) {
+    // the tensor-core batch kernel needs a workspace: the caller's, or one
+    // cached for this stream
+    GemvCall probe = c;
+    probe.N = std::min(ncols, 16);
+    if (probe.N >= 2 && mma_eligible(probe)) {
+      const size_t need = mma_workspace_bytes(K, probe.N);
+      if (caller_ws) {
+        if (!ws || ws_bytes < need)
+          return set_error(ERR_ARG, "this call needs a workspace of %zu bytes, got %zu", need,
+                           ws_bytes);
+        if (misaligned(ws, 16)) return set_error(ERR_ALIGN, "workspace must be 16-byte aligned");
+      } else if (int rc = stream_workspace(st, need, &ws)) {
+        return rc;
+      } else {
+        ws_bytes = need;
+      }
+      c.ws = ws;
+      c.ws_bytes = ws_bytes;
+    }
+  }
   return aos ? gemv_aos(fmt, c, st) : gemv_soa(fmt, c, st);
 }
+
+// Per-(device, stream) workspaces of the plain entry points.
+std::mutex g_ws_mu;
+std::map<std::pair<int, cudaStream_t>, std::pair<void*, size_t>> g_ws;
+
+}  // namespace
+
+int stream_workspace(cudaStream_t st, size_t bytes, void** out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return set_error(ERR_CUDA, "cudaGetDevice: %s", cudaGetErrorString(e));
+  std::lock_guard<std::mutex> lk(g_ws_mu);
+  auto& slot = g_ws[std::make_pair(dev, st)];
+  if (slot.first && slot.second >= bytes) {
+    *out = slot.first;
+    return OK;
+  }
+  cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+  e = cudaStreamIsCapturing(st, &cs);
+  if (e != cudaSuccess || cs != cudaStreamCaptureStatusNone)
+    return set_error(ERR_UNSUPPORTED,
+                     "a batched call on this stream needs a %zu-byte workspace, which cannot be "
+                     "allocated during stream capture: make one uncaptured call of this shape "
+                     "on the stream first, or pass a workspace (qgemv_soa_ws)",
+                     bytes);
+  const size_t grow = std::max(bytes, slot.second * 2);
+  if (slot.first) {
+    // the old buffer may still be read by work queued on this stream
+    if ((e = cudaStreamSynchronize(st)) != cudaSuccess || (e = cudaFree(slot.first)) != cudaSuccess)
+      return set_error(ERR_CUDA, "releasing the stream workspace: %s", cudaGetErrorString(e));
+    slot = std::make_pair(nullptr, (size_t)0);
+  }
+  void* p = nullptr;
+  if ((e = cudaMalloc(&p, grow)) != cudaSuccess)
+    return set_error(ERR_CUDA, "allocating a %zu-byte stream workspace: %s", grow,
+                     cudaGetErrorString(e));
+  slot = std::make_pair(p, grow);
+  *out = p;
+  return OK;
+}
+
+int release_workspaces() {
+  std::lock_guard<std::mutex> lk(g_ws_mu);
+  int rc = OK;
+  for (auto& kv : g_ws) {
+    if (!kv.second.first) continue;
+    int cur = 0;
+    cudaGetDevice(&cur);
+    cudaSetDevice(kv.first.first);
+    cudaError_t e = cudaDeviceSynchronize();
+    if (e == cudaSuccess) e = cudaFree(kv.second.first);
+    cudaSetDevice(cur);
+    if (e != cudaSuccess && rc == OK)
+      rc = set_error(ERR_CUDA, "releasing a stream workspace: %s", cudaGetErrorString(e));
+  }
+  g_ws.clear();
+  return rc;
+}
+
+namespace {
 
 }  // namespace
 }  // namespace qg
@@ -260,9 +343,106 @@ QGEMV_API int qgemv_soa_variant(int format, int variant, int32_t grid, const voi
 }
 
 QGEMV_API int qgemv_check_device_error(int clear, void* stream) {
-  int v = 0;
+  int v = 0, w = 0;
   if (int rc = read_device_error(clear, static_cast<cudaStream_t>(stream), &v)) return rc;
+  if (int rc = read_mma_error(clear, static_cast<cudaStream_t>(stream), &w)) return rc;
+  if (!v) v = w;
   if (v) return set_error(v, "a kernel reported %s on the device", qgemv_status_string(v));
+  return OK;
+}
+
+QGEMV_API size_t qgemv_soa_workspace_bytes(int format, int64_t M, int64_t K, int32_t ncols) {
+  if (check_fmt(format) || check_mk(M, K) || ncols < 2 || M == 0) return 0;
+  GemvCall probe;
+  probe.M = M;
+  probe.K = K;
+  probe.N = std::min(ncols, 16);
+  // alignment is checked per call; assume aligned planes here
+  probe.q = reinterpret_cast<const void*>((uintptr_t)256);
+  probe.d = probe.q;
+  return mma_eligible(probe) ? mma_workspace_bytes(K, probe.N) : 0;
+}
+
+QGEMV_API int qgemv_soa_ws(int format, const void* q, const void* d, const float* x, float* y,
+                           int64_t M, int64_t K, int32_t ncols, int64_t ldx, int64_t ldy,
+                           void* workspace, size_t workspace_bytes, void* stream) {
+  if (int rc = check_fmt(format)) return rc;
+  return gemv_entry(format, false, q, d, x, y, M, K, ncols, ldx, ldy, stream, workspace,
+                    workspace_bytes, true);
+}
+
+QGEMV_API int qgemv_release_workspaces(void) { return release_workspaces(); }
+
+QGEMV_API size_t qgemv_tiled_bytes(int format, int64_t M, int64_t K) {
+  if (check_fmt(format) || check_mk(M, K)) return 0;
+  return tiled_bytes(format, M, K);
+}
+
+QGEMV_API int qgemv_tile_weights(int format, int layout, const void* q, const void* d, int64_t M,
+                                 int64_t K, void* tiled, void* stream) {
+  if (int rc = check_fmt(format)) return rc;
+  if (int rc = check_mk(M, K)) return rc;
+  if (layout != 0 && layout != 1)
+    return set_error(ERR_ARG, "layout must be 0 (SoA planes) or 1 (ggml blocks), got %d", layout);
+  if (M == 0 || K == 0) return OK;
+  if (!q || !tiled || (layout == 0 && !d))
+    return set_error(ERR_NULL, "source and destination must not be NULL");
+  if (misaligned(tiled, 16)) return set_error(ERR_ALIGN, "tiles must be 16-byte aligned");
+  if (layout == 0 && (misaligned(q, 16) || misaligned(d, 2)))
+    return set_error(ERR_ALIGN, "q must be 16-byte and d 2-byte aligned");
+  return tile_weights(format, layout == 1, q, d, M, K, tiled, static_cast<cudaStream_t>(stream));
+}
+
+QGEMV_API size_t qgemv_tiled_workspace_bytes(int64_t K, int32_t ncols) {
+  if (K < 0 || K % QK || ncols < 1) return 0;
+  return mma_workspace_bytes(K, ncols);
+}
+
+QGEMV_API int qgemv_tiled_gemv(int format, const void* tiled, int64_t M, int64_t K,
+                               const float* x, float* y, int32_t ncols, int64_t ldx, int64_t ldy,
+                               void* workspace, size_t workspace_bytes, void* stream) {
+  if (int rc = check_fmt(format)) return rc;
+  if (int rc = check_mk(M, K)) return rc;
+  if (K > ((int64_t)1 << 20))
+    return set_error(ERR_UNSUPPORTED, "K=%lld above 2^20 for batch tiles", (long long)K);
+  if (ncols < 0) return set_error(ERR_SHAPE, "ncols=%d is negative", ncols);
+  if (M == 0 || ncols == 0) return OK;
+  if (!y || (K > 0 && (!x || !tiled))) return set_error(ERR_NULL, "tiles, x and y must not be NULL");
+  if (ncols > 1 && ldx < K) return set_error(ERR_SHAPE, "ldx=%lld < K=%lld", (long long)ldx, (long long)K);
+  if (ncols > 1 && ldy < M) return set_error(ERR_SHAPE, "ldy=%lld < M=%lld", (long long)ldy, (long long)M);
+  if (ncols == 1) {
+    ldx = K;
+    ldy = M;
+  }
+  if (K > 0 && misaligned(tiled, 16)) return set_error(ERR_ALIGN, "tiles must be 16-byte aligned");
+  if (misaligned(x, 4) || misaligned(y, 4)) return set_error(ERR_ALIGN, "x and y must be 4-byte aligned");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (K == 0) return fill_zero_rows(y, M, ncols, ldy, st);
+  const size_t need = mma_workspace_bytes(K, ncols);
+  if (workspace) {
+    if (workspace_bytes < need)
+      return set_error(ERR_ARG, "this call needs a workspace of %zu bytes, got %zu", need,
+                       workspace_bytes);
+    if (misaligned(workspace, 16)) return set_error(ERR_ALIGN, "workspace must be 16-byte aligned");
+  } else if (int rc = stream_workspace(st, need, &workspace)) {
+    return rc;
+  } else {
+    workspace_bytes = need;
+  }
+  GemvCall c;
+  c.q = tiled;
+  c.M = M;
+  c.K = K;
+  c.ldx = ldx;
+  c.ldy = ldy;
+  c.ws = workspace;
+  c.ws_bytes = workspace_bytes;
+  for (int n0 = 0; n0 < ncols; n0 += 16) {
+    c.N = std::min(16, ncols - n0);
+    c.x = x + (int64_t)n0 * ldx;
+    c.y = y + (int64_t)n0 * ldy;
+    if (int rc = gemv_tiled(format, c, st)) return rc;
+  }
   return OK;
 }
 

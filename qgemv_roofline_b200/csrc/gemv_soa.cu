@@ -246,7 +246,9 @@ int gemv_soa(int fmt, const GemvCall& c, cudaStream_t st) {
     part.N = std::min(16, c.N - n0);
     part.x = c.x + (int64_t)n0 * c.ldx;
     part.y = c.y + (int64_t)n0 * c.ldy;
-    rc = fmt == 8 ? dispatch_soa<8>(part, dev, st) : dispatch_soa<4>(part, dev, st);
+    rc = -1;
+    if (part.N >= 2 && part.ws) rc = gemv_soa_mma(fmt, part, st);  // tensor-core batch kernel
+    if (rc == -1) rc = fmt == 8 ? dispatch_soa<8>(part, dev, st) : dispatch_soa<4>(part, dev, st);
     if (rc) return rc;
   }
   return OK;

@@ -38,6 +38,8 @@ struct GemvCall {
   int N = 1;
   int64_t ldx = 0, ldy = 0;
   int grid_override = 0;  // >0: force the grid size (tuning / tests)
+  void* ws = nullptr;     // workspace of the tensor-core batch kernel
+  size_t ws_bytes = 0;
 };
 
 int gemv_soa(int fmt, const GemvCall& c, cudaStream_t st);
@@ -50,6 +52,21 @@ int gemv_soa_tma_mode(int fmt, int mode, const GemvCall& c, cudaStream_t st);
 // GGUF-layout blocks on the TMA path; -1 when the shape is not eligible.
 int gemv_aos_tma(int fmt, const GemvCall& c, cudaStream_t st);
 int read_device_error(int clear, cudaStream_t st, int* out);
+// Tensor-core kernel for 2..16 columns (needs c.ws); -1 when not eligible.
+int gemv_soa_mma(int fmt, const GemvCall& c, cudaStream_t st);
+bool mma_eligible(const GemvCall& c);
+size_t mma_workspace_bytes(int64_t K, int N);
+int read_mma_error(int clear, cudaStream_t st, int* out);
+// Batch tiles: the weights re-laid for the tensor-core kernel (one contiguous
+// block per 16 rows x 512 columns); any K % 32 == 0.
+size_t tiled_bytes(int fmt, int64_t M, int64_t K);
+int tile_weights(int fmt, bool aos, const void* q, const void* d, int64_t M, int64_t K,
+                 void* out, cudaStream_t st);
+int gemv_tiled(int fmt, const GemvCall& c, cudaStream_t st);  // c.q = tiles, 1..16 columns
+// Workspace cached per (device, stream) for callers that pass none; grows on
+// demand (cudaMalloc, outside stream capture only).
+int stream_workspace(cudaStream_t st, size_t bytes, void** out);
+int release_workspaces();
 int soa_variant_count();
 const char* soa_variant_name(int v);
 int gemv_aos(int fmt, const GemvCall& c, cudaStream_t st);

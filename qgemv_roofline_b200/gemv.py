@@ -66,6 +66,15 @@ def qgemv(fmt: str, q: torch.Tensor, d: torch.Tensor, x: torch.Tensor,
         raise ValueError(f"d must be contiguous float16 [{M}, {K // QK}]")
     X, Y, y, N, ldx, ldy = _xy(x, M, K, y, q.device)
     st = torch.cuda.current_stream(q.device).cuda_stream if stream is None else stream
+    if N >= 2:
+        # batched calls: the workspace comes from torch's caching allocator
+        # (stream-ordered, usable under CUDA graph capture)
+        fid = 8 if fmt == "q8_0" else 4
+        nbytes = _lib.lib().qgemv_soa_workspace_bytes(fid, M, K, N)
+        ws = torch.empty(max(nbytes, 1), dtype=torch.uint8, device=q.device)
+        _lib.call("qgemv_soa_ws", fid, q.data_ptr(), d.data_ptr(), X.data_ptr(), Y.data_ptr(),
+                  M, K, N, ldx, ldy, ws.data_ptr(), nbytes, st)
+        return y
     _lib.call(_SOA_FN[fmt], q.data_ptr(), d.data_ptr(), X.data_ptr(), Y.data_ptr(),
               M, K, N, ldx, ldy, st)
     return y
@@ -88,11 +97,55 @@ def qgemv_aos(fmt: str, blocks: torch.Tensor, x: torch.Tensor,
     return y
 
 
+def tile_weights(fmt: str, q: torch.Tensor | None = None, d: torch.Tensor | None = None,
+                 blocks: torch.Tensor | None = None, stream: int | None = None) -> torch.Tensor:
+    """Batch tiles (uint8, 1-D) of a matrix given as SoA planes (q, d) or ggml
+    blocks [M, K/32, 34|18]: the layout the tensor-core batch kernel streams
+    with one bulk copy per 16 rows x 512 columns.  Made once per matrix."""
+    _check_fmt(fmt)
+    fid = _lib.FORMAT_CODE[fmt]
+    if blocks is not None:
+        if not blocks.is_cuda or blocks.dim() != 3 or not blocks.is_contiguous():
+            raise ValueError("blocks must be a contiguous CUDA tensor [M, K/32, bytes]")
+        M, K, src, dsrc, layout, dev = blocks.shape[0], blocks.shape[1] * QK, blocks, None, 1, blocks.device
+    else:
+        if q is None or d is None or not q.is_cuda or not q.is_contiguous() or not d.is_contiguous():
+            raise ValueError("q and d must be contiguous CUDA tensors")
+        M = q.shape[0]
+        K = q.shape[1] if fmt == "q8_0" else q.shape[1] * 2
+        src, dsrc, layout, dev = q, d, 0, q.device
+    out = torch.empty(_lib.lib().qgemv_tiled_bytes(fid, M, K), dtype=torch.uint8, device=dev)
+    st = torch.cuda.current_stream(dev).cuda_stream if stream is None else stream
+    _lib.call("qgemv_tile_weights", fid, layout, src.data_ptr(),
+              None if dsrc is None else dsrc.data_ptr(), M, K, out.data_ptr(), st)
+    return out
+
+
+def qgemv_tiled(fmt: str, tiled: torch.Tensor, M: int, K: int, x: torch.Tensor,
+                y: torch.Tensor | None = None, stream: int | None = None) -> torch.Tensor:
+    """GEMV over batch tiles (tile_weights); x [K] or [N, K] for any N."""
+    _check_fmt(fmt)
+    if not tiled.is_cuda or tiled.dtype != torch.uint8:
+        raise ValueError("tiled must be a uint8 CUDA tensor")
+    fid = _lib.FORMAT_CODE[fmt]
+    if tiled.numel() != _lib.lib().qgemv_tiled_bytes(fid, M, K):
+        raise ValueError(f"tiles hold {tiled.numel()} bytes, not those of a [{M}, {K}] {fmt} matrix")
+    X, Y, y, N, ldx, ldy = _xy(x, M, K, y, tiled.device)
+    st = torch.cuda.current_stream(tiled.device).cuda_stream if stream is None else stream
+    nbytes = _lib.lib().qgemv_tiled_workspace_bytes(K, N)
+    ws = torch.empty(max(nbytes, 16), dtype=torch.uint8, device=tiled.device)
+    _lib.call("qgemv_tiled_gemv", fid, tiled.data_ptr(), M, K, X.data_ptr(), Y.data_ptr(), N,
+              ldx, ldy, ws.data_ptr(), ws.numel(), st)
+    return y
+
+
 @dataclass
 class QuantizedMatrix:
     """A quantized [M, K] weight matrix resident on one GPU.
 
-    ``layout`` is "soa" (planes ``q``, ``d``) or "aos" (ggml ``blocks``).
+    ``layout`` is "soa" (planes ``q``, ``d``), "aos" (ggml ``blocks``) or
+    "tiled" (batch tiles, ``tiled``: the layout of the tensor-core batch
+    kernel, see ``to_tiled``).
     """
 
     fmt: str
@@ -102,6 +155,7 @@ class QuantizedMatrix:
     q: torch.Tensor | None = None
     d: torch.Tensor | None = None
     blocks: torch.Tensor | None = None
+    tiled: torch.Tensor | None = None
 
     @classmethod
     def from_float(cls, W: torch.Tensor, fmt: str, layout: str = "soa") -> "QuantizedMatrix":
@@ -119,18 +173,32 @@ class QuantizedMatrix:
 
     @property
     def device(self):
-        return (self.q if self.layout == "soa" else self.blocks).device
+        return {"soa": self.q, "aos": self.blocks, "tiled": self.tiled}[self.layout].device
+
+    def to_tiled(self) -> "QuantizedMatrix":
+        """The same matrix as batch tiles (for calls with several columns)."""
+        if self.layout == "tiled":
+            return self
+        if self.layout == "soa":
+            t = tile_weights(self.fmt, q=self.q, d=self.d)
+        else:
+            t = tile_weights(self.fmt, blocks=self.blocks)
+        return QuantizedMatrix(self.fmt, self.M, self.K, "tiled", tiled=t)
 
     def matvec(self, x: torch.Tensor, y: torch.Tensor | None = None,
                stream: int | None = None) -> torch.Tensor:
         if self.layout == "soa":
             return qgemv(self.fmt, self.q, self.d, x, y, stream)
+        if self.layout == "tiled":
+            return qgemv_tiled(self.fmt, self.tiled, self.M, self.K, x, y, stream)
         return qgemv_aos(self.fmt, self.blocks, x, y, stream)
 
     __call__ = matvec
 
     def rows(self, r0: int, r1: int) -> "QuantizedMatrix":
         """Row slice [r0, r1) as a new matrix (copies; used for row sharding)."""
+        if self.layout == "tiled":
+            raise ValueError("slice the SoA or ggml-block matrix, then tile the slice")
         if self.layout == "soa":
             return QuantizedMatrix(self.fmt, r1 - r0, self.K, "soa",
                                    q=self.q[r0:r1].contiguous(), d=self.d[r0:r1].contiguous())
@@ -138,6 +206,8 @@ class QuantizedMatrix:
                                blocks=self.blocks[r0:r1].contiguous())
 
     def to(self, device) -> "QuantizedMatrix":
+        if self.layout == "tiled":
+            return QuantizedMatrix(self.fmt, self.M, self.K, "tiled", tiled=self.tiled.to(device))
         if self.layout == "soa":
             return QuantizedMatrix(self.fmt, self.M, self.K, "soa", q=self.q.to(device),
                                    d=self.d.to(device))
