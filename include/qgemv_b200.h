@@ -122,6 +122,24 @@ QGEMV_API int qgemv_soa_ws(int format, const void* q, const void* d, const float
 /* Frees the per-stream workspaces (synchronises their devices). */
 QGEMV_API int qgemv_release_workspaces(void);
 
+/* qgemv_soa_ws with the workspace taken from a 2 MiB array compiled into the
+ * library (one per device) instead of from the caller or from cudaMalloc:
+ * neither this call nor its first-call set-up allocates device memory.  For
+ * callers that must not allocate on the call path and have no device buffer
+ * of their own to lend, e.g. a plugin host that forbids device allocation
+ * after its initialisation, or a foreign-language binding that cannot own
+ * CUDA memory.  Limit: calls needing more than 2 MiB of workspace (above
+ * K = 32256 at 16 columns) fail with QGEMV_ERR_UNSUPPORTED before anything
+ * is launched.  The first call on a device looks up the array's address
+ * (cudaGetSymbolAddress) and caches it; make that call before any stream
+ * capture.  Nothing in the array needs to start at zero.  The array is
+ * shared: calls that overlap in time on one device (two streams or two
+ * threads) race on it; calls on one stream are ordered and safe.  No
+ * counterpart in the reference. */
+QGEMV_API int qgemv_soa_static_ws(int format, const void* q, const void* d, const float* x,
+                                  float* y, int64_t M, int64_t K, int32_t ncols, int64_t ldx,
+                                  int64_t ldy, void* stream);
+
 /* Batch tiles: the same quantized weights re-laid for the tensor-core batch
  * kernel, one contiguous block per 16 rows x 512 columns (quants in the
  * order the kernel reads them, then that block's fp16 scales; rows beyond M

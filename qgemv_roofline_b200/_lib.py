@@ -86,6 +86,8 @@ SIGNATURES = {
     "qgemv_soa_ws": ([ctypes.c_int, _vp, _vp, _vp, _vp, _i64, _i64, _i32, _i64, _i64, _vp,
                       ctypes.c_size_t, _vp], ctypes.c_int),
     "qgemv_release_workspaces": ([], ctypes.c_int),
+    "qgemv_soa_static_ws": ([ctypes.c_int, _vp, _vp, _vp, _vp, _i64, _i64, _i32, _i64, _i64, _vp],
+                            ctypes.c_int),
     "qgemv_tiled_bytes": ([ctypes.c_int, _i64, _i64], ctypes.c_size_t),
     "qgemv_tile_weights": ([ctypes.c_int, ctypes.c_int, _vp, _vp, _i64, _i64, _vp, _vp],
                            ctypes.c_int),

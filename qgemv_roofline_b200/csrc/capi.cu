@@ -373,6 +373,31 @@ QGEMV_API int qgemv_soa_ws(int format, const void* q, const void* d, const float
 
 QGEMV_API int qgemv_release_workspaces(void) { return release_workspaces(); }
 
+QGEMV_API int qgemv_soa_static_ws(int format, const void* q, const void* d, const float* x,
+                                  float* y, int64_t M, int64_t K, int32_t ncols, int64_t ldx,
+                                  int64_t ldy, void* stream) {
+  if (int rc = check_fmt(format)) return rc;
+  if (int rc = check_mk(M, K)) return rc;
+  void* ws = nullptr;
+  size_t ws_bytes = 0;
+  GemvCall probe;
+  probe.q = q;
+  probe.d = d;
+  probe.M = M;
+  probe.K = K;
+  probe.N = std::min(std::max(ncols, 0), 16);
+  if (M > 0 && probe.N >= 2 && mma_eligible(probe)) {
+    const size_t need = mma_workspace_bytes(K, probe.N);
+    if (need > kStaticWsBytes)
+      return set_error(ERR_UNSUPPORTED,
+                       "this call needs %zu bytes of workspace; the static workspace holds %zu "
+                       "(K <= 32256 at 16 columns): use qgemv_soa_ws",
+                       need, kStaticWsBytes);
+    if (int rc = static_workspace(&ws, &ws_bytes)) return rc;
+  }
+  return gemv_entry(format, false, q, d, x, y, M, K, ncols, ldx, ldy, stream, ws, ws_bytes, true);
+}
+
 QGEMV_API size_t qgemv_tiled_bytes(int format, int64_t M, int64_t K) {
   if (check_fmt(format) || check_mk(M, K)) return 0;
   return tiled_bytes(format, M, K);

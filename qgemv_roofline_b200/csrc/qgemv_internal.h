@@ -66,6 +66,9 @@ int gemv_tiled(int fmt, const GemvCall& c, cudaStream_t st);  // c.q = tiles, 1.
 // Workspace cached per (device, stream) for callers that pass none; grows on
 // demand (cudaMalloc, outside stream capture only).
 int stream_workspace(cudaStream_t st, size_t bytes, void** out);
+// The fixed per-device workspace of qgemv_soa_static_ws (static_ws.cu).
+constexpr size_t kStaticWsBytes = (size_t)2 << 20;
+int static_workspace(void** out, size_t* bytes);
 int release_workspaces();
 int soa_variant_count();
 const char* soa_variant_name(int v);
