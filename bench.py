@@ -60,7 +60,14 @@ def parse():
                     help="skip roofs, e2e and the CPU baseline (profiling runs)")
     ap.add_argument("--cpu-seconds", type=float, default=10.0,
                     help="CPU-baseline sample size, in seconds of CPU work")
-    return ap.parse_args()
+    ap.add_argument("--workload", choices=["xl", "stack", "batch"], default="xl",
+                    help="xl: the headline 98304x4096 GEMV (default); stack: the 32-layer "
+                         "decode GEMV stack; batch: 28672x8192 with 1..16 columns")
+    ap.add_argument("--layers", type=int, default=32, help="stack workload: layers")
+    args = ap.parse_args()
+    if args.workload != "xl" and args.steps == 20000:
+        args.steps = 30 if args.workload == "stack" else 200
+    return args
 
 
 def wbytes(fmt, M, K):
@@ -107,6 +114,151 @@ def dram_traffic(kernel_key):
             return json.load(f).get(kernel_key)
     except Exception:
         return None
+
+
+# ------------------------------------------------------- stack / batch workloads
+
+def _timed(torch, dist, dev, world, fn, warmup, steps):
+    """Device time (ms, max over ranks) of `steps` calls of fn after `warmup`."""
+    for _ in range(warmup):
+        fn()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(steps):
+        fn()
+    b.record()
+    b.synchronize()
+    t = torch.tensor([a.elapsed_time(b)], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return t.item()
+
+
+def stack_workload(args, rank, world, dev):
+    """32 decode layers x {QKV 12288x4096, O 4096x4096, gate+up 22016x4096,
+    down 4096x11008}, batch 1, q8_0 then q4_0; rows sharded over the ranks
+    with an NCCL all-gather of every y; one step = one token through all
+    layers, replayed from a CUDA graph."""
+    import torch
+    import torch.distributed as dist
+
+    import qgemv_roofline_b200 as qg
+    from qgemv_roofline_b200 import stack
+    from qgemv_roofline_b200.clocks import ClockSampler
+
+    res, graphs, total_bytes, total_ms = {}, [], 0, 0.0
+    x = torch.randn(4096, generator=torch.Generator(device=dev).manual_seed(SEED), device=dev)
+    uuid = None
+    try:
+        uuid = str(torch.cuda.get_device_properties(dev).uuid)
+        uuid = uuid if uuid.startswith("GPU-") else "GPU-" + uuid
+    except Exception:
+        pass
+    with ClockSampler(uuid) as sampler:
+        for fmt in ("q8_0", "q4_0"):
+            st = stack.DecodeStack.from_random(fmt, n_layers=args.layers, seed=SEED, device=dev)
+            g, out = st.capture(x)
+            graphs.append(g)
+            ms = _timed(torch, dist, dev, world, g.replay, args.warmup, args.steps)
+            per = ms / args.steps
+            res[fmt] = {"us_per_token": per * 1e3, "weight_bytes": st.weight_bytes,
+                        "gbps_aggregate": st.weight_bytes / (per * 1e-3) / 1e9,
+                        "gemv_launches_per_token": len(st.mats),
+                        "allgathers_per_token": len(st.mats) if world > 1 else 0}
+            total_bytes += st.weight_bytes * args.steps
+            total_ms += ms
+            del st, out
+            torch.cuda.empty_cache()
+    graphs.clear()  # graphs holding NCCL calls go before the process group
+    value = total_bytes / (total_ms * 1e-3) / 1e9
+    peak, note = measured_peak()
+    if rank == 0:
+        line = {"metric": "32-layer q8_0/q4_0 decode GEMV stack: weight GB/s (µs/token per format)",
+                "value": value, "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+                "warmup": args.warmup, "ms_per_step": total_ms / args.steps,
+                "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+                "dtype": "fp32", "data": "synthetic (seeded N(0, 0.02) weights, N(0, 1) x)",
+                "config": {"workload": f"{args.layers} layers x (QKV 12288x4096, O 4096x4096, "
+                                       f"gate+up 22016x4096, down 4096x11008), batch 1",
+                           "parallelism": f"row-shard x{world} + NCCL all-gather of every y"
+                           if world > 1 else "single GPU",
+                           "step": "one token through all layers, q8_0 stack then q4_0 stack, "
+                                   "each a CUDA graph replay",
+                           "l2": "inputs larger than L2 (3.6-6.9 GB of weights per stack)"},
+                "per_format": res, "frac_of_peak_per_gpu": value / world / peak,
+                "peak_note": note, "clocks": sampler.summary(),
+                "gpu_launches": args.steps * world * sum(r["gemv_launches_per_token"]
+                                                         for r in res.values())}
+        print(json.dumps(line), flush=True)
+    return 0
+
+
+def batch_workload(args, rank, world, dev):
+    """W [28672, 8192] (rows sharded) with X [N, 8192], N in 1..16, from SoA
+    planes and from batch tiles."""
+    import torch
+    import torch.distributed as dist
+
+    import qgemv_roofline_b200 as qg
+    from qgemv_roofline_b200 import _lib
+
+    M, K = 28672, 8192
+    r0, r1 = M * rank // world, M * (rank + 1) // world
+    rows = r1 - r0
+    out = []
+    lib = _lib.lib()
+    for fmt in ("q8_0", "q4_0"):
+        g = torch.Generator(device=dev).manual_seed(SEED + 7919 * rank)
+        W = torch.randn(rows, K, generator=g, device=dev) * 0.02
+        q, d = (qg.quantize_q8_0 if fmt == "q8_0" else qg.quantize_q4_0)(W)
+        del W
+        copies = max(2, math.ceil(4 * L2_BYTES / wbytes(fmt, rows, K)))
+        soa = [(q, d)] + [(q.clone(), d.clone()) for _ in range(copies - 1)]
+        tiles = [qg.tile_weights(fmt, q=a, d=b) for a, b in soa]
+        fid = 8 if fmt == "q8_0" else 4
+        for N in (1, 2, 4, 8, 16):
+            X = torch.randn(N, K, device=dev)
+            Y = torch.empty(N, rows, device=dev)
+            nb = max(lib.qgemv_tiled_workspace_bytes(K, N), 16)
+            ws = torch.empty(nb, dtype=torch.uint8, device=dev)
+            sp = torch.cuda.current_stream().cuda_stream
+            it = [0]
+
+            def soa_call():
+                a, b = soa[it[0] % copies]
+                it[0] += 1
+                _lib.call("qgemv_soa_ws", fid, a.data_ptr(), b.data_ptr(), X.data_ptr(),
+                          Y.data_ptr(), rows, K, N, K, rows, ws.data_ptr(), nb, sp)
+
+            def tiled_call():
+                t = tiles[it[0] % copies]
+                it[0] += 1
+                _lib.call("qgemv_tiled_gemv", fid, t.data_ptr(), rows, K, X.data_ptr(),
+                          Y.data_ptr(), N, K, rows, ws.data_ptr(), nb, sp)
+
+            for layout, fn in (("soa", soa_call), ("tiled", tiled_call)):
+                ms = _timed(torch, dist, dev, world, fn, args.warmup, args.steps)
+                per = ms / args.steps
+                b = alg_bytes(fmt, rows, K, N)
+                out.append({"fmt": fmt, "layout": layout, "N": N, "us_per_call": per * 1e3,
+                            "gbps_aggregate": world * b / (per * 1e-3) / 1e9})
+        del soa, tiles, q, d
+        torch.cuda.empty_cache()
+    if rank == 0:
+        peak, note = measured_peak()
+        print(json.dumps({"metric": "small-batch GEMV 28672x8192, N columns: GB/s",
+                          "value": max(r["gbps_aggregate"] for r in out if r["N"] == 16),
+                          "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+                          "warmup": args.warmup, "higher_is_better": True, "scaling": "strong",
+                          "vs_baseline": None, "dtype": "fp32",
+                          "data": "synthetic (seeded N(0, 0.02) weights, N(0, 1) X)",
+                          "config": {"workload": "W [28672, 8192], X [N, 8192], N in 1..16",
+                                     "rows_per_gpu": rows, "l2": "rotated weight copies, >= 4x L2"},
+                          "peak": peak, "peak_note": note, "results": out}), flush=True)
+    return 0
 
 
 # ----------------------------------------------------------------- reference arm
@@ -257,6 +409,14 @@ def main():
     if world > 1:
         from datetime import timedelta
         dist.init_process_group("nccl", timeout=timedelta(seconds=180), device_id=dev)
+
+    if args.workload != "xl":
+        fn = stack_workload if args.workload == "stack" else batch_workload
+        rc = fn(args, rank, world, dev)
+        if world > 1:
+            dist.barrier()
+            dist.destroy_process_group()
+        return rc
 
     def barrier():
         if world > 1:

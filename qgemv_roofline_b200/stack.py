@@ -1,0 +1,168 @@
+"""Decode-time layer stack of quantized GEMVs, row-sharded across the GPUs of
+one node.
+
+The 7B-style decode configuration: ``n_layers`` layers, each four GEMVs at
+batch 1 -- QKV [12288, 4096], O [4096, 4096], gate+up [22016, 4096] and down
+[4096, 11008] -- with W ~ N(0, 0.02) quantized to q8_0 or q4_0.  Only the
+GEMVs are on this path: the attention, the gated activation and the residual
+are outside it, so each GEMV reads the leading K entries of the previous
+output (QKV -> O reads its first 4096, gate+up -> down its first 11008, down
+feeds the next layer's QKV).
+
+With P ranks (one process per GPU, ``torch.distributed``) every matrix is
+row-sharded: rank g holds rows ``row_range(M, g, P)`` of each of the
+4 * n_layers matrices and computes that slice of every y; an all-gather (NCCL
+``all_gather_into_tensor`` into a preallocated buffer when P divides M)
+assembles the full y that the next GEMV needs.  One decode step is therefore
+4 * n_layers GEMV launches and, at P > 1, as many all-gathers; ``capture``
+records the whole step as one CUDA graph.
+
+``local_gemv(mat, x, y)`` is the per-rank kernel call (default: the sm_100a
+C ABI through ``QuantizedMatrix.matvec``); it is a parameter so the sharding
+and gather plumbing can be exercised without a GPU.
+"""
+
+from __future__ import annotations
+
+from dataclasses import dataclass
+from typing import Callable, Sequence
+
+import torch
+import torch.distributed as dist
+
+from .gemv import QuantizedMatrix
+from .shard import row_range
+
+# (name, M, K) of the four GEMVs of a 7B-style decode layer
+LAYER_7B = (("qkv", 12288, 4096), ("o", 4096, 4096), ("gate_up", 22016, 4096),
+            ("down", 4096, 11008))
+
+
+@dataclass
+class StackMatrix:
+    name: str
+    layer: int
+    M: int
+    K: int
+    r0: int
+    r1: int
+    local: object  # this rank's rows (a QuantizedMatrix, or whatever local_gemv takes)
+
+
+def weight_bytes(fmt: str, shapes: Sequence = LAYER_7B, n_layers: int = 32) -> int:
+    per = {"q8_0": 34, "q4_0": 18}[fmt]
+    return n_layers * sum(M * (K // 32) * per for _, M, K in shapes)
+
+
+class DecodeStack:
+    """``n_layers`` x ``shapes`` quantized GEMVs, this rank's row slices.
+
+    ``make_local(layer, index, name, M, K, r0, r1)`` returns the rank's slice
+    of one matrix; ``from_random`` builds them on the GPU from seeded
+    N(0, 0.02) weights (identical for every world size).
+    """
+
+    def __init__(self, fmt: str, matrices: list[StackMatrix], n_layers: int,
+                 shapes: Sequence = LAYER_7B, device=None, group=None,
+                 local_gemv: Callable | None = None):
+        self.fmt, self.n_layers, self.shapes = fmt, n_layers, tuple(shapes)
+        self.group = group
+        self.world = dist.get_world_size(group) if dist.is_initialized() else 1
+        self.rank = dist.get_rank(group) if dist.is_initialized() else 0
+        self.mats = matrices
+        self.device = torch.device(device) if device is not None else torch.device("cpu")
+        self.local_gemv = local_gemv or (lambda m, x, y: m.local.matvec(x, y))
+        # one local and one gathered output buffer per matrix kind (reused by every layer)
+        self.y_local, self.y_full = [], []
+        for _, M, _ in self.shapes:
+            r0, r1 = row_range(M, self.rank, self.world)
+            self.y_local.append(torch.empty(r1 - r0, dtype=torch.float32, device=self.device))
+            self.y_full.append(torch.empty(M, dtype=torch.float32, device=self.device)
+                               if self.world > 1 else None)
+        self.nccl = self.world > 1 and dist.get_backend(group) == "nccl"
+
+    @classmethod
+    def from_random(cls, fmt: str, n_layers: int = 32, shapes: Sequence = LAYER_7B,
+                    seed: int = 0, device=None, group=None, layout: str = "soa",
+                    keep_full: bool = False) -> "DecodeStack":
+        """Seeded weights W ~ N(0, 0.02), generated and quantized on ``device``;
+        each rank keeps its rows (``keep_full`` also keeps the full matrices on
+        ``.full``, for tests)."""
+        from . import qformats
+        dev = torch.device(device) if device is not None else torch.device("cuda")
+        world = dist.get_world_size(group) if dist.is_initialized() else 1
+        rank = dist.get_rank(group) if dist.is_initialized() else 0
+        quant = qformats.quantize_q8_0 if fmt == "q8_0" else qformats.quantize_q4_0
+        mats, full = [], []
+        for layer in range(n_layers):
+            for i, (name, M, K) in enumerate(shapes):
+                g = torch.Generator(device=dev).manual_seed(seed * 100003 + layer * 16 + i)
+                W = torch.randn(M, K, generator=g, device=dev) * 0.02
+                q, d = quant(W)
+                del W
+                r0, r1 = row_range(M, rank, world)
+                part = QuantizedMatrix(fmt, r1 - r0, K, "soa", q=q[r0:r1].contiguous(),
+                                       d=d[r0:r1].contiguous())
+                if layout == "tiled":
+                    part = part.to_tiled()
+                mats.append(StackMatrix(name, layer, M, K, r0, r1, part))
+                if keep_full:
+                    full.append((q, d))
+                del q, d
+        st = cls(fmt, mats, n_layers, shapes, device=dev, group=group)
+        st.full = full
+        return st
+
+    @property
+    def weight_bytes(self) -> int:
+        return weight_bytes(self.fmt, self.shapes, self.n_layers)
+
+    def _gather(self, i: int, y_local: torch.Tensor, M: int) -> torch.Tensor:
+        if self.world == 1:
+            return y_local
+        out = self.y_full[i]
+        if self.nccl and M % self.world == 0:
+            dist.all_gather_into_tensor(out, y_local, group=self.group)
+            return out
+        S = -(-M // self.world)
+        pad = torch.zeros(S, dtype=y_local.dtype, device=y_local.device)
+        pad[:y_local.numel()] = y_local
+        parts = [torch.empty_like(pad) for _ in range(self.world)]
+        dist.all_gather(parts, pad, group=self.group)
+        cols = []
+        for g in range(self.world):
+            a, b = row_range(M, g, self.world)
+            cols.append(parts[g][:b - a])
+        out.copy_(torch.cat(cols))
+        return out
+
+    def forward(self, x: torch.Tensor, trace: list | None = None) -> torch.Tensor:
+        """One decode step: x [K of the first matrix] -> the last matrix's y.
+
+        ``trace``, when given, receives (matrix, input, full output) per GEMV."""
+        cur = x
+        nk = len(self.shapes)
+        for j, m in enumerate(self.mats):
+            i = j % nk
+            xin = cur[:m.K]
+            y_loc = self.local_gemv(m, xin, self.y_local[i])
+            cur = self._gather(i, y_loc, m.M)
+            if trace is not None:
+                trace.append((m, xin.clone(), cur.clone()))
+        return cur
+
+    __call__ = forward
+
+    def capture(self, x_static: torch.Tensor, warmup: int = 2):
+        """A CUDA graph of one ``forward`` on ``x_static`` (returns the graph
+        and the output tensor it writes)."""
+        s = torch.cuda.Stream(self.device)
+        s.wait_stream(torch.cuda.current_stream(self.device))
+        with torch.cuda.stream(s):
+            for _ in range(warmup):
+                self.forward(x_static)
+        torch.cuda.current_stream(self.device).wait_stream(s)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            out = self.forward(x_static)
+        return g, out

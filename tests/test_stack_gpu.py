@@ -1,0 +1,61 @@
+"""The decode layer stack on one GPU: every GEMV of a step against the
+float64 oracle (given the input that GEMV actually received), the CUDA-graph
+replay against the eager step, and the full 7B layer shapes on sampled rows."""
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import qformats_oracle as o
+from qgemv_roofline_b200 import stack
+
+pytestmark = pytest.mark.gpu
+SMALL = (("qkv", 384, 256), ("o", 256, 256), ("gate_up", 704, 256), ("down", 256, 352))
+
+
+def check_trace(fmt, st, trace, rows=None):
+    for (m, xin, yout), (q, d) in zip(trace, st.full):
+        qh = q.cpu().numpy()
+        dh = d.cpu().numpy()
+        X = xin.cpu().numpy()[None, :].astype(np.float32)
+        r = slice(None) if rows is None else rows
+        y_ref = o.matvec_ref(fmt, qh[r], dh[r], X)
+        wn = o.row_norms(fmt, qh[r], dh[r])
+        Y = yout.cpu().numpy()[None, :][:, r]
+        ok, worst = o.check_rowwise(Y.astype(np.float64), y_ref, wn, X, 1e-5)
+        assert ok, (m.name, m.layer, worst)
+
+
+@pytest.mark.parametrize("fmt", ["q8_0", "q4_0"])
+@pytest.mark.parametrize("layout", ["soa", "tiled"])
+def test_small_stack_every_gemv(fmt, layout):
+    st = stack.DecodeStack.from_random(fmt, n_layers=2, shapes=SMALL, seed=3, device="cuda",
+                                       layout=layout, keep_full=True)
+    x = torch.randn(256, device="cuda", generator=torch.Generator(device="cuda").manual_seed(1))
+    trace = []
+    y = st(x, trace=trace)
+    assert len(trace) == 8 and tuple(y.shape) == (256,)
+    check_trace(fmt, st, trace)
+
+
+@pytest.mark.parametrize("fmt", ["q8_0", "q4_0"])
+def test_graph_replay_matches_eager(fmt):
+    st = stack.DecodeStack.from_random(fmt, n_layers=3, shapes=SMALL, seed=4, device="cuda")
+    x = torch.randn(256, device="cuda")
+    y_eager = st(x).clone()
+    g, out = st.capture(x)
+    out.zero_()
+    g.replay()
+    torch.cuda.synchronize()
+    assert torch.equal(out, y_eager)
+
+
+@pytest.mark.parametrize("fmt", ["q8_0", "q4_0"])
+def test_7b_layer_shapes_spot_rows(fmt):
+    st = stack.DecodeStack.from_random(fmt, n_layers=1, seed=5, device="cuda", keep_full=True)
+    x = torch.randn(4096, device="cuda")
+    trace = []
+    st(x, trace=trace)
+    rows = np.random.default_rng(0).choice(4096, 64, replace=False)
+    check_trace(fmt, st, trace, rows=np.sort(rows))
+    assert st.weight_bytes == stack.weight_bytes(fmt, n_layers=1)
