@@ -81,6 +81,17 @@ __device__ __forceinline__ bool mbar_try(uint32_t bar, uint32_t parity) {
   return done != 0;
 }
 
+__device__ __forceinline__ bool mbar_test(uint32_t bar, uint32_t parity) {
+  uint32_t done;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n"
+      " selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(done)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return done != 0;
+}
+
 // Bounded wait; gives up early when another thread raised the abort flag.
 __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort_flag) {
   if (mbar_try(bar, parity)) return true;
@@ -173,6 +184,17 @@ __device__ __forceinline__ unsigned short lds16(uint32_t addr) {
   unsigned short v;
   asm volatile("ld.shared.u16 %0, [%1];" : "=h"(v) : "r"(addr));
   return v;
+}
+
+// D = A B (C = 0), m16n8k16, f16 x f16 -> f32.
+__device__ __forceinline__ void mma16816_zc(float (&d)[4], const uint32_t (&a)[4], uint32_t b0,
+                                            uint32_t b1) {
+  const float z = 0.0f;
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
+      "{%8,%9}, {%10,%10,%10,%10};"
+      : "=f"(d[0]), "=f"(d[1]), "=f"(d[2]), "=f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1), "f"(z));
 }
 
 // D = A B + D, m16n8k16, f16 x f16 -> f32.
@@ -365,17 +387,18 @@ struct MmaFmt {
 
 // Batch-tile layout (qgemv_tiled_bytes / qgemv_tile_weights): for each
 // 16-row tile t and 512-column K tile kt, one contiguous block of
-// QST + DST bytes at ((t * nkt) + kt) * (QST + DST):
+// QST + DST bytes at ((kt * T) + t) * (QST + DST), T = ceil(M / 16), so that
+// the consecutive tiles of one K tile are consecutive in memory:
 //   quants: NBOX boxes of [16 rows][128 bytes]; within a box, 16-byte chunk
 //           j of row r is stored at chunk position j ^ (r & 7) (the TMA
 //           128-byte swizzle, so that ldmatrix reads are conflict-free);
 //   scales: [16 rows][16 blocks] fp16.
-// Rows beyond M and columns beyond K are zero.  A tile is then one bulk
-// copy, which streams at the HBM rate where 16 strided row pieces do not.
+// Rows beyond M and columns beyond K are zero.  A few tiles are then one
+// bulk copy, which streams at the HBM rate where 16 strided row pieces do not.
 // KSPLIT warps share a row tile (each takes KC/32/KSPLIT blocks of every
 // stage) and each warp holds TW tiles, so CONS/KSPLIT*TW tiles are in flight
 // per CTA: few enough that the ring keeps ~100 KB of weights in flight.
-template <int FMT, int NT, int TW, int KSPLIT, bool TILED>
+template <int FMT, int NT, int TW, int KSPLIT>
 __global__ void __launch_bounds__(THREADS, 1) k_gemv_mma(const __grid_constant__ MmaArgs p) {
   using F = MmaFmt<FMT>;
   extern __shared__ uint8_t sm_raw[];
@@ -437,18 +460,13 @@ __global__ void __launch_bounds__(THREADS, 1) k_gemv_mma(const __grid_constant__
       const uint32_t slot = ring + (uint32_t)s * F::SLOT;
       // the slot's previous stage has been released: name the new one
       st_release(saddr(&tag[s]), g);
-      if (TILED) {
-        mbar_expect(bar, F::BLK);
-        bulk_g2s(slot, p.tiled + ((size_t)tile * nkt + kt) * F::BLK, F::BLK, bar);
-      } else {
-        // boxes wholly beyond the row end (last K tile) are not fetched: the
-        // stale bytes there meet x' = 0 and finite quants give exact zeros
-        const int nbox = min(F::NBOX, (qrow_bytes - kt * F::QROW) / 128);
-        mbar_expect(bar, (uint32_t)nbox * (TILE * 128) + DST);
-        for (int bx = 0; bx < nbox; ++bx)
-          tensor_g2s(slot + bx * (TILE * 128), &p.qmap, kt * F::QROW + bx * 128, tile * TILE, bar);
-        tensor_g2s(slot + F::QST, &p.dmap, kt * (KC / QK), tile * TILE, bar);
-      }
+      // boxes wholly beyond the row end (last K tile) are not fetched: the
+      // stale bytes there meet x' = 0 and finite quants give exact zeros
+      const int nbox = min(F::NBOX, (qrow_bytes - kt * F::QROW) / 128);
+      mbar_expect(bar, (uint32_t)nbox * (TILE * 128) + DST);
+      for (int bx = 0; bx < nbox; ++bx)
+        tensor_g2s(slot + bx * (TILE * 128), &p.qmap, kt * F::QROW + bx * 128, tile * TILE, bar);
+      tensor_g2s(slot + F::QST, &p.dmap, kt * (KC / QK), tile * TILE, bar);
     };
     // Weight tiles do not depend on the previous kernel: prefetch the first
     // S of them before waiting for x prep.
@@ -604,16 +622,16 @@ __global__ void __launch_bounds__(THREADS, 1) k_gemv_mma(const __grid_constant__
             const float dg8 = half_bits_to_float(lds16(da + 8 * (KC / QK) * 2));
 #pragma unroll
             for (int nt = 0; nt < NT; ++nt) {
-              // hi and lo parts in two independent two-deep chains
-              float Dh[4] = {0.0f, 0.0f, 0.0f, 0.0f}, Dl[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-              mma16816(Dh, A0, bh[nt].x, bh[nt].y);
-              mma16816(Dl, A0, bl[nt].x, bl[nt].y);
-              mma16816(Dh, A1, bh[nt].z, bh[nt].w);
-              mma16816(Dl, A1, bl[nt].z, bl[nt].w);
-              acc[i][nt][0] = fmaf(dg, Dh[0] + Dl[0], acc[i][nt][0]);
-              acc[i][nt][1] = fmaf(dg, Dh[1] + Dl[1], acc[i][nt][1]);
-              acc[i][nt][2] = fmaf(dg8, Dh[2] + Dl[2], acc[i][nt][2]);
-              acc[i][nt][3] = fmaf(dg8, Dh[3] + Dl[3], acc[i][nt][3]);
+              // the block's dot: hi and lo parts of both k16 steps in one chain
+              float D[4];
+              mma16816_zc(D, A0, bh[nt].x, bh[nt].y);
+              mma16816(D, A0, bl[nt].x, bl[nt].y);
+              mma16816(D, A1, bh[nt].z, bh[nt].w);
+              mma16816(D, A1, bl[nt].z, bl[nt].w);
+              acc[i][nt][0] = fmaf(dg, D[0], acc[i][nt][0]);
+              acc[i][nt][1] = fmaf(dg, D[1], acc[i][nt][1]);
+              acc[i][nt][2] = fmaf(dg8, D[2], acc[i][nt][2]);
+              acc[i][nt][3] = fmaf(dg8, D[3], acc[i][nt][3]);
             }
           }
         }
@@ -685,6 +703,304 @@ __global__ void __launch_bounds__(THREADS, 1) k_gemv_mma(const __grid_constant__
   }
 }
 
+// GEMV over batch tiles.  A stage is TPS consecutive tiles of one K tile
+// (about 18 KB: 2 tiles of q8_0, 4 of q4_0), one bulk copy.  Warps 2j and
+// 2j+1 own tile j of the current chunk of 8 and take the two K halves of
+// each stage; a warp copies its quants and scales from the stage into
+// registers (ldmatrix) and releases the slot before it computes, so the ring
+// keeps nearly all its stages in flight.  The per-block arithmetic and its
+// order are those of k_gemv_mma (two warps per tile), so both give the same
+// bits for the same matrix.
+template <int FMT, int NT>
+__global__ void __launch_bounds__(THREADS, 1) k_gemv_tiles(const __grid_constant__ MmaArgs p) {
+  using F = MmaFmt<FMT>;
+  constexpr int KSP = 2;                   // warps per tile (K halves)
+  constexpr int CT = CONS / KSP;           // tiles per chunk
+  constexpr int TPS = FMT == 8 ? 2 : 4;    // tiles per stage
+  constexpr int SLOT = (TPS * F::BLK + 1023) / 1024 * 1024;
+  constexpr int HB = KC / QK / KSP;        // K blocks per warp per stage (8)
+  constexpr int AREG = FMT == 8 ? HB : HB / 2;  // ldmatrix.x4 per warp per stage
+  constexpr int XSL = 2;                   // x tile slots (prefetched XSL - 1 K steps ahead)
+  extern __shared__ uint8_t sm_raw[];
+  __shared__ __align__(8) unsigned long long full[MAX_STAGES];
+  __shared__ __align__(8) unsigned long long empty[MAX_STAGES];
+  __shared__ __align__(8) unsigned long long xfull[XSL];
+  __shared__ __align__(8) unsigned long long xempty[XSL];
+  __shared__ __align__(8) unsigned long long redfull;
+  __shared__ __align__(8) unsigned long long redempty;
+  __shared__ uint32_t tag[MAX_STAGES];
+  __shared__ int abort_flag;
+
+  const int S = p.S, N = p.N, K = p.K;
+  // shared memory: [ring S x SLOT (1024-aligned)][x slots XSL x NT*8*XS][partials CT x NT*4*32 floats]
+  const uint32_t raw = saddr(sm_raw);
+  const uint32_t ring = (raw + 1023u) & ~1023u;
+  const uint32_t xslot0 = ring + (uint32_t)S * SLOT;
+  const uint32_t xslot_bytes = (uint32_t)(NT * 8) * XS;
+  constexpr int RED_WARP = NT * 4 * 32;
+  float* red = reinterpret_cast<float*>(sm_raw + (xslot0 + (uint32_t)XSL * xslot_bytes - raw));
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int T = (p.M + TILE - 1) / TILE;
+  const int t0 = (int)((int64_t)T * blockIdx.x / gridDim.x);
+  const int ntc = (int)((int64_t)T * (blockIdx.x + 1) / gridDim.x) - t0;
+  const int nkt = (K + KC - 1) / KC;
+  const int nch = (ntc + CT - 1) / CT;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S; ++s) {
+      asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(saddr(&full[s])));
+      asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(saddr(&empty[s])),
+                   "r"(KSP * TPS));
+      tag[s] = 0xFFFFFFFFu;
+    }
+    for (int s = 0; s < XSL; ++s) {
+      asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(saddr(&xfull[s])));
+      asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(saddr(&xempty[s])), "r"(CONS));
+    }
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(saddr(&redfull)), "r"(CT));
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(saddr(&redempty)), "r"(CT));
+    abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  __syncthreads();
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (lane != 0) return;
+    const uint32_t xbytes = (uint32_t)N * XS;
+    auto issue_stage = [&](uint32_t g, int tile, int ntile, int kt) {
+      const int s = (int)(g % (uint32_t)S);
+      const uint32_t bar = saddr(&full[s]);
+      st_release(saddr(&tag[s]), g);
+      const uint32_t bytes = (uint32_t)ntile * F::BLK;
+      mbar_expect(bar, bytes);
+      bulk_g2s(ring + (uint32_t)s * SLOT, p.tiled + ((size_t)kt * T + tile) * F::BLK, bytes, bar);
+    };
+    const int tcn0 = min(CT, ntc), nst0 = (tcn0 + TPS - 1) / TPS;
+    const uint32_t pre = (uint32_t)min(S, nst0);
+    for (uint32_t g = 0; g < pre; ++g)
+      issue_stage(g, t0 + (int)g * TPS, min(TPS, tcn0 - (int)g * TPS), 0);
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    // x tiles: sequence q is K tile q % nkt of chunk q / nkt; issued up to
+    // XSL - 1 steps ahead of the weight stages, as their slots free up
+    const uint32_t nxs = (uint32_t)(nch * nkt);
+    uint32_t xnext = 0;
+    int last_x[XSL];
+    for (int i = 0; i < XSL; ++i) last_x[i] = -1;
+    auto issue_x = [&](uint32_t q) {
+      const int xs = (int)(q % (uint32_t)XSL);
+      mbar_expect(saddr(&xfull[xs]), xbytes);
+      bulk_g2s(xslot0 + (uint32_t)xs * xslot_bytes, p.ws + HDR + (size_t)(q % nkt) * N * XS,
+               xbytes, saddr(&xfull[xs]));
+      last_x[xs] = (int)q;
+    };
+    auto x_free = [&](uint32_t q) {  // non-blocking: slot of x tile q released?
+      return q < (uint32_t)XSL ||
+             mbar_test(saddr(&xempty[q % XSL]), ((q / XSL) - 1) & 1u);
+    };
+    uint32_t g = 0, xseq = 0;
+    bool ok = true;
+    for (int c = 0; c < nch && ok; ++c) {
+      const int tc0 = c * CT, tcn = min(CT, ntc - tc0), nst = (tcn + TPS - 1) / TPS;
+      for (int kt = 0; kt < nkt && ok; ++kt, ++xseq) {
+        // x tile of this step (blocking), then any later ones whose slots are free
+        while (xnext <= xseq) {
+          if (xnext >= (uint32_t)XSL &&
+              !mbar_wait(saddr(&xempty[xnext % XSL]), ((xnext / XSL) - 1) & 1u, &abort_flag)) {
+            ok = false;
+            break;
+          }
+          issue_x(xnext++);
+        }
+        if (!ok) break;
+        while (xnext < nxs && xnext < xseq + XSL && x_free(xnext)) issue_x(xnext++);
+        for (int js = 0; js < nst; ++js, ++g) {
+          if (g < pre) continue;  // prefetched above
+          const uint32_t s = g % (uint32_t)S, u = g / (uint32_t)S;
+          if (u >= 1 && !mbar_wait(saddr(&empty[s]), (u - 1) & 1u, &abort_flag)) {
+            ok = false;
+            break;
+          }
+          issue_stage(g, t0 + tc0 + js * TPS, min(TPS, tcn - js * TPS), kt);
+          if (xnext < nxs && xnext < xseq + XSL && x_free(xnext)) issue_x(xnext++);
+        }
+      }
+    }
+    if (!ok) {
+      const uint32_t issued = g > pre ? g : pre;
+      for (uint32_t s = 0; s < (uint32_t)S && s < issued; ++s) {
+        const uint32_t last = s + ((issued - 1 - s) / (uint32_t)S) * (uint32_t)S;
+        mbar_wait_drain(saddr(&full[s]), (last / (uint32_t)S) & 1u);
+      }
+      for (int xs = 0; xs < XSL; ++xs)
+        if (last_x[xs] >= 0)
+          mbar_wait_drain(saddr(&xfull[xs]), ((uint32_t)last_x[xs] / XSL) & 1u);
+    }
+    return;
+  }
+
+  // -------------------------------------------------------------- consumers
+  const int cw = warp - 1;
+  const int ts = cw / KSP, kh = cw % KSP;
+  const int gq = lane >> 2, tq = lane & 3;
+  asm volatile("griddepcontrol.wait;" ::: "memory");  // y and the workspace header
+  const int lm = lane >> 3, lr = lane & 7;
+  const uint32_t a_row_off = (uint32_t)(((lm & 1) * 8 + lr) * 128);
+  const int js = ts / TPS, tin = ts % TPS;  // this warp's stage in a K step, tile in the stage
+
+  float acc[NT][4];
+  uint32_t g = 0, xseq = 0;
+  bool ok = true;
+  for (int c = 0; c < nch && ok; ++c) {
+    const int tc0 = c * CT, tcn = min(CT, ntc - tc0), nst = (tcn + TPS - 1) / TPS;
+    const bool live = ts < tcn;
+    const int tis = min(TPS, tcn - js * TPS);  // tiles in this warp's stage
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) acc[nt][e] = 0.0f;
+    for (int kt = 0; kt < nkt; ++kt, ++xseq, g += (uint32_t)nst) {
+      const int xs = (int)(xseq % (uint32_t)XSL);
+      bool good = __all_sync(0xffffffffu,
+                             mbar_wait(saddr(&xfull[xs]), (xseq / XSL) & 1u, &abort_flag));
+      uint32_t aw[AREG][4];
+      uint32_t dh[2][4];  // scales of rows g and g+8, this warp's 8 blocks (fp16 pairs)
+      if (live && good) {
+        const uint32_t gi = g + (uint32_t)js, s = gi % (uint32_t)S;
+        good = __all_sync(0xffffffffu,
+                          tag_wait(saddr(&tag[s]), gi, &abort_flag) &&
+                              mbar_wait(saddr(&full[s]), (gi / (uint32_t)S) & 1u, &abort_flag));
+        if (good) {
+          const uint32_t qb = ring + s * SLOT + (uint32_t)tin * F::BLK;
+#pragma unroll
+          for (int i = 0; i < AREG; ++i) {
+            if (FMT == 8) {
+              const int b = kh * HB + i;
+              const int jj = 2 * (b & 3) + (lm >> 1);
+              ldsm_x4(aw[i], qb + (uint32_t)(b >> 2) * (TILE * 128) + a_row_off +
+                                 (uint32_t)((jj ^ lr) << 4));
+            } else {
+              const int b = kh * HB + 2 * i;
+              const int jj = (b & 7) + (lm >> 1);
+              ldsm_x4(aw[i], qb + (uint32_t)(b >> 3) * (TILE * 128) + a_row_off +
+                                 (uint32_t)((jj ^ lr) << 4));
+            }
+          }
+          const uint32_t db = qb + F::QST + (uint32_t)kh * (HB * 2);
+          const uint4 d0 = lds128(db + (uint32_t)gq * ((KC / QK) * 2));
+          const uint4 d1 = lds128(db + (uint32_t)(gq + 8) * ((KC / QK) * 2));
+          dh[0][0] = d0.x; dh[0][1] = d0.y; dh[0][2] = d0.z; dh[0][3] = d0.w;
+          dh[1][0] = d1.x; dh[1][1] = d1.y; dh[1][2] = d1.z; dh[1][3] = d1.w;
+          __syncwarp();
+          if (lane == 0) {
+            // the stage's first warp also answers for the tiles a short stage lacks
+            const uint32_t cnt = 1u + ((tin == 0 && kh == 0) ? (uint32_t)(KSP * (TPS - tis)) : 0u);
+            asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0], %1;" ::"r"(saddr(&empty[s])),
+                         "r"(cnt)
+                         : "memory");
+          }
+        }
+      }
+      if (!good) {
+        ok = false;
+        break;
+      }
+      if (live) {
+        const uint32_t xb = xslot0 + (uint32_t)xs * xslot_bytes + (uint32_t)gq * XS + tq * 32;
+#pragma unroll
+        for (int i = 0; i < HB; ++i) {
+          const int b = kh * HB + i;
+          uint4 bh[NT], bl[NT];
+#pragma unroll
+          for (int nt = 0; nt < NT; ++nt) {
+            const uint32_t xa = xb + (uint32_t)(nt * 8) * XS + (uint32_t)b * 128;
+            bh[nt] = lds128(xa);
+            bl[nt] = lds128(xa + 16);
+          }
+          uint32_t A0[4], A1[4];
+          if (FMT == 8) {
+            const uint32_t* w = aw[i];
+            A0[0] = q8_pair02(w[0]); A0[1] = q8_pair02(w[1]);
+            A0[2] = q8_pair13(w[0]); A0[3] = q8_pair13(w[1]);
+            A1[0] = q8_pair02(w[2]); A1[1] = q8_pair02(w[3]);
+            A1[2] = q8_pair13(w[2]); A1[3] = q8_pair13(w[3]);
+          } else {
+            const uint32_t w0 = aw[i >> 1][2 * (i & 1)], w1 = aw[i >> 1][2 * (i & 1) + 1];
+            const uint32_t v0 = w0 >> 8, v1 = w1 >> 8;
+            A0[0] = q4_lo02(w0); A0[1] = q4_lo02(w1);
+            A0[2] = q4_lo02(v0); A0[3] = q4_lo02(v1);
+            A1[0] = q4_hi02(w0); A1[1] = q4_hi02(w1);
+            A1[2] = q4_hi02(v0); A1[3] = q4_hi02(v1);
+          }
+          const float dg = half_bits_to_float((unsigned short)(dh[0][i >> 1] >> (16 * (i & 1))));
+          const float dg8 = half_bits_to_float((unsigned short)(dh[1][i >> 1] >> (16 * (i & 1))));
+#pragma unroll
+          for (int nt = 0; nt < NT; ++nt) {
+            float D[4];  // the block's dot, as in k_gemv_mma
+            mma16816_zc(D, A0, bh[nt].x, bh[nt].y);
+            mma16816(D, A0, bl[nt].x, bl[nt].y);
+            mma16816(D, A1, bh[nt].z, bh[nt].w);
+            mma16816(D, A1, bl[nt].z, bl[nt].w);
+            acc[nt][0] = fmaf(dg, D[0], acc[nt][0]);
+            acc[nt][1] = fmaf(dg, D[1], acc[nt][1]);
+            acc[nt][2] = fmaf(dg8, D[2], acc[nt][2]);
+            acc[nt][3] = fmaf(dg8, D[3], acc[nt][3]);
+          }
+        }
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(saddr(&xempty[xs]));
+    }
+    if (!ok) break;
+    // the K-half warp hands its partial sums to its partner
+    float* rp = red + (size_t)ts * RED_WARP + lane;
+    if (kh == 1) {
+      if (c >= 1 && !__all_sync(0xffffffffu, mbar_wait(saddr(&redempty), (c - 1) & 1u,
+                                                        &abort_flag))) {
+        ok = false;
+        break;
+      }
+      if (live) {
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+          for (int e = 0; e < 4; ++e) rp[(nt * 4 + e) * 32] = acc[nt][e];
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(saddr(&redfull));
+      continue;
+    }
+    if (!__all_sync(0xffffffffu, mbar_wait(saddr(&redfull), c & 1u, &abort_flag))) {
+      ok = false;
+      break;
+    }
+    if (live) {
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) acc[nt][e] += rp[(nt * 4 + e) * 32];
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(saddr(&redempty));
+    if (!live) continue;
+    const float* hdr = reinterpret_cast<const float*>(p.ws);
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) {
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        const int n = nt * 8 + 2 * tq + e;
+        if (n >= N) continue;
+        const float g1 = hdr[2 * n], g2 = hdr[2 * n + 1];
+        const int r = (t0 + tc0 + ts) * TILE + gq;
+        if (r < p.M) p.y[(int64_t)n * p.ldy + r] = (acc[nt][e] * g1) * g2;
+        if (r + 8 < p.M) p.y[(int64_t)n * p.ldy + r + 8] = (acc[nt][e + 2] * g1) * g2;
+      }
+    }
+  }
+}
+
 // Batch tiles from SoA planes (q: [M][K / ROW_DIV] bytes, d: [M][K/32] fp16)
 // or from ggml blocks (AOS: [M][K/32] blocks of 34 / 18 bytes, d first).
 // One thread writes one 16-byte chunk of the output.
@@ -694,15 +1010,15 @@ __global__ void __launch_bounds__(256) k_tile(const uint8_t* __restrict__ q,
                                               int K, uint8_t* __restrict__ out, int64_t nchunks) {
   using F = MmaFmt<FMT>;
   constexpr int BS = FMT == 8 ? 34 : 18;
-  const int nkt = (K + KC - 1) / KC;
   const int nb = K / QK;
   const int64_t qrow = FMT == 8 ? K : K / 2;
   for (int64_t c = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; c < nchunks;
        c += (int64_t)gridDim.x * blockDim.x) {
     const int64_t blk = c / (F::BLK / 16);
     const int off = (int)(c - blk * (F::BLK / 16)) * 16;
-    const int64_t tile = blk / nkt;
-    const int kt = (int)(blk - tile * nkt);
+    const int64_t T = (M + TILE - 1) / TILE;
+    const int kt = (int)(blk / T);
+    const int64_t tile = blk - (int64_t)kt * T;
     uint32_t w[4] = {0u, 0u, 0u, 0u};
     if (off < F::QST) {
       const int bx = off / (TILE * 128), r = (off % (TILE * 128)) / 128, pc = (off % 128) / 16;
@@ -800,7 +1116,11 @@ std::map<std::tuple<const void*, int, int64_t>, MmaPlan> g_plans;
 template <int FMT, int NT, int TW, int KSPLIT, bool TILED>
 int launch_mma(const GemvCall& c, const DeviceInfo& dev, cudaStream_t st) {
   using F = MmaFmt<FMT>;
-  auto kern = k_gemv_mma<FMT, NT, TW, KSPLIT, TILED>;
+  constexpr int SLOT = TILED ? ((FMT == 8 ? 2 : 4) * F::BLK + 1023) / 1024 * 1024 : F::SLOT;
+  constexpr size_t RED = TILED ? (size_t)(CONS / 2) * NT * 4 * 32 * sizeof(float)
+                               : (size_t)(CONS / KSPLIT) * (KSPLIT - 1) * TW * NT * 4 * 32 *
+                                     sizeof(float);
+  auto kern = TILED ? k_gemv_tiles<FMT, NT> : k_gemv_mma<FMT, NT, TW, KSPLIT>;
   const void* kp = reinterpret_cast<const void*>(kern);
   MmaPlan pl;
   bool have = false;
@@ -816,13 +1136,12 @@ int launch_mma(const GemvCall& c, const DeviceInfo& dev, cudaStream_t st) {
     if (int rc = allow_max_smem(kp, dev)) return rc;
     cudaFuncAttributes fa;
     if (cudaFuncGetAttributes(&fa, kp) != cudaSuccess) return check_launch("cudaFuncGetAttributes");
-    const size_t fixed = 1024 + 2 * (size_t)(NT * 8) * XS +
-                         (size_t)(CONS / KSPLIT) * (KSPLIT - 1) * TW * NT * 4 * 32 * sizeof(float);
+    const size_t fixed = 1024 + 2 * (size_t)(NT * 8) * XS + RED;
     const size_t avail = (size_t)dev.smem_optin - fa.sharedSizeBytes;
-    if (avail < fixed + 4 * (size_t)F::SLOT)
+    if (avail < fixed + 4 * (size_t)SLOT)
       return set_error(ERR_UNSUPPORTED, "shared memory too small for the tensor-core GEMV");
-    pl.S = (int)std::min<size_t>(MAX_STAGES, (avail - fixed) / F::SLOT);
-    pl.smem = fixed + (size_t)pl.S * F::SLOT;
+    pl.S = (int)std::min<size_t>(MAX_STAGES, (avail - fixed) / SLOT);
+    pl.smem = fixed + (size_t)pl.S * SLOT;
     const int64_t T = (c.M + TILE - 1) / TILE;
     pl.grid = (int)std::max<int64_t>(1, std::min<int64_t>(dev.sms, T));
     std::lock_guard<std::mutex> lk(g_mu);

@@ -257,8 +257,8 @@ def tiles_np(fmt, q, d, M, K):
     dp = np.zeros((T * 16, nkt * 16), np.uint16)
     dp[:M, :K // 32] = d.view(np.uint16).reshape(M, K // 32)
     out = []
-    for t in range(T):
-        for kt in range(nkt):
+    for kt in range(nkt):
+        for t in range(T):
             rows = qp[16 * t:16 * t + 16, kt * QROW:(kt + 1) * QROW]
             qb = np.zeros((nbox, 16, 8, 16), np.uint8)
             for bx in range(nbox):
