@@ -494,7 +494,12 @@ def main():
         for f in per_format:
             per_format[f]["frac_of_stream_read_roof"] = per_format[f]["gbps_per_gpu"] / sr
     dom = "q8_0" if q8_ms >= q4_ms else "q4_0"
-    kname = (f"k_gemv_tma<{8 if dom == 'q8_0' else 4},1,4>" if args.layout == "soa" else f"k_gemv_aos<{8 if dom == 'q8_0' else 4},1,4>")
+    # the configuration the library dispatches for this slice (csrc/gemv_tma.cu)
+    if dom == "q4_0":
+        targs = "4,1,8,8"
+    else:
+        targs = "8,1,4,8" if rows * (K + K // 16) < (256 << 20) else "8,1,4,16"
+    kname = f"k_gemv_tma<{targs},{'false' if args.layout == 'soa' else 'true'}>"
     ach = per_format[dom]["gbps_per_gpu"]
     traffic = dram_traffic(f"{dom}_{args.layout}_{rows}x{K}")
     roofline = {"bound": "hbm", "achieved": ach, "peak": peak, "unit": "GB/s",
