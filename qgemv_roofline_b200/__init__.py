@@ -8,12 +8,13 @@ Public API (torch tensors as buffers; compute in libqgemv_b200.so):
 * GEMV: ``qgemv(fmt, q, d, x)``, ``qgemv_aos(fmt, blocks, x)``,
   ``qgemv_tiled(fmt, tile_weights(fmt, q, d), M, K, X)`` (batch tiles),
   ``QuantizedMatrix``;
+* GGUF files: ``gguf.GGUFReader`` (load q8_0 / q4_0 tensors onto a GPU), ``gguf.write_gguf``;
 * roof probes: ``roof.measure``, ``roof.cublas_fp16_mv``;
 * multi-GPU row sharding: ``shard.ShardedQGemv``; the decode layer stack:
   ``stack.DecodeStack``.
 """
 
-from . import _lib, gemv, qformats, roof, shard, stack, timing  # noqa: F401
+from . import _lib, gemv, gguf, qformats, roof, shard, stack, timing  # noqa: F401
 from ._lib import QGemvError, device_info  # noqa: F401
 from .gemv import (QuantizedMatrix, algorithmic_bytes, qgemv, qgemv_aos,  # noqa: F401
                    qgemv_tiled, tile_weights)
