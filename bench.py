@@ -64,6 +64,9 @@ def parse():
                     help="xl: the headline 98304x4096 GEMV (default); stack: the 32-layer "
                          "decode GEMV stack; batch: 28672x8192 with 1..16 columns")
     ap.add_argument("--layers", type=int, default=32, help="stack workload: layers")
+    ap.add_argument("--fused", action="store_true",
+                    help="stack workload: all-gather inside the GEMV kernels (peer stores, "
+                         "symmetric memory) instead of NCCL")
     args = ap.parse_args()
     if args.workload != "xl" and args.steps == 20000:
         args.steps = 30 if args.workload == "stack" else 200
@@ -150,6 +153,15 @@ def stack_workload(args, rank, world, dev):
     from qgemv_roofline_b200.clocks import ClockSampler
 
     res, graphs, total_bytes, total_ms = {}, [], 0, 0.0
+    if args.fused and not dist.is_initialized():
+        # the fused path addresses buffers through a process group, even of one
+        import socket
+        sk = socket.socket()
+        sk.bind(("127.0.0.1", 0))
+        os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+        os.environ["MASTER_PORT"] = str(sk.getsockname()[1])
+        sk.close()
+        dist.init_process_group("nccl", rank=0, world_size=1, device_id=dev)
     x = torch.randn(4096, generator=torch.Generator(device=dev).manual_seed(SEED), device=dev)
     uuid = None
     try:
@@ -159,7 +171,8 @@ def stack_workload(args, rank, world, dev):
         pass
     with ClockSampler(uuid) as sampler:
         for fmt in ("q8_0", "q4_0"):
-            st = stack.DecodeStack.from_random(fmt, n_layers=args.layers, seed=SEED, device=dev)
+            st = stack.DecodeStack.from_random(fmt, n_layers=args.layers, seed=SEED, device=dev,
+                                               fused=args.fused)
             g, out = st.capture(x)
             graphs.append(g)
             ms = _timed(torch, dist, dev, world, g.replay, args.warmup, args.steps)
@@ -167,7 +180,8 @@ def stack_workload(args, rank, world, dev):
             res[fmt] = {"us_per_token": per * 1e3, "weight_bytes": st.weight_bytes,
                         "gbps_aggregate": st.weight_bytes / (per * 1e-3) / 1e9,
                         "gemv_launches_per_token": len(st.mats),
-                        "allgathers_per_token": len(st.mats) if world > 1 else 0}
+                        "allgathers_per_token": (0 if args.fused else len(st.mats))
+                        if world > 1 else 0}
             total_bytes += st.weight_bytes * args.steps
             total_ms += ms
             del st, out
@@ -183,8 +197,11 @@ def stack_workload(args, rank, world, dev):
                 "dtype": "fp32", "data": "synthetic (seeded N(0, 0.02) weights, N(0, 1) x)",
                 "config": {"workload": f"{args.layers} layers x (QKV 12288x4096, O 4096x4096, "
                                        f"gate+up 22016x4096, down 4096x11008), batch 1",
-                           "parallelism": f"row-shard x{world} + NCCL all-gather of every y"
-                           if world > 1 else "single GPU",
+                           "parallelism": (f"row-shard x{world} + " +
+                                           ("all-gather of every y inside the GEMV kernels "
+                                            "(peer stores, counters)" if args.fused else
+                                            "NCCL all-gather of every y"))
+                           if world > 1 else "single GPU" + (", fused path" if args.fused else ""),
                            "step": "one token through all layers, q8_0 stack then q4_0 stack, "
                                    "each a CUDA graph replay",
                            "l2": "inputs larger than L2 (3.6-6.9 GB of weights per stack)"},
@@ -413,7 +430,7 @@ def main():
     if args.workload != "xl":
         fn = stack_workload if args.workload == "stack" else batch_workload
         rc = fn(args, rank, world, dev)
-        if world > 1:
+        if dist.is_initialized():
             dist.barrier()
             dist.destroy_process_group()
         return rc

@@ -140,6 +140,38 @@ QGEMV_API int qgemv_soa_static_ws(int format, const void* q, const void* d, cons
                                   float* y, int64_t M, int64_t K, int32_t ncols, int64_t ldx,
                                   int64_t ldy, void* stream);
 
+/* -------------------------------------------- fused all-gather (P GPUs) --- */
+
+/* Single-column SoA GEMV of this rank's rows whose y is all-gathered by the
+ * kernel itself: besides y (this rank's rows, usually inside its own full-y
+ * buffer) it stores the rows into every other rank's full-y buffer through
+ * peer pointers (NVLink), and the CTA that finishes last adds 1 to every
+ * rank's counter sig_out[k].  With sig_in set, the kernel first waits until
+ * the counter of the call that produced x reaches (*tok + 1) * nranks, i.e.
+ * until every rank has delivered its part of x for the current token.  All
+ * waits are bounded (~1 s; QGEMV_ERR_TIMEOUT in qgemv_check_device_error).
+ * Buffers and counters must be mapped on every rank (e.g. symmetric memory);
+ * counters start at zero; cta_count is a zeroed local counter per call site.
+ * Replaces the NCCL all-gather after a GEMV (the reference was single-GPU). */
+#define QGEMV_MAX_RANKS 8
+typedef struct qgemv_fuse {
+  float* peer_y[QGEMV_MAX_RANKS];     /* other ranks' buffers, at this rank's first row */
+  unsigned* sig_out[QGEMV_MAX_RANKS]; /* every rank's counter for this call (this rank's too) */
+  unsigned* cta_count;                /* local, zeroed, one per call site */
+  const unsigned* sig_in;             /* local counter of the call that produced x, or NULL */
+  const unsigned* tok;                /* local token count (qgemv_token_fence) */
+  int32_t npeer;                      /* entries of peer_y */
+  int32_t nranks;                     /* entries of sig_out */
+} qgemv_fuse;
+QGEMV_API int qgemv_soa_fused(int format, const void* q, const void* d, const float* x, float* y,
+                              int64_t M, int64_t K, const qgemv_fuse* fuse, void* stream);
+
+/* End of a token of fused calls: adds 1 to every rank's done[k], waits
+ * (bounded) until done_local reaches (*tok + 1) * nranks -- every rank has
+ * finished the token, so buffers may be rewritten -- and advances *tok. */
+QGEMV_API int qgemv_token_fence(unsigned* const* done, int32_t nranks, const unsigned* done_local,
+                                unsigned* tok, void* stream);
+
 /* Batch tiles: the same quantized weights re-laid for the tensor-core batch
  * kernel, one contiguous block per 16 rows x 512 columns (quants in the
  * order the kernel reads them, then that block's fp16 scales; rows beyond M

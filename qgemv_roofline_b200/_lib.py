@@ -23,6 +23,16 @@ STATUS_NAMES = {
 FORMAT_CODE = {"q8_0": 8, "q4_0": 4}
 
 
+MAX_RANKS = 8
+
+
+class FuseDesc(ctypes.Structure):
+    """qgemv_fuse of include/qgemv_b200.h."""
+    _fields_ = [("peer_y", ctypes.c_void_p * MAX_RANKS), ("sig_out", ctypes.c_void_p * MAX_RANKS),
+                ("cta_count", ctypes.c_void_p), ("sig_in", ctypes.c_void_p),
+                ("tok", ctypes.c_void_p), ("npeer", ctypes.c_int32), ("nranks", ctypes.c_int32)]
+
+
 class QGemvError(RuntimeError):
     """A C-ABI call returned a non-zero qgemv_status."""
 
@@ -86,6 +96,8 @@ SIGNATURES = {
     "qgemv_soa_ws": ([ctypes.c_int, _vp, _vp, _vp, _vp, _i64, _i64, _i32, _i64, _i64, _vp,
                       ctypes.c_size_t, _vp], ctypes.c_int),
     "qgemv_release_workspaces": ([], ctypes.c_int),
+    "qgemv_soa_fused": ([ctypes.c_int, _vp, _vp, _vp, _vp, _i64, _i64, _vp, _vp], ctypes.c_int),
+    "qgemv_token_fence": ([_vp, _i32, _vp, _vp, _vp], ctypes.c_int),
     "qgemv_soa_static_ws": ([ctypes.c_int, _vp, _vp, _vp, _vp, _i64, _i64, _i32, _i64, _i64, _vp],
                             ctypes.c_int),
     "qgemv_tiled_bytes": ([ctypes.c_int, _i64, _i64], ctypes.c_size_t),

@@ -373,6 +373,59 @@ QGEMV_API int qgemv_soa_ws(int format, const void* q, const void* d, const float
 
 QGEMV_API int qgemv_release_workspaces(void) { return release_workspaces(); }
 
+QGEMV_API int qgemv_soa_fused(int format, const void* q, const void* d, const float* x, float* y,
+                              int64_t M, int64_t K, const qgemv_fuse* fuse, void* stream) {
+  if (int rc = check_fmt(format)) return rc;
+  if (int rc = check_mk(M, K)) return rc;
+  if (!fuse) return set_error(ERR_NULL, "fuse must not be NULL");
+  if (fuse->nranks < 1 || fuse->nranks > kMaxRanks || fuse->npeer < 0 ||
+      fuse->npeer > kMaxRanks - 1)
+    return set_error(ERR_ARG, "nranks must be in [1, %d] and npeer in [0, %d]", kMaxRanks,
+                     kMaxRanks - 1);
+  if (!fuse->cta_count || !fuse->tok) return set_error(ERR_NULL, "cta_count and tok must be set");
+  for (int k = 0; k < fuse->nranks; ++k)
+    if (!fuse->sig_out[k]) return set_error(ERR_NULL, "sig_out[%d] is NULL", k);
+  for (int k = 0; k < fuse->npeer; ++k)
+    if (!fuse->peer_y[k] || misaligned(fuse->peer_y[k], 4))
+      return set_error(ERR_ALIGN, "peer_y[%d] must be a 4-byte aligned device pointer", k);
+  if (M == 0) return OK;
+  if (!q || !d || !x || !y) return set_error(ERR_NULL, "q, d, x and y must not be NULL");
+  if (misaligned(q, 16) || misaligned(d, 2) || misaligned(y, 4))
+    return set_error(ERR_ALIGN, "q must be 16-byte, d 2-byte and y 4-byte aligned");
+  GemvCall c;
+  c.q = q;
+  c.d = d;
+  c.x = x;
+  c.y = y;
+  c.M = M;
+  c.K = K;
+  c.N = 1;
+  c.ldx = K;
+  c.ldy = M;
+  if (!tma_eligible(c))
+    return set_error(ERR_UNSUPPORTED,
+                     "the fused all-gather needs the TMA kernel: K %% 256 == 0, 256 <= K <= 16384, "
+                     "x 16-byte aligned");
+  for (int k = 0; k < fuse->nranks; ++k) c.f.sig_out[k] = fuse->sig_out[k];
+  for (int k = 0; k < fuse->npeer; ++k) c.f.peer_y[k] = fuse->peer_y[k];
+  c.f.cta_count = fuse->cta_count;
+  c.f.sig_in = fuse->sig_in;
+  c.f.tok = fuse->tok;
+  c.f.npeer = fuse->npeer;
+  c.f.nranks = fuse->nranks;
+  return gemv_soa_tma(format, c, static_cast<cudaStream_t>(stream));
+}
+
+QGEMV_API int qgemv_token_fence(unsigned* const* done, int32_t nranks, const unsigned* done_local,
+                                unsigned* tok, void* stream) {
+  if (nranks < 1 || nranks > kMaxRanks) return set_error(ERR_ARG, "nranks must be in [1, %d]", kMaxRanks);
+  if (!done || !done_local || !tok) return set_error(ERR_NULL, "done, done_local and tok must be set");
+  for (int k = 0; k < nranks; ++k)
+    if (!done[k]) return set_error(ERR_NULL, "done[%d] is NULL", k);
+  return token_fence(const_cast<unsigned* const*>(done), nranks, done_local, tok,
+                     static_cast<cudaStream_t>(stream));
+}
+
 QGEMV_API int qgemv_soa_static_ws(int format, const void* q, const void* d, const float* x,
                                   float* y, int64_t M, int64_t K, int32_t ncols, int64_t ldx,
                                   int64_t ldy, void* stream) {

@@ -243,7 +243,32 @@ struct TmaArgs {
   const float* x;
   float* y;
   int M, K, TR, S, KS;
+  FuseArgs f;  // all-gather of y into peer buffers (f.nranks == 0: none)
 };
+
+__device__ __forceinline__ unsigned ld_acquire_sys(const unsigned* p) {
+  unsigned v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void red_release_sys(unsigned* p, unsigned v) {
+  asm volatile("red.release.sys.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+// Bounded wait (~1 s) until the counter at `c` reaches `target` (mod 2^32).
+__device__ __forceinline__ bool wait_count(const unsigned* c, unsigned target,
+                                           volatile int* abort_flag) {
+  const long long t0 = clock64();
+  while ((int)(ld_acquire_sys(c) - target) < 0) {
+    if (abort_flag && *abort_flag) return false;
+    if (clock64() - t0 > SPIN_LIMIT) {
+      if (abort_flag) *abort_flag = 1;
+      atomicExch(&g_device_error, (int)ERR_TIMEOUT);
+      return false;
+    }
+  }
+  return true;
+}
 
 // MODE 0: quants converted to fp32 with the magic-number trick and FFMA2
 //         accumulation (x as fp32).
@@ -261,6 +286,7 @@ k_gemv_tma(const TmaArgs p) {
   __shared__ __align__(8) unsigned long long full[MAX_STAGES];
   __shared__ __align__(8) unsigned long long empty[MAX_STAGES];
   __shared__ int abort_flag;
+  __shared__ uint32_t x_ready;
 
   const int K = p.K, TR = p.TR, S = p.S, KS = p.KS;
   // bytes per row of the quant plane / of the scale plane (AoS: whole blocks, no plane)
@@ -280,6 +306,7 @@ k_gemv_tma(const TmaArgs p) {
                    "r"(CONSUMERS));
     }
     abort_flag = 0;
+    x_ready = 0u;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   __syncthreads();
@@ -311,6 +338,7 @@ k_gemv_tma(const TmaArgs p) {
           float v = 0.0f;
           for (int k = 0; k < KS; ++k) v += ps[i * KS + k];
           p.y[a + r0 + i] = v;
+          for (int k = 0; k < p.f.npeer; ++k) p.f.peer_y[k][a + r0 + i] = v;  // NVLink stores
         }
         __syncwarp();
       }
@@ -336,6 +364,20 @@ k_gemv_tma(const TmaArgs p) {
       for (int s = 0; s < S; ++s)
         if (last_issued[s] >= 0)
           mbar_wait_drain(saddr(&full[s]), (uint32_t)((last_issued[s] / S) & 1));
+    }
+    if (p.f.nranks > 0) {
+      // The CTA that finishes last tells every rank that this rank's slice of
+      // y is in its buffer: each CTA orders its stores (system scope) before
+      // its count; the last one orders all of them before the signals.
+      __threadfence_system();
+      __syncwarp();
+      if (lane == 0) {
+        const unsigned old = atomicAdd(p.f.cta_count, 1u);
+        if (old % gridDim.x == gridDim.x - 1) {
+          __threadfence_system();
+          for (int k = 0; k < p.f.nranks; ++k) red_release_sys(p.f.sig_out[k], 1u);
+        }
+      }
     }
     return;
   }
@@ -376,6 +418,22 @@ k_gemv_tma(const TmaArgs p) {
     }
   } else {
     asm volatile("griddepcontrol.wait;" ::: "memory");  // x may be the previous kernel's y
+    if (p.f.sig_in) {
+      // x is assembled by every rank's previous GEMV: one signal per rank per token
+      if (cw == 0 && lane == 0) {
+        const unsigned target = (*(volatile const unsigned*)p.f.tok + 1u) * (unsigned)p.f.nranks;
+        if (wait_count(p.f.sig_in, target, &abort_flag))
+          asm volatile("st.release.cta.shared::cta.u32 [%0], %1;" ::"r"(saddr(&x_ready)), "r"(1u)
+                       : "memory");
+      }
+      const long long t0 = clock64();
+      for (;;) {
+        uint32_t r;
+        asm volatile("ld.acquire.cta.shared::cta.u32 %0, [%1];" : "=r"(r) : "r"(saddr(&x_ready))
+                     : "memory");
+        if (r || abort_flag || clock64() - t0 > 2 * SPIN_LIMIT) break;
+      }
+    }
     if (cval) {
       make_planes(p.x + cidx * 32, xp);
     } else {
@@ -617,7 +675,7 @@ int launch_tma(const GemvCall& c, const DeviceInfo& dev, cudaStream_t st) {
     return rc;
   const int grid = c.grid_override > 0 ? c.grid_override : pl.grid;
   TmaArgs a{static_cast<const uint8_t*>(c.q), static_cast<const unsigned short*>(c.d), c.x, c.y,
-            M, K, pl.TR, pl.S, pl.KS};
+            M, K, pl.TR, pl.S, pl.KS, c.f};
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(grid);
   cfg.blockDim = dim3(tma_threads(CONSUMERS));
@@ -690,6 +748,36 @@ int gemv_soa_tma_mode(int fmt, int mode, const GemvCall& c, cudaStream_t st) {
     case 4: return fmt == 8 ? launch_tma<8, 1, 8, 8>(c, dev, st) : launch_tma<4, 1, 8, 8>(c, dev, st);
     default: return fmt == 8 ? launch_tma<8, 1, 4, 16>(c, dev, st) : launch_tma<4, 1, 4, 16>(c, dev, st);
   }
+}
+
+namespace {
+struct FenceArgs {
+  unsigned* done[kMaxRanks];
+  const unsigned* done_local;
+  unsigned* tok;
+  int nranks;
+};
+
+__global__ void k_token_fence(const FenceArgs f) {
+  if (threadIdx.x != 0) return;
+  __threadfence_system();
+  for (int k = 0; k < f.nranks; ++k) red_release_sys(f.done[k], 1u);
+  const unsigned t = *(volatile unsigned*)f.tok;
+  wait_count(f.done_local, (t + 1u) * (unsigned)f.nranks, nullptr);
+  *(volatile unsigned*)f.tok = t + 1u;
+  __threadfence_system();
+}
+}  // namespace
+
+int token_fence(unsigned* const* done, int nranks, const unsigned* done_local, unsigned* tok,
+                cudaStream_t st) {
+  FenceArgs f = {};
+  for (int k = 0; k < nranks; ++k) f.done[k] = done[k];
+  f.done_local = done_local;
+  f.tok = tok;
+  f.nranks = nranks;
+  k_token_fence<<<1, 32, 0, st>>>(f);
+  return check_launch("k_token_fence");
 }
 
 int read_device_error(int clear, cudaStream_t st, int* out) {

@@ -29,6 +29,21 @@ int allow_max_smem(const void* func, const DeviceInfo& dev);
 // Resident blocks per SM of `func` (cached per device, block size and smem).
 int occupancy(const void* func, const DeviceInfo& dev, int threads, size_t smem, int* out);
 
+// All-gather fused into the single-column GEMV (one process per GPU): the
+// kernel also stores its rows into the other ranks' y buffers (peer
+// pointers) and the CTA that finishes last adds 1 to every rank's counter
+// sig_out[k]; with sig_in set, the kernel first waits (bounded) until the
+// counter of its input reaches (*tok + 1) * nranks.
+constexpr int kMaxRanks = 8;
+struct FuseArgs {
+  float* peer_y[kMaxRanks] = {};
+  unsigned* sig_out[kMaxRanks] = {};
+  unsigned* cta_count = nullptr;
+  const unsigned* sig_in = nullptr;
+  const unsigned* tok = nullptr;
+  int npeer = 0, nranks = 0;
+};
+
 struct GemvCall {
   const void* q = nullptr;  // SoA quant plane, or AoS blocks
   const void* d = nullptr;  // SoA scale plane (fp16 bits); unused for AoS
@@ -40,6 +55,7 @@ struct GemvCall {
   int grid_override = 0;  // >0: force the grid size (tuning / tests)
   void* ws = nullptr;     // workspace of the tensor-core batch kernel
   size_t ws_bytes = 0;
+  FuseArgs f;             // fused all-gather (f.nranks == 0: none)
 };
 
 int gemv_soa(int fmt, const GemvCall& c, cudaStream_t st);
@@ -52,6 +68,10 @@ int gemv_soa_tma_mode(int fmt, int mode, const GemvCall& c, cudaStream_t st);
 // GGUF-layout blocks on the TMA path; -1 when the shape is not eligible.
 int gemv_aos_tma(int fmt, const GemvCall& c, cudaStream_t st);
 int read_device_error(int clear, cudaStream_t st, int* out);
+// End of a token of fused calls: signal every rank's done[k], wait (bounded)
+// until done_local reaches (*tok + 1) * nranks, then advance *tok.
+int token_fence(unsigned* const* done, int nranks, const unsigned* done_local, unsigned* tok,
+                cudaStream_t st);
 // Tensor-core kernel for 2..16 columns (needs c.ws); -1 when not eligible.
 int gemv_soa_mma(int fmt, const GemvCall& c, cudaStream_t st);
 bool mma_eligible(const GemvCall& c);

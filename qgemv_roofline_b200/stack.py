@@ -64,7 +64,7 @@ class DecodeStack:
 
     def __init__(self, fmt: str, matrices: list[StackMatrix], n_layers: int,
                  shapes: Sequence = LAYER_7B, device=None, group=None,
-                 local_gemv: Callable | None = None):
+                 local_gemv: Callable | None = None, fused: bool = False):
         self.fmt, self.n_layers, self.shapes = fmt, n_layers, tuple(shapes)
         self.group = group
         self.world = dist.get_world_size(group) if dist.is_initialized() else 1
@@ -80,11 +80,14 @@ class DecodeStack:
             self.y_full.append(torch.empty(M, dtype=torch.float32, device=self.device)
                                if self.world > 1 else None)
         self.nccl = self.world > 1 and dist.get_backend(group) == "nccl"
+        self.fused = None
+        if fused:
+            self.fused = _FusedGather(self)
 
     @classmethod
     def from_random(cls, fmt: str, n_layers: int = 32, shapes: Sequence = LAYER_7B,
                     seed: int = 0, device=None, group=None, layout: str = "soa",
-                    keep_full: bool = False) -> "DecodeStack":
+                    keep_full: bool = False, fused: bool = False) -> "DecodeStack":
         """Seeded weights W ~ N(0, 0.02), generated and quantized on ``device``;
         each rank keeps its rows (``keep_full`` also keeps the full matrices on
         ``.full``, for tests)."""
@@ -109,7 +112,7 @@ class DecodeStack:
                 if keep_full:
                     full.append((q, d))
                 del q, d
-        st = cls(fmt, mats, n_layers, shapes, device=dev, group=group)
+        st = cls(fmt, mats, n_layers, shapes, device=dev, group=group, fused=fused)
         st.full = full
         return st
 
@@ -140,6 +143,8 @@ class DecodeStack:
         """One decode step: x [K of the first matrix] -> the last matrix's y.
 
         ``trace``, when given, receives (matrix, input, full output) per GEMV."""
+        if self.fused is not None:
+            return self.fused.forward(x, trace)
         cur = x
         nk = len(self.shapes)
         for j, m in enumerate(self.mats):
@@ -166,3 +171,85 @@ class DecodeStack:
         with torch.cuda.graph(g):
             out = self.forward(x_static)
         return g, out
+
+
+class _FusedGather:
+    """Symmetric buffers, counters and call descriptors of a fused stack.
+
+    Every rank holds one full-y buffer per matrix kind and a counter array
+    (one counter per GEMV of a token plus one for the token fence) in
+    symmetric memory, so each GEMV kernel stores its rows into every rank's
+    buffer itself and signals with a counter (``qgemv_soa_fused``); a token
+    ends with ``qgemv_token_fence``.  No NCCL call is left on the path.
+    """
+
+    def __init__(self, st: "DecodeStack"):
+        import ctypes
+
+        import torch.distributed._symmetric_memory as symm_mem
+
+        from . import _lib
+
+        if not dist.is_initialized():
+            raise RuntimeError("the fused stack needs an initialised process group")
+        try:
+            symm_mem.set_backend("CUDA")
+        except Exception:
+            pass
+        self.st, self.lib = st, _lib.lib()
+        dev, world, rank = st.device, st.world, st.rank
+        group = st.group or dist.group.WORLD
+        n = len(st.mats)
+        self.y = [symm_mem.empty(M, dtype=torch.float32, device=dev) for _, M, _ in st.shapes]
+        self.y_h = [symm_mem.rendezvous(t, group) for t in self.y]
+        self.sig = symm_mem.empty(n + 1, dtype=torch.int32, device=dev)
+        self.sig.zero_()
+        self.sig_h = symm_mem.rendezvous(self.sig, group)
+        self.cta = torch.zeros(n, dtype=torch.int32, device=dev)
+        self.tok = torch.zeros(1, dtype=torch.int32, device=dev)
+        torch.cuda.synchronize(dev)
+        dist.barrier(group)
+        sig_ptrs = list(self.sig_h.buffer_ptrs)
+        nk = len(st.shapes)
+        self.desc = []
+        for j, m in enumerate(st.mats):
+            i = j % nk
+            d = _lib.FuseDesc()
+            peers = [k for k in range(world) if k != rank]
+            for slot, k in enumerate(peers):
+                d.peer_y[slot] = self.y_h[i].buffer_ptrs[k] + 4 * m.r0
+            for k in range(world):
+                d.sig_out[k] = sig_ptrs[k] + 4 * j
+            d.cta_count = self.cta.data_ptr() + 4 * j
+            d.sig_in = self.sig.data_ptr() + 4 * (j - 1) if j > 0 else None
+            d.tok = self.tok.data_ptr()
+            d.npeer, d.nranks = len(peers), world
+            self.desc.append(d)
+        self.done = (ctypes.c_void_p * world)(*[p + 4 * n for p in sig_ptrs])
+        self.done_local = self.sig.data_ptr() + 4 * n
+        self.fid = _lib.FORMAT_CODE[st.fmt]
+
+    def forward(self, x, trace=None):
+        """One token; returns this rank's full output buffer of the last GEMV
+        (complete once the token fence has run)."""
+        import ctypes
+
+        from . import _lib
+
+        if trace is not None:
+            raise ValueError("the fused stack keeps no per-GEMV outputs to trace")
+        st = self.st
+        nk = len(st.shapes)
+        s = torch.cuda.current_stream(st.device).cuda_stream
+        cur = x
+        for j, m in enumerate(st.mats):
+            i = j % nk
+            q = m.local
+            if q.layout != "soa":
+                raise ValueError("the fused stack runs on SoA planes")
+            _lib.call("qgemv_soa_fused", self.fid, q.q.data_ptr(), q.d.data_ptr(),
+                      cur[:m.K].data_ptr(), self.y[i][m.r0:m.r1].data_ptr(), m.r1 - m.r0, m.K,
+                      ctypes.byref(self.desc[j]), s)
+            cur = self.y[i]
+        _lib.call("qgemv_token_fence", self.done, st.world, self.done_local, self.tok.data_ptr(), s)
+        return cur

@@ -59,3 +59,44 @@ def test_7b_layer_shapes_spot_rows(fmt):
     rows = np.random.default_rng(0).choice(4096, 64, replace=False)
     check_trace(fmt, st, trace, rows=np.sort(rows))
     assert st.weight_bytes == stack.weight_bytes(fmt, n_layers=1)
+
+
+def _init_single_rank_group():
+    import os
+    import socket
+    import torch.distributed as dist
+    if dist.is_initialized():
+        return
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("nccl", rank=0, world_size=1, device_id=torch.device("cuda", 0))
+
+
+@pytest.mark.parametrize("fmt", ["q8_0", "q4_0"])
+def test_fused_stack_one_rank_matches_plain(fmt):
+    """The fused path (kernel-side stores and counters, token fence) on one
+    rank: same bits as the plain stack, over several graph replays (the
+    counters keep growing from token to token)."""
+    _init_single_rank_group()
+    shapes = (("qkv", 768, 512), ("o", 512, 512), ("gate_up", 1280, 512), ("down", 512, 768))
+    plain = stack.DecodeStack.from_random(fmt, n_layers=2, shapes=shapes, seed=6, device="cuda")
+    fused = stack.DecodeStack.from_random(fmt, n_layers=2, shapes=shapes, seed=6, device="cuda",
+                                          fused=True)
+    x = torch.randn(512, device="cuda")
+    y_plain = plain(x).clone()
+    y_fused = fused(x).clone()
+    torch.cuda.synchronize()
+    assert torch.equal(y_plain, y_fused)
+    g, out = fused.capture(x)
+    for _ in range(3):
+        out.zero_()
+        g.replay()
+        torch.cuda.synchronize()
+        assert torch.equal(out, y_plain)
+    from qgemv_roofline_b200 import _lib
+    assert _lib.lib().qgemv_check_device_error(0, None) == 0
+    del g
