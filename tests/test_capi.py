@@ -101,3 +101,38 @@ def test_python_raises_typed_error():
     with pytest.raises(_lib.QGemvError) as ei:
         _lib.call("qgemv_q8_0_soa", FAKE, FAKE, FAKE, FAKE, 64, 100, 1, 100, 64, None)
     assert ei.value.status == 2 and "QGEMV_ERR_SHAPE" in str(ei.value)
+
+
+def test_workspace_and_tile_sizes_are_host_computations():
+    lib = _lib.lib()
+    # batched SoA calls: 128 + 2064 * ceil(K / 512) * min(N, 16) bytes, 0 when no workspace
+    assert lib.qgemv_soa_workspace_bytes(8, 1000, 4096, 4) == 128 + 2064 * 8 * 4
+    assert lib.qgemv_soa_workspace_bytes(4, 1000, 4096, 40) == 128 + 2064 * 8 * 16
+    assert lib.qgemv_soa_workspace_bytes(8, 1000, 4096, 1) == 0
+    assert lib.qgemv_soa_workspace_bytes(8, 1000, 4000, 4) == 0     # K % 256 != 0
+    assert lib.qgemv_soa_workspace_bytes(3, 1000, 4096, 4) == 0     # bad format
+    assert lib.qgemv_tiled_workspace_bytes(800, 3) == 128 + 2064 * 2 * 3
+    assert lib.qgemv_tiled_workspace_bytes(800, 0) == 0
+    # batch tiles: ceil(M/16) * ceil(K/512) blocks of 16 x 512 quants + 512 scale bytes
+    assert lib.qgemv_tiled_bytes(8, 17, 800) == 2 * 2 * (16 * 512 + 512)
+    assert lib.qgemv_tiled_bytes(4, 16, 512) == 1 * 1 * (16 * 256 + 512)
+    assert lib.qgemv_tiled_bytes(8, 16, 33) == 0                    # K % 32 != 0
+
+
+def test_fused_and_tiled_validation():
+    from qgemv_roofline_b200._lib import FuseDesc
+    f = FuseDesc()
+    f.nranks = 0
+    assert rc("qgemv_soa_fused", 8, FAKE, FAKE, FAKE, FAKE, 64, 4096, ctypes.byref(f), None) == 7
+    f.nranks, f.npeer = 2, 1
+    assert rc("qgemv_soa_fused", 8, FAKE, FAKE, FAKE, FAKE, 64, 4096, ctypes.byref(f), None) == 1
+    assert rc("qgemv_soa_fused", 8, FAKE, FAKE, FAKE, FAKE, 64, 4096, None, None) == 1
+    assert rc("qgemv_token_fence", None, 0, FAKE, FAKE, None) == 7
+    assert rc("qgemv_token_fence", None, 2, FAKE, FAKE, None) == 1
+    assert rc("qgemv_tile_weights", 8, 2, FAKE, FAKE, 16, 512, FAKE, None) == 7   # bad layout
+    assert rc("qgemv_tile_weights", 8, 0, FAKE, FAKE, 16, 512, FAKE + 8, None) == 3
+    assert rc("qgemv_tiled_gemv", 8, FAKE, 16, 100, FAKE, FAKE, 1, 100, 16, None, 0, None) == 2
+    assert rc("qgemv_tiled_gemv", 8, FAKE, 16, 1 << 21, FAKE, FAKE, 1, 1 << 21, 16, None, 0,
+              None) == 5
+    assert rc("qgemv_tiled_gemv", 8, FAKE + 4, 16, 512, FAKE, FAKE, 1, 512, 16, None, 0,
+              None) == 3
