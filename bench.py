@@ -64,6 +64,8 @@ def parse():
                     help="xl: the headline 98304x4096 GEMV (default); stack: the 32-layer "
                          "decode GEMV stack; batch: 28672x8192 with 1..16 columns")
     ap.add_argument("--layers", type=int, default=32, help="stack workload: layers")
+    ap.add_argument("--persistent", action="store_true",
+                    help="stack workload, one GPU: all GEMVs of a token in one cooperative launch")
     ap.add_argument("--fused", action="store_true",
                     help="stack workload: all-gather inside the GEMV kernels (peer stores, "
                          "symmetric memory) instead of NCCL")
@@ -172,14 +174,15 @@ def stack_workload(args, rank, world, dev):
     with ClockSampler(uuid) as sampler:
         for fmt in ("q8_0", "q4_0"):
             st = stack.DecodeStack.from_random(fmt, n_layers=args.layers, seed=SEED, device=dev,
-                                               fused=args.fused)
+                                               fused=args.fused,
+                                               persistent=args.persistent and world == 1)
             g, out = st.capture(x)
             graphs.append(g)
             ms = _timed(torch, dist, dev, world, g.replay, args.warmup, args.steps)
             per = ms / args.steps
             res[fmt] = {"us_per_token": per * 1e3, "weight_bytes": st.weight_bytes,
                         "gbps_aggregate": st.weight_bytes / (per * 1e-3) / 1e9,
-                        "gemv_launches_per_token": len(st.mats),
+                        "gemv_launches_per_token": 1 if st.persistent is not None else len(st.mats),
                         "allgathers_per_token": (0 if args.fused else len(st.mats))
                         if world > 1 else 0}
             total_bytes += st.weight_bytes * args.steps
@@ -201,7 +204,8 @@ def stack_workload(args, rank, world, dev):
                                            ("all-gather of every y inside the GEMV kernels "
                                             "(peer stores, counters)" if args.fused else
                                             "NCCL all-gather of every y"))
-                           if world > 1 else "single GPU" + (", fused path" if args.fused else ""),
+                           if world > 1 else "single GPU" + (", fused path" if args.fused else "")
+                           + (", one persistent launch per token" if args.persistent else ""),
                            "step": "one token through all layers, q8_0 stack then q4_0 stack, "
                                    "each a CUDA graph replay",
                            "l2": "inputs larger than L2 (3.6-6.9 GB of weights per stack)"},

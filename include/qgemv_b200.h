@@ -140,6 +140,35 @@ QGEMV_API int qgemv_soa_static_ws(int format, const void* q, const void* d, cons
                                   float* y, int64_t M, int64_t K, int32_t ncols, int64_t ldx,
                                   int64_t ldy, void* stream);
 
+/* ------------------------------------------------ persistent decode stack --- */
+
+/* A sequence of single-column SoA GEMVs run by one cooperative launch per
+ * call of qgemv_stack_run (e.g. the 4 x n_layers GEMVs of a decode token):
+ * GEMV j may read GEMV j-1's y as its x; one CTA per SM keeps a row slice of
+ * every matrix and streams the next matrix's weights while the current one
+ * drains, so the per-launch completion and pipeline fill are paid once per
+ * sequence instead of once per GEMV.  Each GEMV needs the TMA kernel's shapes
+ * (256 <= K <= 16384, K % 256 == 0, q and x 16-byte aligned).  The pointers
+ * are fixed at creation (copy a new input into the first x buffer before a
+ * run); qgemv_stack_create allocates the handle's small device state (not on
+ * the GEMV path).  Grid-wide waits are bounded (~1 s; QGEMV_ERR_TIMEOUT in
+ * qgemv_check_device_error).  On the 32 layers of a 7B-shaped decode token it
+ * measured slower than one PDL launch per GEMV (a CTA holds only a few tiles
+ * of each matrix, so the grid-wide wait and the refill after it dominate);
+ * the per-launch path stays the default.  No reference counterpart (the
+ * reference timed one GEMV at a time). */
+typedef struct qgemv_stack_gemv {
+  const void* q;  /* quant plane */
+  const void* d;  /* scale plane */
+  const float* x; /* K inputs */
+  float* y;       /* M outputs */
+  int64_t M, K;
+} qgemv_stack_gemv;
+QGEMV_API int qgemv_stack_create(int format, const qgemv_stack_gemv* gemvs, int32_t n,
+                                 void** handle);
+QGEMV_API int qgemv_stack_run(void* handle, void* stream);
+QGEMV_API int qgemv_stack_destroy(void* handle);
+
 /* -------------------------------------------- fused all-gather (P GPUs) --- */
 
 /* Single-column SoA GEMV of this rank's rows whose y is all-gathered by the

@@ -33,6 +33,12 @@ class FuseDesc(ctypes.Structure):
                 ("tok", ctypes.c_void_p), ("npeer", ctypes.c_int32), ("nranks", ctypes.c_int32)]
 
 
+class StackGemvDesc(ctypes.Structure):
+    """qgemv_stack_gemv of include/qgemv_b200.h."""
+    _fields_ = [("q", ctypes.c_void_p), ("d", ctypes.c_void_p), ("x", ctypes.c_void_p),
+                ("y", ctypes.c_void_p), ("M", ctypes.c_int64), ("K", ctypes.c_int64)]
+
+
 class QGemvError(RuntimeError):
     """A C-ABI call returned a non-zero qgemv_status."""
 
@@ -98,6 +104,10 @@ SIGNATURES = {
     "qgemv_release_workspaces": ([], ctypes.c_int),
     "qgemv_soa_fused": ([ctypes.c_int, _vp, _vp, _vp, _vp, _i64, _i64, _vp, _vp], ctypes.c_int),
     "qgemv_token_fence": ([_vp, _i32, _vp, _vp, _vp], ctypes.c_int),
+    "qgemv_stack_create": ([ctypes.c_int, _vp, _i32, ctypes.POINTER(ctypes.c_void_p)],
+                           ctypes.c_int),
+    "qgemv_stack_run": ([_vp, _vp], ctypes.c_int),
+    "qgemv_stack_destroy": ([_vp], ctypes.c_int),
     "qgemv_soa_static_ws": ([ctypes.c_int, _vp, _vp, _vp, _vp, _i64, _i64, _i32, _i64, _i64, _vp],
                             ctypes.c_int),
     "qgemv_tiled_bytes": ([ctypes.c_int, _i64, _i64], ctypes.c_size_t),

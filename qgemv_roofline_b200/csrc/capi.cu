@@ -15,6 +15,7 @@
 #include <map>
 #include <set>
 #include <utility>
+#include <vector>
 
 #include "qgemv_common.cuh"
 #include "qgemv_internal.h"
@@ -415,6 +416,31 @@ QGEMV_API int qgemv_soa_fused(int format, const void* q, const void* d, const fl
   c.f.nranks = fuse->nranks;
   return gemv_soa_tma(format, c, static_cast<cudaStream_t>(stream));
 }
+
+QGEMV_API int qgemv_stack_create(int format, const qgemv_stack_gemv* gemvs, int32_t n,
+                                 void** handle) {
+  if (int rc = check_fmt(format)) return rc;
+  if (!gemvs || !handle) return set_error(ERR_NULL, "gemvs and handle must not be NULL");
+  if (n < 1 || n > 65536) return set_error(ERR_ARG, "n=%d out of range [1, 65536]", n);
+  std::vector<StackCall> calls(n);
+  for (int j = 0; j < n; ++j) {
+    const qgemv_stack_gemv& g = gemvs[j];
+    if (int rc = check_mk(g.M, g.K)) return rc;
+    if (!g.q || !g.d || !g.x || !g.y) return set_error(ERR_NULL, "stack GEMV %d: NULL pointer", j);
+    if (misaligned(g.d, 2) || misaligned(g.y, 4))
+      return set_error(ERR_ALIGN, "stack GEMV %d: d must be 2-byte and y 4-byte aligned", j);
+    calls[j] = StackCall{g.q, g.d, g.x, g.y, g.M, g.K};
+  }
+  *handle = nullptr;
+  return stack_create(format, calls.data(), n, handle);
+}
+
+QGEMV_API int qgemv_stack_run(void* handle, void* stream) {
+  if (!handle) return set_error(ERR_NULL, "handle must not be NULL");
+  return stack_run(handle, static_cast<cudaStream_t>(stream));
+}
+
+QGEMV_API int qgemv_stack_destroy(void* handle) { return stack_destroy(handle); }
 
 QGEMV_API int qgemv_token_fence(unsigned* const* done, int32_t nranks, const unsigned* done_local,
                                 unsigned* tok, void* stream) {

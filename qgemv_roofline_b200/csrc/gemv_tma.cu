@@ -40,6 +40,7 @@
 #include <algorithm>
 #include <map>
 #include <mutex>
+#include <vector>
 
 namespace qg {
 
@@ -197,6 +198,8 @@ struct XPlanes {
   bool finite;
 };
 
+__device__ __forceinline__ void make_planes_from(const float (&v)[32], XPlanes& o);
+
 __device__ __forceinline__ void make_planes(const float* __restrict__ xb, XPlanes& o) {
   float v[32];
 #pragma unroll
@@ -204,6 +207,10 @@ __device__ __forceinline__ void make_planes(const float* __restrict__ xb, XPlane
     const float4 f = *reinterpret_cast<const float4*>(xb + 4 * i);
     v[4 * i] = f.x; v[4 * i + 1] = f.y; v[4 * i + 2] = f.z; v[4 * i + 3] = f.w;
   }
+  make_planes_from(v, o);
+}
+
+__device__ __forceinline__ void make_planes_from(const float (&v)[32], XPlanes& o) {
   uint32_t amax = 0u;  // bits of max |x| (ordered like the values for non-NaN)
 #pragma unroll
   for (int j = 0; j < 32; ++j) amax = max(amax, __float_as_uint(v[j]) & 0x7FFFFFFFu);
@@ -235,6 +242,65 @@ __device__ __forceinline__ void make_planes(const float* __restrict__ xb, XPlane
                                 __byte_perm(X[4 * w + 2], X[4 * w + 3], sel), 0x5410);
     }
   }
+}
+
+// The exact integer dot of one 32-weight block with the x planes, folded to
+// one float: F = S2 2^16 + (S1 2^8 + S0) (q4_0: 16 x that, minus the bias of
+// the -8 offset).  wq: the block's quant words (q8_0: 8 words of int8, word w
+// = elements 4w..4w+3; q4_0: 4 words, word t = elements 4t..4t+3 in the low
+// nibbles and 16+4t.. in the high nibbles).
+template <int FMT>
+__device__ __forceinline__ float block_fold(const uint32_t* wq, const XPlanes& xp) {
+  int S0 = 0, S1 = 0, S2 = 0;
+  if (FMT == 8) {
+#pragma unroll
+    for (int w = 0; w < 8; ++w) {
+      S0 = dp4a_su(wq[w], xp.pl[w][0], S0);
+      S1 = dp4a_su(wq[w], xp.pl[w][1], S1);
+      S2 = dp4a_ss(wq[w], xp.pl[w][2], S2);
+    }
+  } else {
+    uint32_t L0 = 0u, L1 = 0u, H0 = 0u, H1 = 0u;
+    int H2 = 0;
+#pragma unroll
+    for (int t4 = 0; t4 < 4; ++t4) {
+      const uint32_t lo = wq[t4] & 0x0F0F0F0Fu, hi = wq[t4] & 0xF0F0F0F0u;
+      L0 = dp4a_uu(lo, xp.pl[t4][0], L0);
+      L1 = dp4a_uu(lo, xp.pl[t4][1], L1);
+      S2 = dp4a_us(lo, xp.pl[t4][2], S2);
+      H0 = dp4a_uu(hi, xp.pl[t4 + 4][0], H0);
+      H1 = dp4a_uu(hi, xp.pl[t4 + 4][1], H1);
+      H2 = dp4a_us(hi, xp.pl[t4 + 4][2], H2);
+    }
+    // 16 * sum n X per plane (all below 2^21 in magnitude)
+    S0 = (int)((L0 << 4) + H0);
+    S1 = (int)((L1 << 4) + H1);
+    S2 = (S2 << 4) + H2;
+  }
+  // fold the two low planes in int32 (< 2^30), then one fp32 combination
+  const int lo = (S1 << 8) + S0;
+  float Fv = fmaf((float)S2, 65536.0f, (float)lo);
+  // q4_0: 16 * sum (n - 8) X = 16 sum n X - 128 sum X; the 1/16 is in the block scale
+  if (FMT == 4) Fv -= xp.bias;
+  return Fv;
+}
+
+// The block scale 2^t of a lane's x block: t = e - 22 (q4_0: - 4 more), as
+// two exact power-of-two factors (each a normal float for every e), or as one
+// when d * 2^t is exact for every fp16 d; NaN for a non-finite block.
+struct XScale {
+  float xs1, xs2, xsc;
+  bool one_factor;
+};
+template <int FMT>
+__device__ __forceinline__ XScale x_scale(const XPlanes& xp) {
+  XScale r;
+  const int t = xp.e - 22 - (FMT == 4 ? 4 : 0), h = t / 2;
+  r.xs1 = xp.finite ? __int_as_float((127 + h) << 23) : __int_as_float(0x7FC00000);
+  r.xs2 = __int_as_float((127 + t - h) << 23);
+  r.one_factor = t >= -100 && t <= 100;
+  r.xsc = r.one_factor ? r.xs1 * r.xs2 : 0.0f;
+  return r;
 }
 
 struct TmaArgs {
@@ -444,18 +510,15 @@ k_gemv_tma(const TmaArgs p) {
       xp.finite = true;
     }
     // X_j = x_j 2^(22-e): the block's dot is its integer dot times 2^(e-22)
-    // (q4_0: times 2^-4 more, see below).  Split in two exact power-of-two
-    // factors, each a normal float for every e, so the product only rounds
-    // where the true value itself under- or overflows.  NaN for a non-finite
-    // block so that y is NaN, as a float dot product would be.
-    const int t = xp.e - 22 - (FMT == 4 ? 4 : 0), h = t / 2;
-    xs1 = xp.finite ? __int_as_float((127 + h) << 23) : __int_as_float(0x7FC00000);
-    xs2 = __int_as_float((127 + t - h) << 23);
-    // one factor when d * 2^t is exact for every fp16 d (no overflow, no
-    // subnormal result): true for all but extreme x, and then (d * 2^t) * F
-    // is the same correctly rounded product as (d * F) * 2^t
-    one_factor = t >= -100 && t <= 100;
-    xsc = one_factor ? xs1 * xs2 : 0.0f;
+    // (q4_0: times 2^-4 more).  With one factor (d * 2^t exact for every fp16
+    // d: all but extreme x), (d * 2^t) * F is the same correctly rounded
+    // product as (d * F) * 2^t; otherwise two exact factors, so the product
+    // only rounds where the true value itself under- or overflows.
+    const XScale xq = x_scale<FMT>(xp);
+    xs1 = xq.xs1;
+    xs2 = xq.xs2;
+    one_factor = xq.one_factor;
+    xsc = xq.xsc;
   }
 
   for (int t = 0; t < ntiles; ++t) {
@@ -520,7 +583,6 @@ k_gemv_tma(const TmaArgs p) {
 #pragma unroll
           for (int r = 0; r < R; ++r) {
             const uint8_t* rowp = st + (size_t)(r0 + r) * QB;
-            int S0 = 0, S1 = 0, S2 = 0;
             // AoS: the lane's block starts at byte cidx * (34|18) of the row
             // (2-byte aligned; rows start on 16-byte boundaries); read the
             // aligned words covering it and realign the quants with PRMT.
@@ -535,58 +597,24 @@ k_gemv_tma(const TmaArgs p) {
 #pragma unroll
               for (int i = 0; i < QW; ++i) aw[i] = __byte_perm(wd[i], wd[i + 1], aos_sel);
             }
-            if (FMT == 8) {
+            uint32_t wq[FMT == 8 ? 8 : 4];
+            if (AOS) {
+#pragma unroll
+              for (int w = 0; w < (FMT == 8 ? 8 : 4); ++w) wq[w] = aw[w % QW];
+            } else if (FMT == 8) {
               // 32 signed quants: words w = 0..7 hold elements 4w..4w+3
-              uint32_t wq[8];
-              if (AOS) {
-#pragma unroll
-                for (int w = 0; w < 8; ++w) wq[w] = aw[w % QW];
-              } else {
-                const uint4 u0 = *reinterpret_cast<const uint4*>(rowp + cidx * 32);
-                const uint4 u1 = *reinterpret_cast<const uint4*>(rowp + cidx * 32 + 16);
-                wq[0] = u0.x; wq[1] = u0.y; wq[2] = u0.z; wq[3] = u0.w;
-                wq[4] = u1.x; wq[5] = u1.y; wq[6] = u1.z; wq[7] = u1.w;
-              }
-#pragma unroll
-              for (int w = 0; w < 8; ++w) {
-                S0 = dp4a_su(wq[w], xp.pl[w][0], S0);
-                S1 = dp4a_su(wq[w], xp.pl[w][1], S1);
-                S2 = dp4a_ss(wq[w], xp.pl[w][2], S2);
-              }
+              const uint4 u0 = *reinterpret_cast<const uint4*>(rowp + cidx * 32);
+              const uint4 u1 = *reinterpret_cast<const uint4*>(rowp + cidx * 32 + 16);
+              wq[0] = u0.x; wq[1] = u0.y; wq[2] = u0.z; wq[3] = u0.w;
+              wq[4 % (FMT == 8 ? 8 : 4)] = u1.x; wq[5 % (FMT == 8 ? 8 : 4)] = u1.y;
+              wq[6 % (FMT == 8 ? 8 : 4)] = u1.z; wq[7 % (FMT == 8 ? 8 : 4)] = u1.w;
             } else {
               // 16 bytes: word t holds elements 4t..4t+3 (low nibbles) and
               // 16+4t..16+4t+3 (high nibbles, taken in place as 16 * n)
-              uint32_t wq[4];
-              if (AOS) {
-#pragma unroll
-                for (int w = 0; w < 4; ++w) wq[w] = aw[w];
-              } else {
-                const uint4 u = *reinterpret_cast<const uint4*>(rowp + cidx * 16);
-                wq[0] = u.x; wq[1] = u.y; wq[2] = u.z; wq[3] = u.w;
-              }
-              uint32_t L0 = 0u, L1 = 0u, H0 = 0u, H1 = 0u;
-              int H2 = 0;
-#pragma unroll
-              for (int t4 = 0; t4 < 4; ++t4) {
-                const uint32_t lo = wq[t4] & 0x0F0F0F0Fu, hi = wq[t4] & 0xF0F0F0F0u;
-                L0 = dp4a_uu(lo, xp.pl[t4][0], L0);
-                L1 = dp4a_uu(lo, xp.pl[t4][1], L1);
-                S2 = dp4a_us(lo, xp.pl[t4][2], S2);
-                H0 = dp4a_uu(hi, xp.pl[t4 + 4][0], H0);
-                H1 = dp4a_uu(hi, xp.pl[t4 + 4][1], H1);
-                H2 = dp4a_us(hi, xp.pl[t4 + 4][2], H2);
-              }
-              // 16 * sum n X per plane (all below 2^21 in magnitude)
-              S0 = (int)((L0 << 4) + H0);
-              S1 = (int)((L1 << 4) + H1);
-              S2 = (S2 << 4) + H2;
+              const uint4 u = *reinterpret_cast<const uint4*>(rowp + cidx * 16);
+              wq[0] = u.x; wq[1] = u.y; wq[2] = u.z; wq[3] = u.w;
             }
-            // fold the two low planes in int32 (< 2^30), then one fp32
-            // combination: F = S2 * 2^16 + (S1 * 2^8 + S0)
-            const int lo = (S1 << 8) + S0;
-            float Fv = fmaf((float)S2, 65536.0f, (float)lo);
-            // q4_0: 16 * sum (n - 8) X = 16 sum n X - 128 sum X; the 1/16 is in xs1 xs2
-            if (FMT == 4) Fv -= xp.bias;
+            const float Fv = block_fold<FMT>(wq, xp);
             acc[r] = one_factor ? (dv[r] * xsc) * Fv : ((dv[r] * Fv) * xs1) * xs2;
           }
         }
@@ -598,6 +626,266 @@ k_gemv_tma(const TmaArgs p) {
     __syncwarp();
     if (lane == 0)
       asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(saddr(&empty[s])) : "memory");
+  }
+}
+
+// ------------------------------------------------- persistent decode stack
+// One cooperative launch runs a whole sequence of single-column GEMVs (a
+// decode token: QKV, O, gate+up, down per layer), GEMV j reading GEMV j-1's
+// output.  One CTA per SM keeps a row slice of every matrix; its producer
+// warp streams the tiles of GEMV j, j+1, ... through one ring without
+// pausing at GEMV boundaries (weights never depend on x), so the next
+// matrix's first tiles are in shared memory while the current one drains.
+// The consumers of GEMV j+1 wait until every CTA has written its rows of
+// GEMV j (a grid-wide counter, bounded wait), read x from L2 and convert it
+// to planes, then run the arithmetic of k_gemv_tma.  What the per-launch
+// chain paid at every GEMV -- grid completion, the next launch, its
+// pipeline fill -- is paid once per token.
+struct StackGemv {
+  const uint8_t* q;
+  const unsigned short* d;
+  const float* x;
+  float* y;
+  int M, K, TR, KS;
+};
+struct StackArgs {
+  const StackGemv* g;
+  int n;
+  unsigned* bar;  // per GEMV: CTAs that have written their rows (zeroed at the end)
+  int S, SB, PB;  // ring stages, bytes per stage, partial floats per stage
+};
+
+__device__ __forceinline__ unsigned ld_acquire_gpu(const unsigned* p) {
+  unsigned v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// Bounded wait (~1 s) for a grid-wide counter of this device, polling with a
+// short sleep so the CTAs that increment it are not slowed by the polls.
+__device__ __forceinline__ bool wait_grid(const unsigned* c, unsigned target,
+                                          volatile int* abort_flag) {
+  if ((int)(ld_acquire_gpu(c) - target) >= 0) return true;
+  const long long t0 = clock64();
+  while ((int)(ld_acquire_gpu(c) - target) < 0) {
+    if (*abort_flag) return false;
+    if (clock64() - t0 > SPIN_LIMIT) {
+      *abort_flag = 1;
+      atomicExch(&g_device_error, (int)ERR_TIMEOUT);
+      return false;
+    }
+    __nanosleep(64);
+  }
+  return true;
+}
+
+// x planes from memory written by other CTAs of this grid: L2 loads (.cg)
+__device__ __forceinline__ void make_planes_l2(const float* __restrict__ xb, XPlanes& o) {
+  float v[32];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const float4 f = __ldcg(reinterpret_cast<const float4*>(xb + 4 * i));
+    v[4 * i] = f.x; v[4 * i + 1] = f.y; v[4 * i + 2] = f.z; v[4 * i + 3] = f.w;
+  }
+  make_planes_from(v, o);
+}
+
+template <int FMT, int R>
+__global__ void __launch_bounds__(tma_threads(16), 1) k_gemv_stack(const __grid_constant__ StackArgs p) {
+  constexpr int CONSUMERS = 16;
+  using F = Fmt<FMT>;
+  extern __shared__ __align__(128) uint8_t sm[];
+  __shared__ __align__(8) unsigned long long full[MAX_STAGES];
+  __shared__ __align__(8) unsigned long long empty[MAX_STAGES];
+  __shared__ int abort_flag;
+
+  const int S = p.S, G = gridDim.x, b = blockIdx.x;
+  float* part = reinterpret_cast<float*>(sm + (size_t)S * p.SB);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S; ++s) {
+      asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(saddr(&full[s])));
+      asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(saddr(&empty[s])),
+                   "r"(CONSUMERS));
+    }
+    abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  __syncthreads();
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    // issue cursor (ji, ti) and finalize cursor (jf, tf) over (GEMV, tile)
+    int ji = 0, ti = 0, jf = 0, tf = 0;
+    uint32_t u = 0, f = 0;
+    int last_issued[MAX_STAGES];
+    for (int s = 0; s < MAX_STAGES; ++s) last_issued[s] = -1;
+    auto rows_of = [&](int j, int& a, int& nrows) {
+      const int M = p.g[j].M;
+      a = (int)((int64_t)M * b / G);
+      nrows = (int)((int64_t)M * (b + 1) / G) - a;
+    };
+    bool ok = true;
+    for (;;) {
+      // issue while the ring has room
+      while (ji < p.n && u - f < (uint32_t)S) {
+        int a, nrows;
+        rows_of(ji, a, nrows);
+        const StackGemv g = p.g[ji];
+        const int ntiles = (nrows + g.TR - 1) / g.TR;
+        if (ti >= ntiles) {
+          ++ji;
+          ti = 0;
+          continue;
+        }
+        if (lane == 0) {
+          const int s = (int)(u % (uint32_t)S);
+          const int QB = g.K / F::ROW_DIV, DB = g.K / 16;
+          const int r0 = ti * g.TR, nr = min(g.TR, nrows - r0);
+          const uint32_t bar = saddr(&full[s]);
+          uint8_t* st = sm + (size_t)s * p.SB;
+          asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar),
+                       "r"((uint32_t)nr * (QB + DB))
+                       : "memory");
+          bulk_g2s(saddr(st), g.q + (int64_t)(a + r0) * QB, (uint32_t)nr * QB, bar);
+          bulk_g2s(saddr(st + (size_t)g.TR * QB),
+                   reinterpret_cast<const uint8_t*>(g.d) + (int64_t)(a + r0) * DB,
+                   (uint32_t)nr * DB, bar);
+          last_issued[s] = (int)u;
+        }
+        ++ti;
+        ++u;
+      }
+      if (jf >= p.n) break;
+      int a, nrows;
+      rows_of(jf, a, nrows);
+      const StackGemv g = p.g[jf];
+      const int ntiles = (nrows + g.TR - 1) / g.TR;
+      if (tf < ntiles) {
+        // finalize tile f: the consumers are done with it; write its rows of y
+        const int s = (int)(f % (uint32_t)S);
+        ok = __all_sync(0xffffffffu, mbar_wait(saddr(&empty[s]), (f / (uint32_t)S) & 1u,
+                                               &abort_flag));
+        if (!ok) break;
+        const int r0 = tf * g.TR, nr = min(g.TR, nrows - r0);
+        const float* ps = part + (size_t)s * p.PB;
+        for (int i = lane; i < nr; i += 32) {  // partials [KS][TR]: conflict-free
+          float v = 0.0f;
+          for (int k = 0; k < g.KS; ++k) v += ps[k * g.TR + i];
+          g.y[a + r0 + i] = v;
+        }
+        __syncwarp();
+        ++tf;
+        ++f;
+      }
+      if (tf >= ntiles) {
+        // this CTA's rows of GEMV jf are written: count it for the grid
+        __threadfence();
+        __syncwarp();
+        if (lane == 0) atomicAdd(&p.bar[jf], 1u);
+        ++jf;
+        tf = 0;
+      }
+    }
+    if (!ok && lane == 0) {
+      for (int s = 0; s < S; ++s)
+        if (last_issued[s] >= 0)
+          mbar_wait_drain(saddr(&full[s]), (uint32_t)((last_issued[s] / S) & 1));
+    }
+    if (b == 0 && lane == 0 && ok) {
+      // every CTA has passed every wait once all have counted the last GEMV:
+      // reset the counters for the next token
+      if (wait_grid(&p.bar[p.n - 1], (unsigned)G, &abort_flag)) {
+        for (int j = 0; j < p.n; ++j) atomicExch(&p.bar[j], 0u);
+        __threadfence();
+      }
+    }
+    return;
+  }
+
+  // -------------------------------------------------------------- consumers
+  const int cw = warp - 1;
+  uint32_t u = 0;
+  bool dead = false;  // after an abort: still reach every named barrier, do no work
+  for (int j = 0; j < p.n; ++j) {
+    const StackGemv g = p.g[j];
+    const int KS = g.KS, ks = cw % KS, rg = cw / KS, RG = CONSUMERS / KS;
+    const int QB = g.K / F::ROW_DIV, DB = g.K / 16;
+    const int a = (int)((int64_t)g.M * b / G);
+    const int nrows = (int)((int64_t)g.M * (b + 1) / G) - a;
+    const int ntiles = (nrows + g.TR - 1) / g.TR;
+    const int c = ks * 32 + lane;
+    const bool cval = c < g.K / QK;
+    const int cidx = cval ? c : 0;
+    if (j > 0) {
+      // x = GEMV j-1's y: one thread waits (bounded) until every CTA has
+      // written its rows; the other consumers wait for it at a named barrier
+      // (the producer warp is not part of it), which the waiting thread
+      // always reaches.
+      if (cw == 0 && lane == 0 && !dead) wait_grid(&p.bar[j - 1], (unsigned)G, &abort_flag);
+      asm volatile("bar.sync 1, %0;" ::"r"(CONSUMERS * 32) : "memory");
+      if (abort_flag) dead = true;
+    }
+    if (dead) continue;
+    XPlanes xp;
+    if (cval) {
+      if (j > 0) make_planes_l2(g.x + cidx * 32, xp);
+      else make_planes(g.x + cidx * 32, xp);
+    } else {
+      for (int w = 0; w < 8; ++w)
+        for (int pl = 0; pl < NPL; ++pl) xp.pl[w][pl] = 0u;
+      xp.e = -149;
+      xp.bias = 0.0f;
+      xp.finite = true;
+    }
+    const XScale xq = x_scale<FMT>(xp);
+    bool ok = true;
+    for (int t = 0; t < ntiles; ++t, ++u) {
+      const int s = (int)(u % (uint32_t)S);
+      if (!__all_sync(0xffffffffu, mbar_wait(saddr(&full[s]), (u / (uint32_t)S) & 1u,
+                                             &abort_flag))) {
+        ok = false;
+        break;
+      }
+      const int nr = min(g.TR, nrows - t * g.TR);
+      const uint8_t* st = sm + (size_t)s * p.SB;
+      const uint8_t* sd = st + (size_t)g.TR * QB;
+      float* ps = part + (size_t)s * p.PB;
+      for (int r0 = rg * R; r0 < nr; r0 += RG * R) {
+        float acc[R];
+#pragma unroll
+        for (int r = 0; r < R; ++r) acc[r] = 0.0f;
+        if (cval) {
+          // rows beyond nr read stale in-bounds bytes; never stored
+#pragma unroll
+          for (int r = 0; r < R; ++r) {
+            const uint8_t* rowp = st + (size_t)(r0 + r) * QB;
+            const float dv = half_bits_to_float(
+                *reinterpret_cast<const unsigned short*>(sd + (size_t)(r0 + r) * DB + cidx * 2));
+            uint32_t wq[FMT == 8 ? 8 : 4];
+            if (FMT == 8) {
+              const uint4 u0 = *reinterpret_cast<const uint4*>(rowp + cidx * 32);
+              const uint4 u1 = *reinterpret_cast<const uint4*>(rowp + cidx * 32 + 16);
+              wq[0] = u0.x; wq[1] = u0.y; wq[2] = u0.z; wq[3] = u0.w;
+              wq[4 % (FMT == 8 ? 8 : 4)] = u1.x; wq[5 % (FMT == 8 ? 8 : 4)] = u1.y;
+              wq[6 % (FMT == 8 ? 8 : 4)] = u1.z; wq[7 % (FMT == 8 ? 8 : 4)] = u1.w;
+            } else {
+              const uint4 uq = *reinterpret_cast<const uint4*>(rowp + cidx * 16);
+              wq[0] = uq.x; wq[1] = uq.y; wq[2] = uq.z; wq[3] = uq.w;
+            }
+            const float Fv = block_fold<FMT>(wq, xp);
+            acc[r] = xq.one_factor ? (dv * xq.xsc) * Fv : ((dv * Fv) * xq.xs1) * xq.xs2;
+          }
+        }
+        const float v = reduce_rows<R>(acc, lane);
+        const int r = row_of_lane<R>(lane);
+        if ((lane & (32 / R - 1)) == 0 && r0 + r < nr) ps[ks * g.TR + r0 + r] = v;
+      }
+      __syncwarp();
+      if (lane == 0)
+        asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(saddr(&empty[s])) : "memory");
+    }
+    if (!ok) dead = true;
   }
 }
 
@@ -778,6 +1066,107 @@ int token_fence(unsigned* const* done, int nranks, const unsigned* done_local, u
   f.nranks = nranks;
   k_token_fence<<<1, 32, 0, st>>>(f);
   return check_launch("k_token_fence");
+}
+
+namespace {
+struct StackHandle {
+  int fmt, device, n, grid;
+  StackArgs args;
+  size_t smem;
+  StackGemv* dev_g;
+  unsigned* dev_bar;
+};
+}  // namespace
+
+int stack_create(int fmt, const StackCall* calls, int n, void** out) {
+  DeviceInfo dev;
+  if (int rc = current_device_info(dev)) return rc;
+  if (n < 1) return set_error(ERR_ARG, "a stack needs at least one GEMV");
+  const int R = fmt == 8 ? 4 : 8;  // rows per warp pass, as in the per-launch kernel
+  std::vector<StackGemv> g(n);
+  int SB = 0, PB = 0;
+  for (int j = 0; j < n; ++j) {
+    const StackCall& c = calls[j];
+    if (c.K < 256 || c.K % 256 || c.K > 16384 || c.M < 1)
+      return set_error(ERR_UNSUPPORTED, "stack GEMV %d: needs 256 <= K <= 16384, K %% 256 == 0", j);
+    if ((reinterpret_cast<uintptr_t>(c.x) & 15) || (reinterpret_cast<uintptr_t>(c.q) & 15))
+      return set_error(ERR_ALIGN, "stack GEMV %d: q and x must be 16-byte aligned", j);
+    const int QB = (int)(fmt == 8 ? c.K : c.K / 2), DB = (int)(c.K / 16), row = QB + DB;
+    const int nunits = (int)(c.K / QK);
+    int KS = 1;
+    while (KS * 32 < nunits) KS *= 2;
+    const int unit = (16 / KS) * R;
+    const int TR = unit * std::max(1, (32 * 1024) / (unit * row));
+    g[j] = StackGemv{static_cast<const uint8_t*>(c.q), static_cast<const unsigned short*>(c.d),
+                     c.x, c.y, (int)c.M, (int)c.K, TR, KS};
+    SB = std::max(SB, (TR * row + 15) / 16 * 16);
+    PB = std::max(PB, TR * KS);
+  }
+  auto kern = fmt == 8 ? k_gemv_stack<8, 4> : k_gemv_stack<4, 8>;
+  const void* kp = reinterpret_cast<const void*>(kern);
+  if (int rc = allow_max_smem(kp, dev)) return rc;
+  cudaFuncAttributes fa;
+  if (cudaFuncGetAttributes(&fa, kp) != cudaSuccess) return check_launch("cudaFuncGetAttributes");
+  const int avail = dev.smem_optin - (int)fa.sharedSizeBytes;
+  const int S = std::min(MAX_STAGES, avail / (SB + 4 * PB));
+  if (S < 2) return set_error(ERR_UNSUPPORTED, "stack tiles of %d bytes do not fit twice", SB);
+  StackHandle* h = new StackHandle();
+  h->fmt = fmt;
+  h->device = dev.device;
+  h->n = n;
+  h->grid = dev.sms;
+  h->smem = (size_t)S * (SB + 4 * PB);
+  cudaError_t e = cudaMalloc(&h->dev_g, sizeof(StackGemv) * n);
+  if (e == cudaSuccess) e = cudaMalloc(&h->dev_bar, sizeof(unsigned) * n);
+  if (e == cudaSuccess) e = cudaMemcpy(h->dev_g, g.data(), sizeof(StackGemv) * n, cudaMemcpyHostToDevice);
+  if (e == cudaSuccess) e = cudaMemset(h->dev_bar, 0, sizeof(unsigned) * n);
+  if (e != cudaSuccess) {
+    cudaFree(h->dev_g);
+    cudaFree(h->dev_bar);
+    delete h;
+    return set_error(ERR_CUDA, "stack set-up: %s", cudaGetErrorString(e));
+  }
+  h->args = StackArgs{h->dev_g, n, h->dev_bar, S, SB, PB};
+  *out = h;
+  return OK;
+}
+
+int stack_run(void* handle, cudaStream_t st) {
+  StackHandle* h = static_cast<StackHandle*>(handle);
+  int cur = 0;
+  cudaGetDevice(&cur);
+  if (cur != h->device)
+    return set_error(ERR_ARG, "the stack was made on device %d, the current device is %d",
+                     h->device, cur);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(h->grid);
+  cfg.blockDim = dim3(tma_threads(16));
+  cfg.dynamicSmemBytes = h->smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeCooperative;  // every CTA resident: grid-wide waits
+  attr[0].val.cooperative = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  const cudaError_t e = h->fmt == 8 ? cudaLaunchKernelEx(&cfg, k_gemv_stack<8, 4>, h->args)
+                                    : cudaLaunchKernelEx(&cfg, k_gemv_stack<4, 8>, h->args);
+  if (e != cudaSuccess) return set_error(ERR_CUDA, "k_gemv_stack launch: %s", cudaGetErrorString(e));
+  return check_launch("k_gemv_stack");
+}
+
+int stack_destroy(void* handle) {
+  StackHandle* h = static_cast<StackHandle*>(handle);
+  if (!h) return OK;
+  int cur = 0;
+  cudaGetDevice(&cur);
+  cudaSetDevice(h->device);
+  cudaError_t e = cudaDeviceSynchronize();
+  cudaFree(h->dev_g);
+  cudaFree(h->dev_bar);
+  cudaSetDevice(cur);
+  delete h;
+  if (e != cudaSuccess) return set_error(ERR_CUDA, "stack release: %s", cudaGetErrorString(e));
+  return OK;
 }
 
 int read_device_error(int clear, cudaStream_t st, int* out) {

@@ -68,6 +68,18 @@ int gemv_soa_tma_mode(int fmt, int mode, const GemvCall& c, cudaStream_t st);
 // GGUF-layout blocks on the TMA path; -1 when the shape is not eligible.
 int gemv_aos_tma(int fmt, const GemvCall& c, cudaStream_t st);
 int read_device_error(int clear, cudaStream_t st, int* out);
+// Persistent decode stack: a sequence of single-column SoA GEMVs in one
+// cooperative launch (GEMV j usually reads GEMV j-1's y).
+struct StackCall {
+  const void* q;
+  const void* d;
+  const float* x;
+  float* y;
+  int64_t M, K;
+};
+int stack_create(int fmt, const StackCall* calls, int n, void** out);
+int stack_run(void* handle, cudaStream_t st);
+int stack_destroy(void* handle);
 // End of a token of fused calls: signal every rank's done[k], wait (bounded)
 // until done_local reaches (*tok + 1) * nranks, then advance *tok.
 int token_fence(unsigned* const* done, int nranks, const unsigned* done_local, unsigned* tok,

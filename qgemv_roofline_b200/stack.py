@@ -64,7 +64,8 @@ class DecodeStack:
 
     def __init__(self, fmt: str, matrices: list[StackMatrix], n_layers: int,
                  shapes: Sequence = LAYER_7B, device=None, group=None,
-                 local_gemv: Callable | None = None, fused: bool = False):
+                 local_gemv: Callable | None = None, fused: bool = False,
+                 persistent: bool = False):
         self.fmt, self.n_layers, self.shapes = fmt, n_layers, tuple(shapes)
         self.group = group
         self.world = dist.get_world_size(group) if dist.is_initialized() else 1
@@ -83,11 +84,17 @@ class DecodeStack:
         self.fused = None
         if fused:
             self.fused = _FusedGather(self)
+        self.persistent = None
+        if persistent:
+            if self.world != 1 or fused:
+                raise ValueError("the persistent stack runs on one GPU")
+            self.persistent = _PersistentStack(self)
 
     @classmethod
     def from_random(cls, fmt: str, n_layers: int = 32, shapes: Sequence = LAYER_7B,
                     seed: int = 0, device=None, group=None, layout: str = "soa",
-                    keep_full: bool = False, fused: bool = False) -> "DecodeStack":
+                    keep_full: bool = False, fused: bool = False,
+                    persistent: bool = False) -> "DecodeStack":
         """Seeded weights W ~ N(0, 0.02), generated and quantized on ``device``;
         each rank keeps its rows (``keep_full`` also keeps the full matrices on
         ``.full``, for tests)."""
@@ -112,7 +119,8 @@ class DecodeStack:
                 if keep_full:
                     full.append((q, d))
                 del q, d
-        st = cls(fmt, mats, n_layers, shapes, device=dev, group=group, fused=fused)
+        st = cls(fmt, mats, n_layers, shapes, device=dev, group=group, fused=fused,
+                 persistent=persistent)
         st.full = full
         return st
 
@@ -145,6 +153,8 @@ class DecodeStack:
         ``trace``, when given, receives (matrix, input, full output) per GEMV."""
         if self.fused is not None:
             return self.fused.forward(x, trace)
+        if self.persistent is not None:
+            return self.persistent.forward(x, trace)
         cur = x
         nk = len(self.shapes)
         for j, m in enumerate(self.mats):
@@ -253,3 +263,54 @@ class _FusedGather:
             cur = self.y[i]
         _lib.call("qgemv_token_fence", self.done, st.world, self.done_local, self.tok.data_ptr(), s)
         return cur
+
+
+class _PersistentStack:
+    """All GEMVs of a token in one cooperative launch (``qgemv_stack_run``):
+    one CTA per SM streams the next matrix while the current one drains, and
+    grid-wide counters order GEMV j+1's reads of x after GEMV j's writes.
+    Opt-in: on 7B-shaped layers it is slower than one launch per GEMV, since
+    each CTA holds only a few tiles of a matrix and waits for the whole grid
+    before the next one."""
+
+    def __init__(self, st: "DecodeStack"):
+        import ctypes
+
+        from . import _lib
+
+        self.st, self.lib = st, _lib.lib()
+        nk = len(st.shapes)
+        K0 = st.mats[0].K
+        self.x_in = torch.empty(K0, dtype=torch.float32, device=st.device)
+        descs = (_lib.StackGemvDesc * len(st.mats))()
+        for j, m in enumerate(st.mats):
+            q = m.local
+            if q.layout != "soa":
+                raise ValueError("the persistent stack runs on SoA planes")
+            x = self.x_in if j == 0 else st.y_local[(j - 1) % nk]
+            descs[j] = _lib.StackGemvDesc(q.q.data_ptr(), q.d.data_ptr(), x.data_ptr(),
+                                          st.y_local[j % nk].data_ptr(), m.M, m.K)
+        h = ctypes.c_void_p()
+        _lib.call("qgemv_stack_create", _lib.FORMAT_CODE[st.fmt], descs, len(st.mats),
+                  ctypes.byref(h))
+        self.handle = h
+
+    def forward(self, x, trace=None):
+        from . import _lib
+
+        if trace is not None:
+            raise ValueError("the persistent stack keeps no per-GEMV outputs to trace")
+        st = self.st
+        if x.data_ptr() != self.x_in.data_ptr():
+            self.x_in.copy_(x[:self.x_in.numel()])
+        _lib.call("qgemv_stack_run", self.handle,
+                  torch.cuda.current_stream(st.device).cuda_stream)
+        return st.y_local[(len(st.mats) - 1) % len(st.shapes)]
+
+    def __del__(self):
+        h = getattr(self, "handle", None)
+        if h is not None and h.value:
+            try:
+                self.lib.qgemv_stack_destroy(h)
+            except Exception:
+                pass

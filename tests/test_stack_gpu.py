@@ -100,3 +100,48 @@ def test_fused_stack_one_rank_matches_plain(fmt):
     from qgemv_roofline_b200 import _lib
     assert _lib.lib().qgemv_check_device_error(0, None) == 0
     del g
+
+
+
+@pytest.mark.parametrize("fmt", ["q8_0", "q4_0"])
+def test_persistent_stack_matches_per_launch_stack(fmt):
+    """All GEMVs of a token in one cooperative launch: the same output as the
+    per-launch stack (within the oracle's bound, in practice the same bits),
+    eagerly and over CUDA-graph replays, with the grid-wide counters reset
+    between tokens."""
+    shapes = (("qkv", 1536, 1024), ("o", 1024, 1024), ("gate_up", 2816, 1024), ("down", 1024, 1536))
+    plain = stack.DecodeStack.from_random(fmt, n_layers=3, shapes=shapes, seed=9, device="cuda",
+                                          keep_full=True)
+    pers = stack.DecodeStack.from_random(fmt, n_layers=3, shapes=shapes, seed=9, device="cuda",
+                                         persistent=True)
+    x = torch.randn(1024, device="cuda")
+    trace = []
+    y_plain = plain(x, trace=trace).clone()
+    y_pers = pers(x).clone()
+    torch.cuda.synchronize()
+    m, _, _ = trace[-1]
+    q, d = plain.full[-1]
+    y_ref = o.matvec_ref(fmt, q.cpu().numpy(), d.cpu().numpy(),
+                         trace[-1][1].cpu().numpy()[None, :].astype(np.float32))
+    wn = o.row_norms(fmt, q.cpu().numpy(), d.cpu().numpy())
+    ok, worst = o.check_rowwise(y_pers.cpu().numpy()[None, :].astype(np.float64), y_ref, wn,
+                                trace[-1][1].cpu().numpy()[None, :], 1e-5)
+    assert ok, worst
+    assert torch.allclose(y_pers, y_plain, rtol=1e-6, atol=0)
+    g, out = pers.capture(x)
+    for _ in range(3):
+        out.zero_()
+        g.replay()
+        torch.cuda.synchronize()
+        assert torch.equal(out, y_pers)
+    from qgemv_roofline_b200 import _lib
+    assert _lib.lib().qgemv_check_device_error(0, None) == 0
+    del g
+
+
+def test_persistent_stack_7b_layer_spot_rows():
+    st = stack.DecodeStack.from_random("q8_0", n_layers=2, seed=10, device="cuda",
+                                       persistent=True)
+    plain = stack.DecodeStack.from_random("q8_0", n_layers=2, seed=10, device="cuda")
+    x = torch.randn(4096, device="cuda")
+    assert torch.allclose(st(x), plain(x), rtol=1e-6, atol=0)
