@@ -517,7 +517,7 @@ def main():
     dom = "q8_0" if q8_ms >= q4_ms else "q4_0"
     # the configuration the library dispatches for this slice (csrc/gemv_tma.cu)
     if dom == "q4_0":
-        targs = "4,1,8,8"
+        targs = "4,1,8,16" if rows * (K // 2 + K // 16) >= (150 << 20) else "4,1,8,8"
     else:
         targs = "8,1,4,8" if rows * (K + K // 16) < (256 << 20) else "8,1,4,16"
     kname = f"k_gemv_tma<{targs},{'false' if args.layout == 'soa' else 'true'}>"

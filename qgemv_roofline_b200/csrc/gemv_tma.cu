@@ -39,6 +39,7 @@
 
 #include <algorithm>
 #include <map>
+#include <type_traits>
 #include <mutex>
 #include <vector>
 
@@ -120,6 +121,21 @@ __device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t
           "r"(dst),
       "l"(src), "r"(bytes), "r"(bar)
       : "memory");
+}
+
+// Loads from a 32-bit shared-window address.  volatile keeps them after the
+// mbarrier wait that makes the stage's bytes visible.
+__device__ __forceinline__ uint4 lds_v4(uint32_t a) {
+  uint4 v;
+  asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "r"(a));
+  return v;
+}
+__device__ __forceinline__ unsigned short lds_u16(uint32_t a) {
+  unsigned short v;
+  asm volatile("ld.shared.u16 %0, [%1];" : "=h"(v) : "r"(a));
+  return v;
 }
 
 // Sums v[0..R) across the 32 lanes.  Afterwards lane L holds the total of row
@@ -221,26 +237,42 @@ __device__ __forceinline__ void make_planes_from(const float (&v)[32], XPlanes& 
   if (!o.finite) e = 0;
   o.e = e;
   int X[32];
-  float sum = 0.0f;
   if (e >= -105) {
+    // rint(x * 2^(22-e)) without a float-to-int conversion: |x * 2^(22-e)| < 2^22,
+    // so x * 2^(22-e) + 1.5 * 2^23 lies in [2^23, 2^24), where the spacing of
+    // floats is 1: the FFMA (exact product, one rounding, to nearest even)
+    // rounds to the integer, which is the float's bits - 0x4B400000.
     const float sc = __uint_as_float((uint32_t)(149 - e) << 23);  // 2^(22 - e), exact
 #pragma unroll
-    for (int j = 0; j < 32; ++j) X[j] = o.finite ? __float2int_rn(v[j] * sc) : 0;
+    for (int j = 0; j < 32; ++j)
+      X[j] = (int)(__float_as_uint(fmaf(v[j], sc, 12582912.0f)) - 0x4B400000u);
   } else {
 #pragma unroll
     for (int j = 0; j < 32; ++j) X[j] = __float2int_rn(ldexpf(v[j], 22 - e));
   }
+  int sum = 0;  // exact: |sum| < 32 * 2^22
 #pragma unroll
-  for (int j = 0; j < 32; ++j) sum += (float)X[j];
-  o.bias = 128.0f * sum;
+  for (int j = 0; j < 32; ++j) sum += X[j];
+  o.bias = 128.0f * (float)sum;
+  // bytes 0-2 of four consecutive X as three plane words: a 4 x 4 byte
+  // transpose (the fourth byte is not needed), 7 PRMTs per 4 elements
 #pragma unroll
   for (int w = 0; w < 8; ++w) {
+    const uint32_t a = (uint32_t)X[4 * w], b = (uint32_t)X[4 * w + 1];
+    const uint32_t c = (uint32_t)X[4 * w + 2], d = (uint32_t)X[4 * w + 3];
+    const uint32_t t0 = __byte_perm(a, b, 0x5140);  // a0 b0 a1 b1
+    const uint32_t t1 = __byte_perm(c, d, 0x5140);  // c0 d0 c1 d1
+    const uint32_t t2 = __byte_perm(a, b, 0x0062);  // a2 b2 .. ..
+    const uint32_t t3 = __byte_perm(c, d, 0x0062);  // c2 d2 .. ..
+    o.pl[w][0] = __byte_perm(t0, t1, 0x5410);
+    o.pl[w][1] = __byte_perm(t0, t1, 0x7632);
+    o.pl[w][2] = __byte_perm(t2, t3, 0x5410);
+  }
+  if (!o.finite) {  // non-finite block: no planes, the scale makes its products NaN
 #pragma unroll
-    for (int pl = 0; pl < NPL; ++pl) {
-      const uint32_t sel = (uint32_t)pl | ((uint32_t)(pl + 4) << 4);
-      o.pl[w][pl] = __byte_perm(__byte_perm(X[4 * w], X[4 * w + 1], sel),
-                                __byte_perm(X[4 * w + 2], X[4 * w + 3], sel), 0x5410);
-    }
+    for (int w = 0; w < 8; ++w)
+      for (int pl = 0; pl < NPL; ++pl) o.pl[w][pl] = 0u;
+    o.bias = 0.0f;
   }
 }
 
@@ -250,7 +282,7 @@ __device__ __forceinline__ void make_planes_from(const float (&v)[32], XPlanes& 
 // = elements 4w..4w+3; q4_0: 4 words, word t = elements 4t..4t+3 in the low
 // nibbles and 16+4t.. in the high nibbles).
 template <int FMT>
-__device__ __forceinline__ float block_fold(const uint32_t* wq, const XPlanes& xp) {
+__device__ __forceinline__ void block_sums(const uint32_t* wq, const XPlanes& xp, int& lo, int& hi) {
   int S0 = 0, S1 = 0, S2 = 0;
   if (FMT == 8) {
 #pragma unroll
@@ -277,20 +309,25 @@ __device__ __forceinline__ float block_fold(const uint32_t* wq, const XPlanes& x
     S1 = (int)((L1 << 4) + H1);
     S2 = (S2 << 4) + H2;
   }
-  // fold the two low planes in int32 (< 2^30), then one fp32 combination
-  const int lo = (S1 << 8) + S0;
-  float Fv = fmaf((float)S2, 65536.0f, (float)lo);
-  // q4_0: 16 * sum (n - 8) X = 16 sum n X - 128 sum X; the 1/16 is in the block scale
-  if (FMT == 4) Fv -= xp.bias;
-  return Fv;
+  // the two low planes fold in int32 (< 2^30); plane 2 stays apart
+  lo = (S1 << 8) + S0;
+  hi = S2;
 }
 
 // The block scale 2^t of a lane's x block: t = e - 22 (q4_0: - 4 more), as
 // two exact power-of-two factors (each a normal float for every e), or as one
 // when d * 2^t is exact for every fp16 d; NaN for a non-finite block.
+//
+// Fast form (fast: finite block, -100 <= t <= 80): the block's value is
+// d * fma(hi, 2^(t+16), fma(lo, 2^t, -bias 2^t)), every factor a normal
+// power of two (exact scalings), i.e. the fold and the scale in two FFMAs and
+// one FMUL.  Each of its three roundings is at most 2^-24 times a term below
+// 21 ||w_block|| ||x_block|| (q4_0; 12 for q8_0), so together under
+// 4e-6 ||w|| ||x|| for a row (Cauchy-Schwarz across blocks).
 struct XScale {
   float xs1, xs2, xsc;
-  bool one_factor;
+  float xs16, xnb;  // fast form: 2^(t+16), -bias 2^t
+  bool one_factor, fast;
 };
 template <int FMT>
 __device__ __forceinline__ XScale x_scale(const XPlanes& xp) {
@@ -300,7 +337,23 @@ __device__ __forceinline__ XScale x_scale(const XPlanes& xp) {
   r.xs2 = __int_as_float((127 + t - h) << 23);
   r.one_factor = t >= -100 && t <= 100;
   r.xsc = r.one_factor ? r.xs1 * r.xs2 : 0.0f;
+  r.fast = xp.finite && t >= -100 && t <= 80;
+  r.xs16 = r.fast ? __int_as_float((127 + 16 + t) << 23) : 0.0f;
+  r.xnb = r.fast && FMT == 4 ? -xp.bias * r.xsc : 0.0f;
   return r;
+}
+
+// The value d * 2^t * F of one block from its plane sums (lo = S1 2^8 + S0,
+// hi = S2): the fast form when it holds for every lane of the warp (FAST),
+// else the general one.
+template <int FMT, bool FAST>
+__device__ __forceinline__ float block_value(int lo, int hi, float dv, const XScale& xq,
+                                             const XPlanes& xp) {
+  if (FAST) return dv * fmaf((float)hi, xq.xs16, fmaf((float)lo, xq.xsc, xq.xnb));
+  float Fv = fmaf((float)hi, 65536.0f, (float)lo);
+  // q4_0: 16 * sum (n - 8) X = 16 sum n X - 128 sum X; the 1/16 is in the block scale
+  if (FMT == 4) Fv -= xp.bias;
+  return xq.one_factor ? (dv * xq.xsc) * Fv : ((dv * Fv) * xq.xs1) * xq.xs2;
 }
 
 struct TmaArgs {
@@ -388,15 +441,15 @@ k_gemv_tma(const TmaArgs p) {
     int last_issued[MAX_STAGES];
     for (int s = 0; s < MAX_STAGES; ++s) last_issued[s] = -1;
     bool ok = true;
+    int s = 0;         // stage of tile t (t % S)
+    uint32_t cyc = 0;  // t / S
     for (int t = 0; t < ntiles + S && ok; ++t) {
-      const int s = t % S;
       // the first S tiles (weights only) are prefetched before the dependency
       if (t == S) asm volatile("griddepcontrol.wait;" ::: "memory");
       if (t >= S) {
-        const int tt = t - S;  // tile whose stage is recycled now
+        const int tt = t - S;  // tile whose stage is recycled now (cycle cyc - 1)
         // every lane waits (acquire), since every lane reads the partials
-        ok = __all_sync(0xffffffffu,
-                        mbar_wait(saddr(&empty[s]), (uint32_t)((tt / S) & 1), &abort_flag));
+        ok = __all_sync(0xffffffffu, mbar_wait(saddr(&empty[s]), (cyc - 1u) & 1u, &abort_flag));
         if (!ok) break;
         const int r0 = tt * TR, nr = min(TR, nrows - r0);
         const float* ps = part + (size_t)s * TR * KS;
@@ -423,6 +476,10 @@ k_gemv_tma(const TmaArgs p) {
                      reinterpret_cast<const uint8_t*>(p.d) + (int64_t)(a + r0) * DB, db, bar);
         }
         last_issued[s] = t;
+      }
+      if (++s == S) {
+        s = 0;
+        ++cyc;
       }
     }
     if (!ok && lane == 0) {
@@ -466,9 +523,8 @@ k_gemv_tma(const TmaArgs p) {
 
   float xr[MODE == 0 ? EPC : 1];
   XPlanes xp;
-  float xs1 = 0.0f, xs2 = 0.0f;  // MODE 1: the block's scale 2^t, as two factors
-  float xsc = 0.0f;              // ... or as one, when one_factor
-  bool one_factor = false;
+  XScale xq{};        // MODE 1: the scale 2^t of the lane's x block
+  bool fast = false;  // the fast form holds for every lane of the warp
   if (MODE == 0) {
     asm volatile("griddepcontrol.wait;" ::: "memory");
 #pragma unroll
@@ -483,6 +539,13 @@ k_gemv_tma(const TmaArgs p) {
       }
     }
   } else {
+    // Pull the lane's 128 bytes of x into L2 while the previous kernel
+    // finishes (a prefetch consumes no data, so it may precede the wait; the
+    // previous kernel's own writes to x still land in L2 before the loads).
+    if (cval) {
+      asm volatile("prefetch.global.L2 [%0];" ::"l"(p.x + cidx * 32));
+      asm volatile("prefetch.global.L2 [%0];" ::"l"(p.x + cidx * 32 + 31));
+    }
     asm volatile("griddepcontrol.wait;" ::: "memory");  // x may be the previous kernel's y
     if (p.f.sig_in) {
       // x is assembled by every rank's previous GEMV: one signal per rank per token
@@ -514,18 +577,15 @@ k_gemv_tma(const TmaArgs p) {
     // d: all but extreme x), (d * 2^t) * F is the same correctly rounded
     // product as (d * F) * 2^t; otherwise two exact factors, so the product
     // only rounds where the true value itself under- or overflows.
-    const XScale xq = x_scale<FMT>(xp);
-    xs1 = xq.xs1;
-    xs2 = xq.xs2;
-    one_factor = xq.one_factor;
-    xsc = xq.xsc;
+    xq = x_scale<FMT>(xp);
+    fast = __all_sync(0xffffffffu, !cval || xq.fast);  // lanes past K compute nothing
   }
 
+  int s = 0;         // stage of tile t
+  uint32_t ph = 0u;  // its phase parity
   for (int t = 0; t < ntiles; ++t) {
-    const int s = t % S;
     // every lane waits on the barrier, so the bulk-copied bytes are visible to it
-    if (!__all_sync(0xffffffffu, mbar_wait(saddr(&full[s]), (uint32_t)((t / S) & 1), &abort_flag)))
-      break;
+    if (!__all_sync(0xffffffffu, mbar_wait(saddr(&full[s]), ph, &abort_flag))) break;
     const int nr = min(TR, nrows - t * TR);
     const uint8_t* st = sm + (size_t)s * STG;
     const uint8_t* sd = st + (size_t)TR * QB;
@@ -538,14 +598,12 @@ k_gemv_tma(const TmaArgs p) {
         // Rows r0 + r >= nr of a partial last tile read stale (in-bounds)
         // bytes of the stage; their results are never stored, and rows never
         // mix in the reduction below, so no clamping is needed.
-        float dv[R];
-        if (!AOS) {
-          const uint8_t* dbase = sd + (size_t)r0 * DB + (MODE == 0 && FMT == 8 ? (cidx >> 1) : cidx) * 2;
+        if (MODE == 0) {
+          float dv[R];
+          const uint8_t* dbase = sd + (size_t)r0 * DB + (FMT == 8 ? (cidx >> 1) : cidx) * 2;
 #pragma unroll
           for (int r = 0; r < R; ++r)
             dv[r] = half_bits_to_float(*reinterpret_cast<const unsigned short*>(dbase + (size_t)r * DB));
-        }
-        if (MODE == 0) {
           uint4 wv[R];
 #pragma unroll
           for (int r = 0; r < R; ++r)
@@ -580,43 +638,54 @@ k_gemv_tma(const TmaArgs p) {
 #pragma unroll
           for (int r = 0; r < R; ++r) acc[r] = dv[r] * (s2[r].x + s2[r].y);
         } else {
+          // one of two bodies for the whole pass: the fast scale form when it
+          // holds for every lane's block (a warp-uniform branch), else the general one
+          // SoA: the lane's quants and scale of row r0 + r, as 32-bit shared
+          // addresses stepped by the row strides (one add per row each)
+          const uint32_t qa0 =
+              saddr(sm) + (uint32_t)(s * STG + r0 * QB + cidx * (FMT == 8 ? 32 : 16));
+          const uint32_t da0 = saddr(sm) + (uint32_t)(s * STG + TR * QB + r0 * DB + cidx * 2);
+          auto rows = [&](auto fast_c) {
+            constexpr bool FAST = decltype(fast_c)::value;
+            uint32_t qa = qa0, da = da0;
 #pragma unroll
           for (int r = 0; r < R; ++r) {
-            const uint8_t* rowp = st + (size_t)(r0 + r) * QB;
-            // AoS: the lane's block starts at byte cidx * (34|18) of the row
-            // (2-byte aligned; rows start on 16-byte boundaries); read the
-            // aligned words covering it and realign the quants with PRMT.
             constexpr int QW = FMT == 8 ? 8 : 4;  // quant words per block
-            uint32_t aw[QW];
+            uint32_t wq[QW];
+            float dvr;
             if (AOS) {
-              const uint32_t* src = reinterpret_cast<const uint32_t*>(rowp + aos_off);
+              // the lane's block starts at byte cidx * (34|18) of the row
+              // (2-byte aligned; rows start on 16-byte boundaries); read the
+              // aligned words covering it and realign the quants with PRMT.
+              const uint32_t* src =
+                  reinterpret_cast<const uint32_t*>(st + (size_t)(r0 + r) * QB + aos_off);
               uint32_t wd[QW + 1];
 #pragma unroll
               for (int i = 0; i <= QW; ++i) wd[i] = src[i];
-              dv[r] = half_bits_to_float((unsigned short)(aos_odd ? (wd[0] >> 16) : (wd[0] & 0xFFFFu)));
+              dvr = half_bits_to_float((unsigned short)(aos_odd ? (wd[0] >> 16) : (wd[0] & 0xFFFFu)));
 #pragma unroll
-              for (int i = 0; i < QW; ++i) aw[i] = __byte_perm(wd[i], wd[i + 1], aos_sel);
-            }
-            uint32_t wq[FMT == 8 ? 8 : 4];
-            if (AOS) {
-#pragma unroll
-              for (int w = 0; w < (FMT == 8 ? 8 : 4); ++w) wq[w] = aw[w % QW];
-            } else if (FMT == 8) {
-              // 32 signed quants: words w = 0..7 hold elements 4w..4w+3
-              const uint4 u0 = *reinterpret_cast<const uint4*>(rowp + cidx * 32);
-              const uint4 u1 = *reinterpret_cast<const uint4*>(rowp + cidx * 32 + 16);
-              wq[0] = u0.x; wq[1] = u0.y; wq[2] = u0.z; wq[3] = u0.w;
-              wq[4 % (FMT == 8 ? 8 : 4)] = u1.x; wq[5 % (FMT == 8 ? 8 : 4)] = u1.y;
-              wq[6 % (FMT == 8 ? 8 : 4)] = u1.z; wq[7 % (FMT == 8 ? 8 : 4)] = u1.w;
+              for (int i = 0; i < QW; ++i) wq[i] = __byte_perm(wd[i], wd[i + 1], aos_sel);
             } else {
-              // 16 bytes: word t holds elements 4t..4t+3 (low nibbles) and
+              dvr = half_bits_to_float(lds_u16(da));
+              da += DB;
+              // q8_0: 32 signed quants, word w = elements 4w..4w+3.  q4_0: 16
+              // bytes, word t = elements 4t..4t+3 (low nibbles) and
               // 16+4t..16+4t+3 (high nibbles, taken in place as 16 * n)
-              const uint4 u = *reinterpret_cast<const uint4*>(rowp + cidx * 16);
-              wq[0] = u.x; wq[1] = u.y; wq[2] = u.z; wq[3] = u.w;
+              const uint4 u0 = lds_v4(qa);
+              wq[0] = u0.x; wq[1] = u0.y; wq[2] = u0.z; wq[3] = u0.w;
+              if (FMT == 8) {
+                const uint4 u1 = lds_v4(qa + 16);
+                wq[4 % QW] = u1.x; wq[5 % QW] = u1.y; wq[6 % QW] = u1.z; wq[7 % QW] = u1.w;
+              }
+              qa += QB;
             }
-            const float Fv = block_fold<FMT>(wq, xp);
-            acc[r] = one_factor ? (dv[r] * xsc) * Fv : ((dv[r] * Fv) * xs1) * xs2;
+            int lo, hi;
+            block_sums<FMT>(wq, xp, lo, hi);
+            acc[r] = block_value<FMT, FAST>(lo, hi, dvr, xq, xp);
           }
+          };
+          if (fast) rows(std::true_type{});
+          else rows(std::false_type{});
         }
       }
       const float v = reduce_rows<R>(acc, lane);
@@ -626,6 +695,10 @@ k_gemv_tma(const TmaArgs p) {
     __syncwarp();
     if (lane == 0)
       asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(saddr(&empty[s])) : "memory");
+    if (++s == S) {
+      s = 0;
+      ph ^= 1u;
+    }
   }
 }
 
@@ -839,6 +912,7 @@ __global__ void __launch_bounds__(tma_threads(16), 1) k_gemv_stack(const __grid_
       xp.finite = true;
     }
     const XScale xq = x_scale<FMT>(xp);
+    const bool fast = __all_sync(0xffffffffu, !cval || xq.fast);  // as in k_gemv_tma
     bool ok = true;
     for (int t = 0; t < ntiles; ++t, ++u) {
       const int s = (int)(u % (uint32_t)S);
@@ -873,8 +947,10 @@ __global__ void __launch_bounds__(tma_threads(16), 1) k_gemv_stack(const __grid_
               const uint4 uq = *reinterpret_cast<const uint4*>(rowp + cidx * 16);
               wq[0] = uq.x; wq[1] = uq.y; wq[2] = uq.z; wq[3] = uq.w;
             }
-            const float Fv = block_fold<FMT>(wq, xp);
-            acc[r] = xq.one_factor ? (dv * xq.xsc) * Fv : ((dv * Fv) * xq.xs1) * xq.xs2;
+            int lo, hi;
+            block_sums<FMT>(wq, xp, lo, hi);
+            acc[r] = fast ? block_value<FMT, true>(lo, hi, dv, xq, xp)
+                          : block_value<FMT, false>(lo, hi, dv, xq, xp);
           }
         }
         const float v = reduce_rows<R>(acc, lane);
@@ -992,18 +1068,21 @@ int gemv_soa_tma(int fmt, const GemvCall& c, cudaStream_t st) {
   DeviceInfo dev;
   if (int rc = current_device_info(dev)) return rc;
   // Two CTAs of 8 consumer warps per SM overlap one CTA's drain with the
-  // next CTA's fill; measured faster for q4_0 at every size and for q8_0 up
-  // to ~200 MB of weights.  Beyond that q8_0 streams best with one CTA of 16.
-  // q4_0 is issue-bound: 8 rows per pass amortize the per-pass reduction
-  // (falls back to 4 rows, then to one CTA of 16, when the tile does not fit).
+  // next CTA's fill (less idle time per call); one CTA of 16 streams faster
+  // once the call is long enough for that to dominate: measured crossovers
+  // near 150 MB of q4_0 (64k rows of K = 4096) and 256 MB of q8_0.  q4_0 is
+  // issue-bound: 8 rows per pass amortize the per-pass reduction (falls back
+  // to 4 rows, then to one CTA of 16, when the tile does not fit).
   int rc = -1;
+  const int64_t wbytes = c.M * (c.K / (fmt == 8 ? 1 : 2) + c.K / 16);
   if (fmt == 4) {
-    rc = launch_tma<4, 1, 8, 8>(c, dev, st);
+    if (wbytes >= ((int64_t)150 << 20)) rc = launch_tma<4, 1, 8, 16>(c, dev, st);
+    if (rc == -1) rc = launch_tma<4, 1, 8, 8>(c, dev, st);
     if (rc == -1) rc = launch_tma<4, 1, 4, 8>(c, dev, st);
     if (rc == -1) rc = launch_tma<4, 1, 4, 16>(c, dev, st);
     return rc;
   }
-  if (c.M * (c.K + c.K / 16) < ((int64_t)256 << 20)) rc = launch_tma<8, 1, 4, 8>(c, dev, st);
+  if (wbytes < ((int64_t)256 << 20)) rc = launch_tma<8, 1, 4, 8>(c, dev, st);
   if (rc == -1) rc = launch_tma<8, 1, 4, 16>(c, dev, st);
   return rc;
 }
