@@ -53,6 +53,8 @@ namespace {
 // (each with half the shared-memory ring), which lets the next launch's CTA
 // start streaming on an SM while this launch's CTA there drains.
 constexpr int tma_threads(int cw) { return 32 * (cw + 1); }
+// CTAs of `cw` consumer warps per SM: 16 consumer warps per SM in all
+constexpr int tma_ctas_per_sm(int cw) { return cw >= 16 ? 1 : 16 / cw; }
 constexpr int MAX_STAGES = 8;
 constexpr long long SPIN_LIMIT = 2000000000LL;  // clock64 cycles, ~1 s
 
@@ -397,7 +399,7 @@ __device__ __forceinline__ bool wait_count(const unsigned* c, unsigned target,
 // of rows is then one contiguous range and each lane realigns its block from
 // shared memory (MODE 1 only).
 template <int FMT, int MODE, int R, int CONSUMERS, bool AOS = false>
-__global__ void __launch_bounds__(tma_threads(CONSUMERS), 16 / CONSUMERS)
+__global__ void __launch_bounds__(tma_threads(CONSUMERS), tma_ctas_per_sm(CONSUMERS))
 k_gemv_tma(const TmaArgs p) {
   using F = Fmt<FMT>;
   constexpr int EPC = F::ELEMS_PER_CHUNK;
@@ -1001,7 +1003,7 @@ int plan_tma(const void* kern, int M, int K, const DeviceInfo& dev, TmaPlan* out
   const int RG = CONSUMERS / KS;
   const int row_bytes = AOS ? (K / QK) * F::BLOCK_BYTES : K / F::ROW_DIV + K / 16;
   const int unit = RG * R;
-  const int ctas_per_sm = 16 / CONSUMERS;
+  const int ctas_per_sm = tma_ctas_per_sm(CONSUMERS);
   if (int rc = allow_max_smem(kern, dev)) return rc;
   cudaFuncAttributes fa;
   if (cudaFuncGetAttributes(&fa, kern) != cudaSuccess) return check_launch("cudaFuncGetAttributes");
