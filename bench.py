@@ -528,6 +528,22 @@ def main():
                 "note": f"peak {peak_note}; achieved = algorithmic bytes per launch "
                         f"({alg_bytes(dom, rows, K)}) / mean launch time (CUDA events)"}
 
+    # ------------------------------------- opt-in q8_1 activations (not the metric)
+    # x rounded to int8 per 32-element block inside the kernel (ggml's q8_1
+    # route): reported beside the exact path, never as its value.
+    calls81 = [dict(c, activations="q8_1") for c in calls]
+    n81 = min(args.steps, 2000)
+    _, per81 = time_steps(calls81, min(args.warmup, 20), n81, grouped=True)
+    q8_81, q4_81 = max_over_ranks(per81)
+    extras["opt_in_q8_1"] = {
+        f: {"us_per_call": ms / n81 * 1e3,
+            "gbps_per_gpu": alg_bytes(f, rows, K) / (ms / n81 * 1e-3) / 1e9,
+            "frac_of_peak": alg_bytes(f, rows, K) / (ms / n81 * 1e-3) / 1e9 / peak}
+        for f, ms in (("q8_0", q8_81), ("q4_0", q4_81))}
+    extras["opt_in_q8_1"]["numerics"] = ("x rounded to int8 per 32-element block (q8_1); "
+                                         "outside the exact path's 1e-5 bound; "
+                                         f"{n81} calls per format, after the timed region")
+
     # ---------------------------------------------------------- NCCL all-gather
     if world > 1:
         yfull = torch.empty(rows * world, device=dev)

@@ -109,6 +109,22 @@ QGEMV_API int qgemv_q4_0_soa(const void* q, const void* d, const float* x, float
  * ordered (one stream, or events between them).  The reference had no
  * batched kernel. */
 
+/* Opt-in q8_1 activations (one column): x is quantized to int8 per 32-element
+ * block inside the kernel (amax = max|x|, q = rint(x * (127 / amax)), scale
+ * amax / 127, all fp32), the activation format of ggml's q8_1 route that the
+ * reference's README names as the production alternative (README.md:208-210,
+ * 286-292; no kernel for it in the reference).  Each 32-weight block is then
+ * one dp4a set instead of three.  This CHANGES THE NUMERICS: y carries the
+ * rounding of x to 8 bits per block (up to amax / 254 per element), which the
+ * 1e-5 bound of the exact entry points does not cover.  Shapes: K % 256 == 0,
+ * 256 <= K <= 16384, x 16-byte aligned (else QGEMV_ERR_UNSUPPORTED).
+ * qgemv_soa_q8_1 takes SoA planes (q, d as qgemv_q8_0_soa / qgemv_q4_0_soa),
+ * qgemv_aos_q8_1 ggml blocks (as qgemv_q8_0_aos / qgemv_q4_0_aos). */
+QGEMV_API int qgemv_soa_q8_1(int format, const void* q, const void* d, const float* x, float* y,
+                             int64_t M, int64_t K, void* stream);
+QGEMV_API int qgemv_aos_q8_1(int format, const void* blocks, const float* x, float* y,
+                             int64_t M, int64_t K, void* stream);
+
 /* Workspace bytes of a batched SoA call (0 when the call needs none). */
 QGEMV_API size_t qgemv_soa_workspace_bytes(int format, int64_t M, int64_t K, int32_t ncols);
 
@@ -298,7 +314,9 @@ QGEMV_API int qgemv_roof_d2d(void* dst, const void* src, size_t bytes, void* str
  * (copy i % ncopies is used in step i, so the working set can exceed L2). */
 typedef struct qgemv_call_desc {
   int32_t format;        /* QGEMV_Q8_0 or QGEMV_Q4_0                     */
-  int32_t layout;        /* 0 = SoA planes (q, d), 1 = AoS blocks (q)    */
+  int32_t layout;        /* 0 = SoA planes (q, d), 1 = AoS blocks (q);
+                            2 / 3 = the same with q8_1 activations
+                            (qgemv_soa_q8_1 / qgemv_aos_q8_1, ncols 1)   */
   int32_t ncopies;       /* entries in q (and d)                         */
   int32_t ncols;         /* activation vectors                           */
   int64_t M, K, ldx, ldy;

@@ -23,6 +23,14 @@ It restates, in numpy, the reference's algorithm for the path:
   bound ``|y - y_ref| <= 1e-5 * ||w_row||_2 * ||x||_2`` and the reference's
   own gate ``max|y - y_ref| / max|y_ref| <= 1e-5``
   (tests/test_correctness.py:21, src/bench.cu:229-240).
+* ``quantize_x_q8_1`` / ``matvec_q8_1_ref`` restate the opt-in q8_1 activation
+  path, which the reference names but does not implement (README.md:208-210,
+  286-292: ggml's q8_1 route): x is rounded to int8 per 32-element block
+  (``amax = max|x|``, ``id = fp32(127 / amax)``, ``dx = fp32(amax / 127)``,
+  ``q = rint(fp32(x * id))``), then ``y = sum_b dw * dx * sum_j w_j q_j`` with
+  exact integer block dots and a float64 combination.  Parity of that path
+  is against this restatement (unpinned: no golden vectors exist for it);
+  its distance to ``matvec_ref`` is the rounding of x, not a kernel error.
 * ``to_aos`` / ``from_aos`` restate the ggml block byte layout
   (src/qgemv_kernels.cuh:21-26: little-endian fp16 ``d`` then the quants) and
   the AoS<->SoA repack of src/bench.cu:300-314.
@@ -134,6 +142,53 @@ def matvec_ref(fmt: str, q: np.ndarray, d: np.ndarray, X: np.ndarray) -> np.ndar
     if X64.ndim == 1:
         return Wd @ X64
     return X64 @ Wd.T
+
+
+def quantize_x_q8_1(X: np.ndarray):
+    """Activations -> (int8 quants as int32 [..., K], fp32 scales [..., K/32]).
+
+    Per 32-element block: ``amax = max|x|``; ``id = fp32(127 / amax)`` and
+    ``dx = fp32(amax / 127)`` (correctly rounded fp32 divisions; an all-zero
+    block gives ``id = dx = 0``); ``q = rint(fp32(x * id))`` (round half to
+    even), so ``|q| <= 127``.
+    """
+    X = np.asarray(X, dtype=np.float32)
+    K = X.shape[-1]
+    B = X.reshape(X.shape[:-1] + (K // QK, QK))
+    amax = np.abs(B).max(axis=-1)
+    with np.errstate(divide="ignore", invalid="ignore"):
+        idv = np.where(amax > 0, np.float32(127.0) / amax, np.float32(0.0)).astype(np.float32)
+        dx = (amax / np.float32(127.0)).astype(np.float32)
+        prod = (B * idv[..., None]).astype(np.float32)
+    q = np.rint(np.where(np.isfinite(prod), prod, 0.0)).astype(np.int32)
+    return q.reshape(X.shape), dx
+
+
+def matvec_q8_1_ref(fmt: str, q: np.ndarray, d: np.ndarray, X: np.ndarray) -> np.ndarray:
+    """The opt-in q8_1 path: ``y[r] = sum_b dw[r,b] * dx[b] * sum_j w[r,b,j] * xq[b,j]``.
+
+    The integer block dots are exact (int64) and the combination float64; the
+    result is ``[M]`` or ``[N, M]`` like ``matvec_ref``.
+    """
+    if fmt == "q8_0":
+        M, K = q.shape
+        W = q.astype(np.int64)
+    elif fmt == "q4_0":
+        M, K = q.shape[0], q.shape[1] * 2
+        W = q4_nibbles(q).astype(np.int64) - 8
+    else:
+        raise ValueError(fmt)
+    nb = K // QK
+    Wb = W.reshape(M, nb, QK)
+    d64 = d.astype(np.float64)
+    X2 = np.atleast_2d(np.asarray(X, dtype=np.float32))
+    xq, dx = quantize_x_q8_1(X2)
+    out = np.empty((X2.shape[0], M), dtype=np.float64)
+    for n in range(X2.shape[0]):
+        S = np.einsum("mbj,bj->mb", Wb, xq[n].reshape(nb, QK).astype(np.int64))
+        with np.errstate(invalid="ignore"):
+            out[n] = (S.astype(np.float64) * d64 * dx[n].astype(np.float64)[None, :]).sum(axis=1)
+    return out[0] if np.asarray(X).ndim == 1 else out
 
 
 def row_norms(fmt: str, q: np.ndarray, d: np.ndarray) -> np.ndarray:

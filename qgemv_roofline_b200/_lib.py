@@ -102,6 +102,8 @@ SIGNATURES = {
     "qgemv_soa_ws": ([ctypes.c_int, _vp, _vp, _vp, _vp, _i64, _i64, _i32, _i64, _i64, _vp,
                       ctypes.c_size_t, _vp], ctypes.c_int),
     "qgemv_release_workspaces": ([], ctypes.c_int),
+    "qgemv_soa_q8_1": ([ctypes.c_int, _vp, _vp, _vp, _vp, _i64, _i64, _vp], ctypes.c_int),
+    "qgemv_aos_q8_1": ([ctypes.c_int, _vp, _vp, _vp, _i64, _i64, _vp], ctypes.c_int),
     "qgemv_soa_fused": ([ctypes.c_int, _vp, _vp, _vp, _vp, _i64, _i64, _vp, _vp], ctypes.c_int),
     "qgemv_token_fence": ([_vp, _i32, _vp, _vp, _vp], ctypes.c_int),
     "qgemv_stack_create": ([ctypes.c_int, _vp, _i32, ctypes.POINTER(ctypes.c_void_p)],

@@ -417,6 +417,51 @@ QGEMV_API int qgemv_soa_fused(int format, const void* q, const void* d, const fl
   return gemv_soa_tma(format, c, static_cast<cudaStream_t>(stream));
 }
 
+namespace {
+// Single-column GEMV with q8_1 activations (SoA planes or GGUF blocks).
+int q81_entry(int format, bool aos, const void* q, const void* d, const float* x, float* y,
+              int64_t M, int64_t K, void* stream) {
+  if (int rc = check_fmt(format)) return rc;
+  if (int rc = check_mk(M, K)) return rc;
+  if (M == 0) return OK;
+  if (!x || !y || !q || (!aos && !d))
+    return set_error(ERR_NULL, aos ? "blocks, x and y must not be NULL"
+                                   : "q, d, x and y must not be NULL");
+  if (misaligned(q, 16) || (!aos && misaligned(d, 2)) || misaligned(y, 4))
+    return set_error(ERR_ALIGN, aos ? "blocks must be 16-byte and y 4-byte aligned"
+                                    : "q must be 16-byte, d 2-byte and y 4-byte aligned");
+  GemvCall c;
+  c.q = q;
+  c.d = d;
+  c.x = x;
+  c.y = y;
+  c.M = M;
+  c.K = K;
+  c.N = 1;
+  c.ldx = K;
+  c.ldy = M;
+  c.act = 1;
+  if (!tma_eligible(c))
+    return set_error(ERR_UNSUPPORTED,
+                     "q8_1 activations run on the TMA kernel only: K %% 256 == 0, "
+                     "256 <= K <= 16384, x 16-byte aligned");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int rc = aos ? gemv_aos_tma(format, c, st) : gemv_soa_tma(format, c, st);
+  return rc == -1 ? set_error(ERR_UNSUPPORTED, "no q8_1 kernel configuration fits this shape")
+                  : rc;
+}
+}  // namespace
+
+QGEMV_API int qgemv_soa_q8_1(int format, const void* q, const void* d, const float* x, float* y,
+                             int64_t M, int64_t K, void* stream) {
+  return q81_entry(format, false, q, d, x, y, M, K, stream);
+}
+
+QGEMV_API int qgemv_aos_q8_1(int format, const void* blocks, const float* x, float* y,
+                             int64_t M, int64_t K, void* stream) {
+  return q81_entry(format, true, blocks, nullptr, x, y, M, K, stream);
+}
+
 QGEMV_API int qgemv_stack_create(int format, const qgemv_stack_gemv* gemvs, int32_t n,
                                  void** handle) {
   if (int rc = check_fmt(format)) return rc;

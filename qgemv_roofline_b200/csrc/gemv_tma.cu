@@ -345,6 +345,74 @@ __device__ __forceinline__ XScale x_scale(const XPlanes& xp) {
   return r;
 }
 
+// --- q8_1 activations (opt-in) ---------------------------------------------
+// x quantized to int8 per 32-element block, the activation format of ggml's
+// q8_1 route: amax = max |x|, id = 127 / amax and dx = amax / 127 (fp32,
+// correctly rounded), q_j = rint(fp32(x_j * id)) in [-127, 127].  The block's
+// dot with the weights is then one exact int32 dp4a sum times dw * dx; the
+// error against the exact dot is that of rounding x to 8 bits per block (up
+// to amax / 254 per element), far outside the exact mode's 1e-5 bound.
+struct XQ81 {
+  uint32_t q[8];  // word w = elements 4w..4w+3 (signed bytes)
+  float dx;       // the block scale amax / 127 (0 for an all-zero block, NaN if not finite)
+  float dx16;     // dx / 16 (q4_0: the in-place high nibbles count 16 n)
+  int bias;       // 128 * sum_j q_j (q4_0: the -8 offset, in the 16 n units)
+};
+
+__device__ __forceinline__ void make_q81(const float* __restrict__ xb, XQ81& o) {
+  float v[32];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const float4 f = *reinterpret_cast<const float4*>(xb + 4 * i);
+    v[4 * i] = f.x; v[4 * i + 1] = f.y; v[4 * i + 2] = f.z; v[4 * i + 3] = f.w;
+  }
+  uint32_t amax_bits = 0u;
+#pragma unroll
+  for (int j = 0; j < 32; ++j) amax_bits = max(amax_bits, __float_as_uint(v[j]) & 0x7FFFFFFFu);
+  const bool finite = amax_bits < 0x7F800000u;
+  const float amax = __uint_as_float(amax_bits);
+  const bool live = finite && amax_bits != 0u;
+  const float id = live ? __fdiv_rn(127.0f, amax) : 0.0f;
+  o.dx = finite ? __fdiv_rn(amax, 127.0f) : __int_as_float(0x7FC00000);
+  o.dx16 = o.dx * 0.0625f;
+  int q[32], sum = 0;
+#pragma unroll
+  for (int j = 0; j < 32; ++j) {
+    // |x_j * id| <= 127 (+ rounding): adding 1.5 * 2^23 rounds the product to
+    // the nearest integer (ties to even), which is the float's bits - 0x4B400000
+    const float t = __fadd_rn(__fmul_rn(v[j], id), 12582912.0f);
+    q[j] = live ? (int)(__float_as_uint(t) - 0x4B400000u) : 0;
+    sum += q[j];
+  }
+  o.bias = 128 * sum;
+#pragma unroll
+  for (int w = 0; w < 8; ++w)
+    o.q[w] = __byte_perm(__byte_perm((uint32_t)q[4 * w], (uint32_t)q[4 * w + 1], 0x0040),
+                         __byte_perm((uint32_t)q[4 * w + 2], (uint32_t)q[4 * w + 3], 0x0040),
+                         0x5410);
+}
+
+// One block of weights (wq as in block_sums) against q8_1 activations:
+// q8_0: dw * dx * sum w q; q4_0: dw * (dx / 16) * (16 sum n q - 128 sum q).
+// The integer sum is exact (|.| < 2^20) and so is its conversion.
+template <int FMT>
+__device__ __forceinline__ float block_q81(const uint32_t* wq, const XQ81& x8, float dw) {
+  int S = 0;
+  if (FMT == 8) {
+#pragma unroll
+    for (int w = 0; w < 8; ++w) S = dp4a_ss(wq[w], x8.q[w], S);
+    return (float)S * (dw * x8.dx);
+  }
+  int L = 0, H = 0;
+#pragma unroll
+  for (int t4 = 0; t4 < 4; ++t4) {
+    L = dp4a_us(wq[t4] & 0x0F0F0F0Fu, x8.q[t4], L);
+    H = dp4a_us(wq[t4] & 0xF0F0F0F0u, x8.q[t4 + 4], H);
+  }
+  S = (L << 4) + H - x8.bias;
+  return (float)S * (dw * x8.dx16);
+}
+
 // The value d * 2^t * F of one block from its plane sums (lo = S1 2^8 + S0,
 // hi = S2): the fast form when it holds for every lane of the warp (FAST),
 // else the general one.
@@ -393,8 +461,10 @@ __device__ __forceinline__ bool wait_count(const unsigned* c, unsigned target,
 
 // MODE 0: quants converted to fp32 with the magic-number trick and FFMA2
 //         accumulation (x as fp32).
-// MODE 1: x in block fixed point (four byte planes) and exact dp4a integer
+// MODE 1: x in block fixed point (three byte planes) and exact dp4a integer
 //         dot products per 32-weight block, fp32 across blocks.
+// MODE 2: x quantized to int8 per block (q8_1 activations, opt-in; changes
+//         the numerics) and one dp4a set per block.
 // AOS: the weights are ggml blocks [M][K/32] (34 / 18 bytes, d first); a tile
 // of rows is then one contiguous range and each lane realigns its block from
 // shared memory (MODE 1 only).
@@ -527,6 +597,7 @@ k_gemv_tma(const TmaArgs p) {
   XPlanes xp;
   XScale xq{};        // MODE 1: the scale 2^t of the lane's x block
   bool fast = false;  // the fast form holds for every lane of the warp
+  XQ81 x8{};          // MODE 2: the lane's x block as int8 quants
   if (MODE == 0) {
     asm volatile("griddepcontrol.wait;" ::: "memory");
 #pragma unroll
@@ -565,7 +636,9 @@ k_gemv_tma(const TmaArgs p) {
         if (r || abort_flag || clock64() - t0 > 2 * SPIN_LIMIT) break;
       }
     }
-    if (cval) {
+    if (MODE == 2) {
+      if (cval) make_q81(p.x + cidx * 32, x8);  // lanes past K: zero quants, never stored
+    } else if (cval) {
       make_planes(p.x + cidx * 32, xp);
     } else {
       for (int w = 0; w < 8; ++w)
@@ -579,8 +652,10 @@ k_gemv_tma(const TmaArgs p) {
     // d: all but extreme x), (d * 2^t) * F is the same correctly rounded
     // product as (d * F) * 2^t; otherwise two exact factors, so the product
     // only rounds where the true value itself under- or overflows.
-    xq = x_scale<FMT>(xp);
-    fast = __all_sync(0xffffffffu, !cval || xq.fast);  // lanes past K compute nothing
+    if (MODE == 1) {
+      xq = x_scale<FMT>(xp);
+      fast = __all_sync(0xffffffffu, !cval || xq.fast);  // lanes past K compute nothing
+    }
   }
 
   int s = 0;         // stage of tile t
@@ -681,13 +756,17 @@ k_gemv_tma(const TmaArgs p) {
               }
               qa += QB;
             }
-            int lo, hi;
-            block_sums<FMT>(wq, xp, lo, hi);
-            acc[r] = block_value<FMT, FAST>(lo, hi, dvr, xq, xp);
+            if (MODE == 2) {
+              acc[r] = block_q81<FMT>(wq, x8, dvr);
+            } else {
+              int lo, hi;
+              block_sums<FMT>(wq, xp, lo, hi);
+              acc[r] = block_value<FMT, FAST>(lo, hi, dvr, xq, xp);
+            }
           }
           };
-          if (fast) rows(std::true_type{});
-          else rows(std::false_type{});
+          if (MODE == 2 || !fast) rows(std::false_type{});
+          else rows(std::true_type{});
         }
       }
       const float v = reduce_rows<R>(acc, lane);
@@ -1077,6 +1156,17 @@ int gemv_soa_tma(int fmt, const GemvCall& c, cudaStream_t st) {
   // to 4 rows, then to one CTA of 16, when the tile does not fit).
   int rc = -1;
   const int64_t wbytes = c.M * (c.K / (fmt == 8 ? 1 : 2) + c.K / 16);
+  if (c.act == 1) {  // q8_1 activations: one dp4a set per block, the same shapes
+    if (fmt == 4) {
+      if (wbytes >= ((int64_t)150 << 20)) rc = launch_tma<4, 2, 8, 16>(c, dev, st);
+      if (rc == -1) rc = launch_tma<4, 2, 8, 8>(c, dev, st);
+      if (rc == -1) rc = launch_tma<4, 2, 4, 16>(c, dev, st);
+      return rc;
+    }
+    if (wbytes < ((int64_t)256 << 20)) rc = launch_tma<8, 2, 4, 8>(c, dev, st);
+    if (rc == -1) rc = launch_tma<8, 2, 4, 16>(c, dev, st);
+    return rc;
+  }
   if (fmt == 4) {
     if (wbytes >= ((int64_t)150 << 20)) rc = launch_tma<4, 1, 8, 16>(c, dev, st);
     if (rc == -1) rc = launch_tma<4, 1, 8, 8>(c, dev, st);
@@ -1095,6 +1185,16 @@ int gemv_aos_tma(int fmt, const GemvCall& c, cudaStream_t st) {
   DeviceInfo dev;
   if (int rc = current_device_info(dev)) return rc;
   int rc = -1;
+  if (c.act == 1) {  // q8_1 activations
+    if (fmt == 4) {
+      rc = launch_tma<4, 2, 8, 8, true>(c, dev, st);
+      if (rc == -1) rc = launch_tma<4, 2, 4, 16, true>(c, dev, st);
+      return rc;
+    }
+    if (c.M * (c.K + c.K / 16) < ((int64_t)256 << 20)) rc = launch_tma<8, 2, 4, 8, true>(c, dev, st);
+    if (rc == -1) rc = launch_tma<8, 2, 4, 16, true>(c, dev, st);
+    return rc;
+  }
   if (fmt == 4) {
     rc = launch_tma<4, 1, 8, 8, true>(c, dev, st);
     if (rc == -1) rc = launch_tma<4, 1, 4, 8, true>(c, dev, st);

@@ -22,10 +22,13 @@
 namespace qg {
 namespace {
 
+// layout: 0 SoA, 1 AoS, 2 SoA with q8_1 activations, 3 AoS with q8_1 activations
+bool soa_layout(int layout) { return layout == 0 || layout == 2; }
+
 int issue(const qgemv_call_desc& c, int copy, cudaStream_t st) {
   GemvCall g;
   g.q = c.q[copy];
-  g.d = c.layout == 0 ? c.d[copy] : nullptr;
+  g.d = soa_layout(c.layout) ? c.d[copy] : nullptr;
   g.x = c.x;
   g.y = c.y;
   g.M = c.M;
@@ -33,6 +36,11 @@ int issue(const qgemv_call_desc& c, int copy, cudaStream_t st) {
   g.N = c.ncols;
   g.ldx = c.ncols > 1 ? c.ldx : c.K;
   g.ldy = c.ncols > 1 ? c.ldy : c.M;
+  if (c.layout >= 2) {  // q8_1 activations: the TMA kernel only
+    g.act = 1;
+    const int rc = c.layout == 2 ? gemv_soa_tma(c.format, g, st) : gemv_aos_tma(c.format, g, st);
+    return rc == -1 ? set_error(ERR_UNSUPPORTED, "q8_1 activations: shape not supported") : rc;
+  }
   return c.layout == 0 ? gemv_soa(c.format, g, st) : gemv_aos(c.format, g, st);
 }
 
@@ -59,8 +67,10 @@ extern "C" QGEMV_API int qgemv_time_steps(const qgemv_call_desc* calls, int32_t 
   for (int j = 0; j < ncalls; ++j) {
     const qgemv_call_desc& c = calls[j];
     if (c.format != 8 && c.format != 4) return set_error(ERR_ARG, "call %d: bad format", j);
-    if (c.layout != 0 && c.layout != 1) return set_error(ERR_ARG, "call %d: bad layout", j);
-    if (c.ncopies < 1 || !c.q || (c.layout == 0 && !c.d))
+    if (c.layout < 0 || c.layout > 3) return set_error(ERR_ARG, "call %d: bad layout", j);
+    if (c.layout >= 2 && c.ncols != 1)
+      return set_error(ERR_ARG, "call %d: q8_1 activations take one column", j);
+    if (c.ncopies < 1 || !c.q || (soa_layout(c.layout) && !c.d))
       return set_error(ERR_NULL, "call %d: needs ncopies >= 1 weight pointers", j);
     if (c.M < 1 || c.K < QK || c.K % QK || c.M >= (1LL << 31) || c.K >= (1LL << 31))
       return set_error(ERR_SHAPE, "call %d: bad shape", j);
@@ -70,7 +80,7 @@ extern "C" QGEMV_API int qgemv_time_steps(const qgemv_call_desc* calls, int32_t 
     for (int k = 0; k < c.ncopies; ++k) {
       if (!c.q[k] || (reinterpret_cast<uintptr_t>(c.q[k]) & 15))
         return set_error(ERR_ALIGN, "call %d copy %d: weights must be 16-byte aligned", j, k);
-      if (c.layout == 0 && (!c.d[k] || (reinterpret_cast<uintptr_t>(c.d[k]) & 1)))
+      if (soa_layout(c.layout) && (!c.d[k] || (reinterpret_cast<uintptr_t>(c.d[k]) & 1)))
         return set_error(ERR_ALIGN, "call %d copy %d: bad scale pointer", j, k);
     }
   }

@@ -56,6 +56,7 @@ struct GemvCall {
   void* ws = nullptr;     // workspace of the tensor-core batch kernel
   size_t ws_bytes = 0;
   FuseArgs f;             // fused all-gather (f.nranks == 0: none)
+  int act = 0;            // activations: 0 exact (fixed-point planes), 1 q8_1 (opt-in)
 };
 
 int gemv_soa(int fmt, const GemvCall& c, cudaStream_t st);

@@ -52,9 +52,22 @@ def _xy(x: torch.Tensor, M: int, K: int, y: torch.Tensor | None, device):
     return X, Y, y, N, ldx, ldy
 
 
+def _check_act(activations: str, N: int):
+    if activations not in ("exact", "q8_1"):
+        raise ValueError(f"activations must be 'exact' or 'q8_1', got {activations!r}")
+    if activations == "q8_1" and N != 1:
+        raise ValueError("q8_1 activations are a single-column path (x must be [K])")
+
+
 def qgemv(fmt: str, q: torch.Tensor, d: torch.Tensor, x: torch.Tensor,
-          y: torch.Tensor | None = None, stream: int | None = None) -> torch.Tensor:
-    """SoA GEMV: q (int8 [M, K] | uint8 [M, K/2]), d fp16 [M, K/32], x [K] or [N, K]."""
+          y: torch.Tensor | None = None, stream: int | None = None,
+          activations: str = "exact") -> torch.Tensor:
+    """SoA GEMV: q (int8 [M, K] | uint8 [M, K/2]), d fp16 [M, K/32], x [K] or [N, K].
+
+    ``activations="q8_1"`` (one column) rounds x to int8 per 32-element block
+    inside the kernel (ggml's q8_1 route): faster, but y then carries that
+    rounding and is outside the exact path's 1e-5 bound.
+    """
     _check_fmt(fmt)
     if not q.is_cuda:
         raise ValueError("q must be a CUDA tensor (weights stay resident on the GPU)")
@@ -65,7 +78,12 @@ def qgemv(fmt: str, q: torch.Tensor, d: torch.Tensor, x: torch.Tensor,
     if d.dtype != torch.float16 or tuple(d.shape) != (M, K // QK) or not d.is_contiguous():
         raise ValueError(f"d must be contiguous float16 [{M}, {K // QK}]")
     X, Y, y, N, ldx, ldy = _xy(x, M, K, y, q.device)
+    _check_act(activations, N)
     st = torch.cuda.current_stream(q.device).cuda_stream if stream is None else stream
+    if activations == "q8_1":
+        _lib.call("qgemv_soa_q8_1", 8 if fmt == "q8_0" else 4, q.data_ptr(), d.data_ptr(),
+                  X.data_ptr(), Y.data_ptr(), M, K, st)
+        return y
     if N >= 2:
         # batched calls: the workspace comes from torch's caching allocator
         # (stream-ordered, usable under CUDA graph capture)
@@ -81,8 +99,10 @@ def qgemv(fmt: str, q: torch.Tensor, d: torch.Tensor, x: torch.Tensor,
 
 
 def qgemv_aos(fmt: str, blocks: torch.Tensor, x: torch.Tensor,
-              y: torch.Tensor | None = None, stream: int | None = None) -> torch.Tensor:
-    """GEMV over ggml blocks uint8 [M, K/32, 34|18] (GGUF layout, no repack)."""
+              y: torch.Tensor | None = None, stream: int | None = None,
+              activations: str = "exact") -> torch.Tensor:
+    """GEMV over ggml blocks uint8 [M, K/32, 34|18] (GGUF layout, no repack);
+    ``activations`` as in ``qgemv``."""
     _check_fmt(fmt)
     if not blocks.is_cuda:
         raise ValueError("blocks must be a CUDA tensor")
@@ -92,7 +112,12 @@ def qgemv_aos(fmt: str, blocks: torch.Tensor, x: torch.Tensor,
     M, nb, _ = blocks.shape
     K = nb * QK
     X, Y, y, N, ldx, ldy = _xy(x, M, K, y, blocks.device)
+    _check_act(activations, N)
     st = torch.cuda.current_stream(blocks.device).cuda_stream if stream is None else stream
+    if activations == "q8_1":
+        _lib.call("qgemv_aos_q8_1", 8 if fmt == "q8_0" else 4, blocks.data_ptr(), X.data_ptr(),
+                  Y.data_ptr(), M, K, st)
+        return y
     _lib.call(_AOS_FN[fmt], blocks.data_ptr(), X.data_ptr(), Y.data_ptr(), M, K, N, ldx, ldy, st)
     return y
 
@@ -186,12 +211,16 @@ class QuantizedMatrix:
         return QuantizedMatrix(self.fmt, self.M, self.K, "tiled", tiled=t)
 
     def matvec(self, x: torch.Tensor, y: torch.Tensor | None = None,
-               stream: int | None = None) -> torch.Tensor:
+               stream: int | None = None, activations: str = "exact") -> torch.Tensor:
+        """y = W x; ``activations="q8_1"`` selects the opt-in int8-activation
+        kernel (one column; SoA or AoS layout)."""
         if self.layout == "soa":
-            return qgemv(self.fmt, self.q, self.d, x, y, stream)
+            return qgemv(self.fmt, self.q, self.d, x, y, stream, activations)
         if self.layout == "tiled":
+            if activations != "exact":
+                raise ValueError("batch tiles run the exact path only")
             return qgemv_tiled(self.fmt, self.tiled, self.M, self.K, x, y, stream)
-        return qgemv_aos(self.fmt, self.blocks, x, y, stream)
+        return qgemv_aos(self.fmt, self.blocks, x, y, stream, activations)
 
     __call__ = matvec
 

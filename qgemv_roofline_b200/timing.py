@@ -61,7 +61,9 @@ def time_steps(calls, warmup: int, steps: int, stream: int | None = None,
     """Native timed loop (qgemv_time_steps in include/qgemv_b200.h).
 
     ``calls``: list of dicts with keys fmt ("q8_0"/"q4_0"), layout ("soa"/"aos"),
-    copies (list of (q, d) tensor pairs for SoA, or block tensors for AoS),
+    optional activations ("exact", default, or "q8_1": one column, the opt-in
+    int8-activation kernel), copies (list of (q, d) tensor pairs for SoA, or
+    block tensors for AoS),
     M, K, x [N, K] or [K], y.  Step i runs every call once on copy
     i % len(copies).  grouped=False: steps in order, an event after every
     call; grouped=True: each call's launches back to back as one group, events
@@ -87,7 +89,8 @@ def time_steps(calls, warmup: int, steps: int, stream: int | None = None,
         x, y = c["x"], c["y"]
         N = 1 if x.dim() == 1 else x.shape[0]
         descs[j].format = _lib.FORMAT_CODE[c["fmt"]]
-        descs[j].layout = 0 if c.get("layout", "soa") == "soa" else 1
+        descs[j].layout = ((0 if c.get("layout", "soa") == "soa" else 1)
+                           + (2 if c.get("activations", "exact") == "q8_1" else 0))
         descs[j].ncopies = n
         descs[j].ncols = N
         descs[j].M, descs[j].K = c["M"], c["K"]
