@@ -6,11 +6,14 @@
 Workload (the large, L2-safe configuration the headline target is quoted on):
 W [98304, 4096] ~ N(0, 0.02) fp32, quantized on the GPU to q8_0 and to q4_0
 (SoA planes), x fp32 [4096] ~ N(0, 1), batch 1.  One *step* = one q8_0 GEMV
-plus one q4_0 GEMV.  With N GPUs (one process per GPU, torchrun) the rows are
-sharded: rank g owns rows [g*M/N, (g+1)*M/N) of both matrices, resident in its
-HBM; x is replicated; the step needs no collective (an NCCL all-gather of y is
-timed separately and reported beside it).  Total work is fixed as N grows
-("strong" scaling).
+plus one q4_0 GEMV.  With N GPUs (one process per GPU, torchrun) the rows of a
+[N * 98304, 4096] matrix are sharded: rank g owns rows [g*98304, (g+1)*98304)
+of both formats, resident in its HBM; x is replicated; the step needs no
+collective.  Work per GPU is fixed as N grows ("weak" scaling, the default;
+rows are independent, so the path partitions).  Beside it, under N > 1, the
+line reports the same 98304-row matrix sharded N ways (98304 / N rows per
+rank, "row_sharded_fixed_M": total work fixed) and an NCCL all-gather of y,
+each timed separately.  --scaling strong makes the fixed-M sharding the value.
 
 Every rank keeps C_f copies of each format's weight slice and call i of that
 format reads copy i % C_f, with C_f chosen so that the bytes streamed between
@@ -56,6 +59,9 @@ def parse():
     ap.add_argument("--M", type=int, default=M_FULL)
     ap.add_argument("--K", type=int, default=K_FULL)
     ap.add_argument("--layout", choices=["soa", "aos"], default="soa")
+    ap.add_argument("--scaling", choices=["weak", "strong"], default="weak",
+                    help="xl workload under N > 1 GPUs: weak = 98304 rows per GPU (a [N*98304, "
+                         "4096] matrix row-sharded); strong = the 98304-row matrix sharded N ways")
     ap.add_argument("--no-extras", action="store_true",
                     help="skip roofs, e2e and the CPU baseline (profiling runs)")
     ap.add_argument("--cpu-seconds", type=float, default=10.0,
@@ -84,12 +90,13 @@ def alg_bytes(fmt, M, K, N=1):
 
 
 def workload_config(args, world, rows, copies=None):
+    Mtot = rows * world
     cfg = {
-        "workload": f"q8_0 + q4_0 GEMV, W [{args.M}, {args.K}], x fp32 [{args.K}], batch 1"
-                    + (f", rows sharded over {world} GPUs" if world > 1 else ""),
-        "M": args.M, "K": args.K, "batch": 1, "formats": ["q8_0", "q4_0"],
+        "workload": f"q8_0 + q4_0 GEMV, W [{Mtot}, {args.K}], x fp32 [{args.K}], batch 1"
+                    + (f", rows sharded over {world} GPUs ({rows} per GPU)" if world > 1 else ""),
+        "M": Mtot, "K": args.K, "batch": 1, "formats": ["q8_0", "q4_0"],
         "layout": args.layout, "rows_per_gpu": rows,
-        "weights": "W ~ N(0, 0.02) fp32 (seeded), quantized on the GPU; x ~ N(0, 1)",
+        "weights": "W ~ N(0, 0.02) fp32 (seeded per rank), quantized on the GPU; x ~ N(0, 1)",
         "parallelism": f"row-shard x{world}" if world > 1 else "single GPU",
     }
     if copies is not None:
@@ -341,8 +348,10 @@ def reference_arm(args, rank, world):
         "impl": "reference", "metric": METRIC, "value": value, "unit": "GB/s",
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": dt / args.steps * 1e3, "higher_is_better": True,
-        "scaling": "strong", "vs_baseline": None, "dtype": "fp64" if have_ref else "fp32",
-        "data": "synthetic (seeded)", "config": workload_config(args, world, args.M // world),
+        "scaling": args.scaling, "vs_baseline": None, "dtype": "fp64" if have_ref else "fp32",
+        "data": "synthetic (seeded)",
+        "config": workload_config(args, world,
+                                  args.M if args.scaling == "weak" else args.M // world),
         "cpu_baseline": {"value": value, "unit": "GB/s", "cores": cores, "kind": kind,
                          "sample": sample},
         "e2e": {"value": value, "unit": "GB/s", "h2d_bytes_per_step": 0,
@@ -451,8 +460,8 @@ def main():
         return t.tolist()
 
     M, K = args.M, args.K
-    r0, r1 = M * rank // world, M * (rank + 1) // world
-    rows = r1 - r0
+    weak = args.scaling == "weak"
+    rows = M if weak else M * (rank + 1) // world - M * rank // world
     step_bytes_rank = alg_bytes("q8_0", rows, K) + alg_bytes("q4_0", rows, K)
     ncopies = {f: max(2, math.ceil(4 * L2_BYTES / wbytes(f, rows, K))) for f in ("q8_0", "q4_0")}
 
@@ -497,6 +506,38 @@ def main():
         barrier()
     clocks = sampler.summary()
     total_ms, q8_ms, q4_ms = max_over_ranks([total_ms, per_ms[0], per_ms[1]])
+
+    # ------------------------- the fixed 98304-row matrix sharded N ways (N > 1)
+    # Rank slices of M / N rows taken from the resident copies at distinct row
+    # offsets (views, no new memory): copies x N distinct slices per format,
+    # >= 4x L2 streamed between two reads of one slice.
+    if world > 1 and weak:
+        rs = M // world
+        scalls = []
+        for f in ("q8_0", "q4_0"):
+            views = []
+            for cp in mats[f]:
+                for j in range(world):
+                    if args.layout == "soa":
+                        views.append((cp[0][j * rs:(j + 1) * rs], cp[1][j * rs:(j + 1) * rs]))
+                    else:
+                        views.append(cp[j * rs:(j + 1) * rs])
+            scalls.append({"fmt": f, "layout": args.layout, "copies": views, "M": rs, "K": K,
+                           "x": x, "y": ys[f][:rs]})
+        barrier()
+        s_total, s_per = time_steps(scalls, args.warmup, args.steps, grouped=True)
+        barrier()
+        s_total, s_q8, s_q4 = max_over_ranks([s_total, s_per[0], s_per[1]])
+        s_bytes = alg_bytes("q8_0", rs, K) + alg_bytes("q4_0", rs, K)
+        extras["row_sharded_fixed_M"] = {
+            "M": M, "rows_per_gpu": rs, "scaling": "strong",
+            "value": world * s_bytes * args.steps / (s_total * 1e-3) / 1e9, "unit": "GB/s",
+            "ms_per_step": s_total / args.steps,
+            "slices_rotated": {f: len(c["copies"]) for f, c in zip(("q8_0", "q4_0"), scalls)},
+            "per_format": {f: {"us_per_call": ms / args.steps * 1e3,
+                               "gbps_aggregate": world * alg_bytes(f, rs, K)
+                               / (ms / args.steps * 1e-3) / 1e9}
+                           for f, ms in (("q8_0", s_q8), ("q4_0", s_q4))}}
     K_steps = args.steps
     value = world * step_bytes_rank * K_steps / (total_ms * 1e-3) / 1e9
     peak, peak_note = measured_peak()
@@ -615,7 +656,7 @@ def main():
         line = {
             "metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": total_ms / K_steps,
-            "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+            "higher_is_better": True, "scaling": args.scaling, "vs_baseline": None,
             "dtype": "fp32", "data": "synthetic (seeded N(0, 0.02) weights, N(0, 1) x)",
             "config": workload_config(args, world, rows, ncopies),
             "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e,

@@ -24,6 +24,12 @@
 //    and stored per (row, slice) in shared memory.
 //  * Programmatic dependent launch: the next launch may start once this one
 //    has set up; it prefetches only weights before griddepcontrol.wait.
+//  * x reaches the CTA as one bulk copy, issued by the producer right after
+//    its dependency wait into the last ring stage (still empty then); the
+//    consumers convert it from shared memory and release the stage, which
+//    then receives its first weight tile.  Per-lane loads of x from L2 (the
+//    fallback when a stage cannot hold x) cost ~2 us more per call: every
+//    warp of every CTA reads the same bytes at the same moment.
 //  * When a stage is released, the producer warp sums the KS slice partials
 //    of each row in a fixed order (deterministic) and writes y.
 //  * Every mbarrier wait is bounded (~1 s).  On a timeout the CTA raises a
@@ -279,6 +285,37 @@ __device__ __forceinline__ void make_planes_from(const float (&v)[32], XPlanes& 
   }
 }
 
+// The planes of one x block held in shared memory at 32-bit address xb
+// (128 bytes).  A block is exactly 32 banks wide, so in natural order every
+// lane of a warp would read the same 4 banks; lane l reads its eight 16-byte
+// chunks in the order (i + l) & 7 instead (the 8 lanes of a quarter-warp hit 8
+// different bank groups), builds the plane words in that order, and rotates
+// them back by l & 7 with three conditional shifts.  The block maximum, the
+// rounding and the sum do not depend on the order.
+__device__ __forceinline__ void make_planes_smem(uint32_t xb, int lane, XPlanes& o) {
+  float v[32];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const uint4 f = lds_v4(xb + (uint32_t)(((i + lane) & 7) << 4));
+    v[4 * i] = __uint_as_float(f.x); v[4 * i + 1] = __uint_as_float(f.y);
+    v[4 * i + 2] = __uint_as_float(f.z); v[4 * i + 3] = __uint_as_float(f.w);
+  }
+  make_planes_from(v, o);  // o.pl[i] = plane words of chunk (i + l) & 7
+#pragma unroll
+  for (int k = 1; k < 8; k <<= 1) {
+    const bool b = (lane & k) != 0;
+    uint32_t t[8][NPL];
+#pragma unroll
+    for (int c = 0; c < 8; ++c)
+#pragma unroll
+      for (int pl = 0; pl < NPL; ++pl) t[c][pl] = b ? o.pl[(c - k) & 7][pl] : o.pl[c][pl];
+#pragma unroll
+    for (int c = 0; c < 8; ++c)
+#pragma unroll
+      for (int pl = 0; pl < NPL; ++pl) o.pl[c][pl] = t[c][pl];
+  }
+}
+
 // The exact integer dot of one 32-weight block with the x planes, folded to
 // one float: F = S2 2^16 + (S1 2^8 + S0) (q4_0: 16 x that, minus the bias of
 // the -8 offset).  wq: the block's quant words (q8_0: 8 words of int8, word w
@@ -360,6 +397,8 @@ struct XQ81 {
   int bias;       // 128 * sum_j q_j (q4_0: the -8 offset, in the 16 n units)
 };
 
+__device__ __forceinline__ void make_q81_from(const float (&v)[32], XQ81& o);
+
 __device__ __forceinline__ void make_q81(const float* __restrict__ xb, XQ81& o) {
   float v[32];
 #pragma unroll
@@ -367,6 +406,31 @@ __device__ __forceinline__ void make_q81(const float* __restrict__ xb, XQ81& o) 
     const float4 f = *reinterpret_cast<const float4*>(xb + 4 * i);
     v[4 * i] = f.x; v[4 * i + 1] = f.y; v[4 * i + 2] = f.z; v[4 * i + 3] = f.w;
   }
+  make_q81_from(v, o);
+}
+
+// From shared memory, in the rotated chunk order of make_planes_smem.
+__device__ __forceinline__ void make_q81_smem(uint32_t xb, int lane, XQ81& o) {
+  float v[32];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const uint4 f = lds_v4(xb + (uint32_t)(((i + lane) & 7) << 4));
+    v[4 * i] = __uint_as_float(f.x); v[4 * i + 1] = __uint_as_float(f.y);
+    v[4 * i + 2] = __uint_as_float(f.z); v[4 * i + 3] = __uint_as_float(f.w);
+  }
+  make_q81_from(v, o);  // o.q[i] = quants of chunk (i + l) & 7
+#pragma unroll
+  for (int k = 1; k < 8; k <<= 1) {
+    const bool b = (lane & k) != 0;
+    uint32_t t[8];
+#pragma unroll
+    for (int c = 0; c < 8; ++c) t[c] = b ? o.q[(c - k) & 7] : o.q[c];
+#pragma unroll
+    for (int c = 0; c < 8; ++c) o.q[c] = t[c];
+  }
+}
+
+__device__ __forceinline__ void make_q81_from(const float (&v)[32], XQ81& o) {
   uint32_t amax_bits = 0u;
 #pragma unroll
   for (int j = 0; j < 32; ++j) amax_bits = max(amax_bits, __float_as_uint(v[j]) & 0x7FFFFFFFu);
@@ -433,6 +497,10 @@ struct TmaArgs {
   const float* x;
   float* y;
   int M, K, TR, S, KS;
+  // 1: x arrives by one bulk copy per CTA into the last ring stage (MODE 1
+  // and 2, S >= 3, K * 4 <= stage bytes, no fused all-gather); 0: per-lane
+  // loads after the dependency wait
+  int xstage;
   FuseArgs f;  // all-gather of y into peer buffers (f.nranks == 0: none)
 };
 
@@ -477,6 +545,8 @@ k_gemv_tma(const TmaArgs p) {
   extern __shared__ __align__(128) uint8_t sm[];
   __shared__ __align__(8) unsigned long long full[MAX_STAGES];
   __shared__ __align__(8) unsigned long long empty[MAX_STAGES];
+  __shared__ __align__(8) unsigned long long xfull;   // staged x has arrived
+  __shared__ __align__(8) unsigned long long xempty;  // every consumer has read it
   __shared__ int abort_flag;
   __shared__ uint32_t x_ready;
 
@@ -497,6 +567,8 @@ k_gemv_tma(const TmaArgs p) {
       asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(saddr(&empty[s])),
                    "r"(CONSUMERS));
     }
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(saddr(&xfull)));
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(saddr(&xempty)), "r"(CONSUMERS));
     abort_flag = 0;
     x_ready = 0u;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -514,8 +586,12 @@ k_gemv_tma(const TmaArgs p) {
     int last_issued[MAX_STAGES];
     for (int s = 0; s < MAX_STAGES; ++s) last_issued[s] = -1;
     bool ok = true;
+    bool x_issued = false;
     int s = 0;         // stage of tile t (t % S)
     uint32_t cyc = 0;  // t / S
+    if (p.xstage && lane == 0)  // x into L2 while the previous kernel drains (a hint only)
+      asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p.x), "r"((uint32_t)K * 4u)
+                   : "memory");
     for (int t = 0; t < ntiles + S && ok; ++t) {
       // Tile 0 (weights only) is prefetched before the dependency wait, the
       // rest after it.  One tile, not the whole ring: x is loaded right after
@@ -523,7 +599,26 @@ k_gemv_tma(const TmaArgs p) {
       // previous grid) would otherwise queue its x loads behind S tiles of
       // copies.  Measured: 0.6-1.0 us less per call at 12288-24576 rows,
       // unchanged at 98304.
-      if (t == kPrefetchTiles) asm volatile("griddepcontrol.wait;" ::: "memory");
+      if (t == kPrefetchTiles) {
+        asm volatile("griddepcontrol.wait;" ::: "memory");
+        if (p.xstage) {
+          // x (which may be the previous kernel's y) as one bulk copy into the
+          // last stage, issued before any further weight tile; the stage
+          // receives its first tile once every consumer has read x
+          if (lane == 0) {
+            const uint32_t bar = saddr(&xfull);
+            asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar),
+                         "r"((uint32_t)K * 4u)
+                         : "memory");
+            bulk_g2s(saddr(sm + (size_t)(S - 1) * STG), p.x, (uint32_t)K * 4u, bar);
+          }
+          x_issued = true;
+        }
+      }
+      if (x_issued && t == S - 1 && t < ntiles) {
+        ok = __all_sync(0xffffffffu, mbar_wait(saddr(&xempty), 0u, &abort_flag));
+        if (!ok) break;
+      }
       if (t >= S) {
         const int tt = t - S;  // tile whose stage is recycled now (cycle cyc - 1)
         // every lane waits (acquire), since every lane reads the partials
@@ -565,6 +660,7 @@ k_gemv_tma(const TmaArgs p) {
       for (int s = 0; s < S; ++s)
         if (last_issued[s] >= 0)
           mbar_wait_drain(saddr(&full[s]), (uint32_t)((last_issued[s] / S) & 1));
+      if (x_issued) mbar_wait_drain(saddr(&xfull), 0u);
     }
     if (p.f.nranks > 0) {
       // The CTA that finishes last tells every rank that this rank's slice of
@@ -616,6 +712,29 @@ k_gemv_tma(const TmaArgs p) {
         const int jj = 4 * t + (pp >> 1) + 16 * (pp & 1);
         xr[e] = cval ? p.x[cidx * 32 + jj] * __int_as_float((127 - q4_shift(pp)) << 23) : 0.0f;
       }
+    }
+  } else if (p.xstage) {
+    // x staged in the last ring stage by the producer (after its dependency
+    // wait); every consumer warp releases the stage once it has converted x
+    const bool got = __all_sync(0xffffffffu, mbar_wait(saddr(&xfull), 0u, &abort_flag));
+    const uint32_t xb = saddr(sm) + (uint32_t)((S - 1) * STG + cidx * 128);
+    if (MODE == 2) {
+      if (got && cval) make_q81_smem(xb, lane, x8);  // lanes past K: zero quants, never stored
+    } else if (got && cval) {
+      make_planes_smem(xb, lane, xp);
+    } else {
+      for (int w = 0; w < 8; ++w)
+        for (int pl = 0; pl < NPL; ++pl) xp.pl[w][pl] = 0u;
+      xp.e = -149;
+      xp.bias = 0.0f;
+      xp.finite = true;
+    }
+    __syncwarp();
+    if (lane == 0)
+      asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(saddr(&xempty)) : "memory");
+    if (MODE == 1) {
+      xq = x_scale<FMT>(xp);
+      fast = __all_sync(0xffffffffu, !cval || xq.fast);
     }
   } else {
     // Pull the lane's 128 bytes of x into L2 while the previous kernel
@@ -1104,6 +1223,15 @@ int plan_tma(const void* kern, int M, int K, const DeviceInfo& dev, TmaPlan* out
     S = std::min(MAX_STAGES, avail / (TR * row_bytes + TR * KS * 4));
   }
   if (S < 2) return -1;
+  if (MODE != 0 && TR * row_bytes < K * 4) {
+    // x is staged in a ring stage: more rows per tile, if three stages still fit
+    const int TRx = unit * ((K * 4 + unit * row_bytes - 1) / (unit * row_bytes));
+    const int Sx = std::min(MAX_STAGES, avail / (TRx * row_bytes + TRx * KS * 4));
+    if (Sx >= 3) {
+      TR = TRx;
+      S = Sx;
+    }
+  }
   TmaPlan pl;
   pl.TR = TR;
   pl.S = S;
@@ -1125,8 +1253,15 @@ int launch_tma(const GemvCall& c, const DeviceInfo& dev, cudaStream_t st) {
                                                        dev, &pl))
     return rc;
   const int grid = c.grid_override > 0 ? c.grid_override : pl.grid;
+  using F = Fmt<FMT>;
+  const int64_t stage_bytes =
+      (int64_t)pl.TR * (AOS ? (K / QK) * F::BLOCK_BYTES : K / F::ROW_DIV + K / 16);
+  // x by one bulk copy per CTA: measured 1.8-2.6 us less per call than
+  // per-lane loads of x (every warp of every CTA reading the same 16 KB at
+  // the same moment), from 4096 to 98304 rows of K = 4096
+  const int xstage = MODE != 0 && c.f.nranks == 0 && pl.S >= 3 && (int64_t)K * 4 <= stage_bytes;
   TmaArgs a{static_cast<const uint8_t*>(c.q), static_cast<const unsigned short*>(c.d), c.x, c.y,
-            M, K, pl.TR, pl.S, pl.KS, c.f};
+            M, K, pl.TR, pl.S, pl.KS, xstage, c.f};
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(grid);
   cfg.blockDim = dim3(tma_threads(CONSUMERS));
