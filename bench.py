@@ -561,7 +561,8 @@ def main():
         targs = "4,1,8,16" if rows * (K // 2 + K // 16) >= (150 << 20) else "4,1,8,8"
     else:
         targs = "8,1,4,8" if rows * (K + K // 16) < (256 << 20) else "8,1,4,16"
-    kname = f"k_gemv_tma<{targs},{'false' if args.layout == 'soa' else 'true'}>"
+    kname = f"k_gemv_tma<{targs},{'false' if args.layout == 'soa' else 'true'}"
+    kname += ",4096>" if args.layout == "soa" and K == 4096 else ">"
     ach = per_format[dom]["gbps_per_gpu"]
     traffic = dram_traffic(f"{dom}_{args.layout}_{rows}x{K}")
     roofline = {"bound": "hbm", "achieved": ach, "peak": peak, "unit": "GB/s",

@@ -537,7 +537,19 @@ __device__ __forceinline__ bool wait_count(const unsigned* c, unsigned target,
 // AOS: the weights are ggml blocks [M][K/32] (34 / 18 bytes, d first); a tile
 // of rows is then one contiguous range and each lane realigns its block from
 // shared memory (MODE 1 only).
-template <int FMT, int MODE, int R, int CONSUMERS, bool AOS = false>
+// K slices of a row (a power of two): each covers 32 units (MODE 0: 16-byte
+// chunks; else 32-weight blocks)
+template <int FMT, int MODE>
+__host__ __device__ constexpr int slices_of(int K) {
+  const int nunits = MODE == 0 ? K / Fmt<FMT>::ELEMS_PER_CHUNK : K / QK;
+  int ks = 1;
+  while (ks * 32 < nunits) ks *= 2;
+  return ks;
+}
+
+// KF != 0: the kernel is compiled for K == KF (the row strides of the stage
+// become immediate offsets of the shared-memory loads).
+template <int FMT, int MODE, int R, int CONSUMERS, bool AOS = false, int KF = 0>
 __global__ void __launch_bounds__(tma_threads(CONSUMERS), tma_ctas_per_sm(CONSUMERS))
 k_gemv_tma(const TmaArgs p) {
   using F = Fmt<FMT>;
@@ -550,7 +562,8 @@ k_gemv_tma(const TmaArgs p) {
   __shared__ int abort_flag;
   __shared__ uint32_t x_ready;
 
-  const int K = p.K, TR = p.TR, S = p.S, KS = p.KS;
+  const int K = KF ? KF : p.K, TR = p.TR, S = p.S;
+  const int KS = KF ? slices_of<FMT, MODE>(KF) : p.KS;
   // bytes per row of the quant plane / of the scale plane (AoS: whole blocks, no plane)
   const int QB = AOS ? (K / QK) * F::BLOCK_BYTES : K / F::ROW_DIV;
   const int DB = AOS ? 0 : K / 16;
@@ -1244,9 +1257,10 @@ int plan_tma(const void* kern, int M, int K, const DeviceInfo& dev, TmaPlan* out
   return OK;
 }
 
-template <int FMT, int MODE, int R, int CONSUMERS, bool AOS = false>
+template <int FMT, int MODE, int R, int CONSUMERS, bool AOS = false, int KF = 0>
 int launch_tma(const GemvCall& c, const DeviceInfo& dev, cudaStream_t st) {
-  auto kern = k_gemv_tma<FMT, MODE, R, CONSUMERS, AOS>;
+  if (KF != 0 && c.K != KF) return -1;
+  auto kern = k_gemv_tma<FMT, MODE, R, CONSUMERS, AOS, KF>;
   const int K = (int)c.K, M = (int)c.M;
   TmaPlan pl;
   if (int rc = plan_tma<FMT, MODE, R, CONSUMERS, AOS>(reinterpret_cast<const void*>(kern), M, K,
@@ -1308,14 +1322,23 @@ int gemv_soa_tma(int fmt, const GemvCall& c, cudaStream_t st) {
     if (rc == -1) rc = launch_tma<8, 2, 4, 16>(c, dev, st);
     return rc;
   }
+  // K = 4096 (the 7B-class QKV / O / gate+up shape): kernels compiled for it
   if (fmt == 4) {
-    if (wbytes >= ((int64_t)150 << 20)) rc = launch_tma<4, 1, 8, 16>(c, dev, st);
+    const bool big = wbytes >= ((int64_t)150 << 20);
+    if (c.K == 4096)
+      rc = big ? launch_tma<4, 1, 8, 16, false, 4096>(c, dev, st)
+               : launch_tma<4, 1, 8, 8, false, 4096>(c, dev, st);
+    if (rc == -1 && big) rc = launch_tma<4, 1, 8, 16>(c, dev, st);
     if (rc == -1) rc = launch_tma<4, 1, 8, 8>(c, dev, st);
     if (rc == -1) rc = launch_tma<4, 1, 4, 8>(c, dev, st);
     if (rc == -1) rc = launch_tma<4, 1, 4, 16>(c, dev, st);
     return rc;
   }
-  if (wbytes < ((int64_t)256 << 20)) rc = launch_tma<8, 1, 4, 8>(c, dev, st);
+  const bool small = wbytes < ((int64_t)256 << 20);
+  if (c.K == 4096)
+    rc = small ? launch_tma<8, 1, 4, 8, false, 4096>(c, dev, st)
+               : launch_tma<8, 1, 4, 16, false, 4096>(c, dev, st);
+  if (rc == -1 && small) rc = launch_tma<8, 1, 4, 8>(c, dev, st);
   if (rc == -1) rc = launch_tma<8, 1, 4, 16>(c, dev, st);
   return rc;
 }
