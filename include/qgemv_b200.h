@@ -219,8 +219,9 @@ QGEMV_API int qgemv_token_fence(unsigned* const* done, int32_t nranks, const uns
 
 /* Batch tiles: the same quantized weights re-laid for the tensor-core batch
  * kernel, one contiguous block per 16 rows x 512 columns (quants in the
- * order the kernel reads them, then that block's fp16 scales; rows beyond M
- * and columns beyond K zero).  A block is then a single bulk copy; the SoA
+ * order the kernel reads them -- q8_0 bytes as w + 128, the sign bit flipped
+ * -- then that block's fp16 scales; rows beyond M and columns beyond K hold
+ * zero weights).  A block is then a single bulk copy; the SoA
  * planes, whose 16 rows lie K bytes apart, need 16 copies per block and
  * stream at a fraction of the HBM rate on this path.  Made once per weight
  * matrix (qgemv_tile_weights), from SoA planes (layout 0: q, d) or from

@@ -236,6 +236,15 @@ __device__ __forceinline__ uint32_t q8_pair02(uint32_t w) {
   return hadd2(lop3_and_xor(w, 0x00FF00FFu, 0x64806480u), 0xE480E480u);
 }
 __device__ __forceinline__ uint32_t q8_pair13(uint32_t w) { return q8_pair02(w >> 8); }
+// q8_0 batch tiles hold u = w + 128 (sign bit flipped): one PRMT puts bytes
+// 0 and 2 (1 and 3) under the fp16 exponent byte 0x64, fp16(1024 + u), and
+// adding -1152 leaves w -- no shift and no mask.
+__device__ __forceinline__ uint32_t q8u_pair02(uint32_t u) {
+  return hadd2(__byte_perm(u, 0x64646464u, 0x6240), 0xE480E480u);
+}
+__device__ __forceinline__ uint32_t q8u_pair13(uint32_t u) {
+  return hadd2(__byte_perm(u, 0x64646464u, 0x6341), 0xE480E480u);
+}
 // q4_0: word = bytes (p0, p1, p2, p3), byte i = n_i | m_i << 4.  Low nibbles
 // of bytes 0 and 2: fp16(1024 + n) - 1032 = n - 8.  High nibbles in place:
 // fp16(1024 + 16 m) * 1/16 - 72 = m - 8.
@@ -392,8 +401,9 @@ struct MmaFmt {
 //   quants: NBOX boxes of [16 rows][128 bytes]; within a box, 16-byte chunk
 //           j of row r is stored at chunk position j ^ (r & 7) (the TMA
 //           128-byte swizzle, so that ldmatrix reads are conflict-free);
+//           q8_0 bytes hold w + 128 (the int8 with its sign bit flipped);
 //   scales: [16 rows][16 blocks] fp16.
-// Rows beyond M and columns beyond K are zero.  A few tiles are then one
+// Rows beyond M and columns beyond K hold zero weights.  A few tiles are then one
 // bulk copy, which streams at the HBM rate where 16 strided row pieces do not.
 // KSPLIT warps share a row tile (each takes KC/32/KSPLIT blocks of every
 // stage) and each warp holds TW tiles, so CONS/KSPLIT*TW tiles are in flight
@@ -921,11 +931,11 @@ __global__ void __launch_bounds__(THREADS, 1) k_gemv_tiles(const __grid_constant
           }
           uint32_t A0[4], A1[4];
           if (FMT == 8) {
-            const uint32_t* w = aw[i];
-            A0[0] = q8_pair02(w[0]); A0[1] = q8_pair02(w[1]);
-            A0[2] = q8_pair13(w[0]); A0[3] = q8_pair13(w[1]);
-            A1[0] = q8_pair02(w[2]); A1[1] = q8_pair02(w[3]);
-            A1[2] = q8_pair13(w[2]); A1[3] = q8_pair13(w[3]);
+            const uint32_t* w = aw[i];  // w + 128 per byte (batch tiles)
+            A0[0] = q8u_pair02(w[0]); A0[1] = q8u_pair02(w[1]);
+            A0[2] = q8u_pair13(w[0]); A0[3] = q8u_pair13(w[1]);
+            A1[0] = q8u_pair02(w[2]); A1[1] = q8u_pair02(w[3]);
+            A1[2] = q8u_pair13(w[2]); A1[3] = q8u_pair13(w[3]);
           } else {
             const uint32_t w0 = aw[i >> 1][2 * (i & 1)], w1 = aw[i >> 1][2 * (i & 1) + 1];
             const uint32_t v0 = w0 >> 8, v1 = w1 >> 8;
@@ -1019,8 +1029,11 @@ __global__ void __launch_bounds__(256) k_tile(const uint8_t* __restrict__ q,
     const int64_t T = (M + TILE - 1) / TILE;
     const int kt = (int)(blk / T);
     const int64_t tile = blk - (int64_t)kt * T;
+    // q8_0 quants are stored as w + 128 (sign bit flipped; padding is w = 0)
+    const uint32_t qpad = FMT == 8 ? 0x80808080u : 0u;
     uint32_t w[4] = {0u, 0u, 0u, 0u};
     if (off < F::QST) {
+      w[0] = w[1] = w[2] = w[3] = qpad;
       const int bx = off / (TILE * 128), r = (off % (TILE * 128)) / 128, pc = (off % 128) / 16;
       const int j = pc ^ (r & 7);
       const int64_t R = tile * TILE + r;
@@ -1028,13 +1041,17 @@ __global__ void __launch_bounds__(256) k_tile(const uint8_t* __restrict__ q,
       if (R < M && col < qrow) {
         if (!AOS) {
           const uint4 v = *reinterpret_cast<const uint4*>(q + R * qrow + col);
-          w[0] = v.x; w[1] = v.y; w[2] = v.z; w[3] = v.w;
+          w[0] = v.x ^ qpad; w[1] = v.y ^ qpad; w[2] = v.z ^ qpad; w[3] = v.w ^ qpad;
         } else {
           // q8_0: 16 of a block's 32 quants; q4_0: a block's 16 quant bytes
           const int64_t kb = FMT == 8 ? col / 32 : col / 16;
           const uint8_t* src = q + (R * nb + kb) * BS + 2 + (FMT == 8 ? col % 32 : 0);
 #pragma unroll
+          for (int i = 0; i < 4; ++i) w[i] = 0u;
+#pragma unroll
           for (int i = 0; i < 16; ++i) w[i >> 2] |= (uint32_t)src[i] << (8 * (i & 3));
+#pragma unroll
+          for (int i = 0; i < 4; ++i) w[i] ^= qpad;
         }
       }
     } else {

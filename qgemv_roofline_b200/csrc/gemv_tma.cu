@@ -62,7 +62,7 @@ constexpr int tma_threads(int cw) { return 32 * (cw + 1); }
 // CTAs of `cw` consumer warps per SM: 16 consumer warps per SM in all
 constexpr int tma_ctas_per_sm(int cw) { return cw >= 16 ? 1 : 16 / cw; }
 constexpr int MAX_STAGES = 8;
-constexpr int kPrefetchTiles = 1;  // weight tiles issued before the dependency wait (<= S)
+constexpr int kPrefetchTiles = 1;  // weight tiles issued before the dependency wait (<= S - 1)
 constexpr long long SPIN_LIMIT = 2000000000LL;  // clock64 cycles, ~1 s
 
 __device__ __forceinline__ uint32_t saddr(const void* p) {
@@ -609,9 +609,9 @@ k_gemv_tma(const TmaArgs p) {
       // Tile 0 (weights only) is prefetched before the dependency wait, the
       // rest after it.  One tile, not the whole ring: x is loaded right after
       // the wait, and a CTA that starts late (its SM freed at the end of the
-      // previous grid) would otherwise queue its x loads behind S tiles of
-      // copies.  Measured: 0.6-1.0 us less per call at 12288-24576 rows,
-      // unchanged at 98304.
+      // previous grid) would otherwise queue x behind the prefetched copies.
+      // Measured against 2 and S - 1 tiles (x staged): 0.4-0.9 us less per
+      // call from 4096 to 49152 rows, 0.4 us more for q8_0 at 98304.
       if (t == kPrefetchTiles) {
         asm volatile("griddepcontrol.wait;" ::: "memory");
         if (p.xstage) {

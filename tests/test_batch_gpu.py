@@ -252,8 +252,10 @@ def tiles_np(fmt, q, d, M, K):
     qrow = K if fmt == "q8_0" else K // 2
     QROW = KC if fmt == "q8_0" else KC // 2
     nbox = QROW // 128
-    qp = np.zeros((T * 16, nkt * QROW), np.uint8)
-    qp[:M, :qrow] = q.view(np.uint8).reshape(M, qrow)
+    # q8_0 quants are stored as w + 128 (sign bit flipped), padding as w = 0
+    flip = 0x80 if fmt == "q8_0" else 0
+    qp = np.full((T * 16, nkt * QROW), flip, np.uint8)
+    qp[:M, :qrow] = q.view(np.uint8).reshape(M, qrow) ^ flip
     dp = np.zeros((T * 16, nkt * 16), np.uint16)
     dp[:M, :K // 32] = d.view(np.uint16).reshape(M, K // 32)
     out = []
