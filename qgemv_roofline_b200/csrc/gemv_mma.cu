@@ -715,17 +715,17 @@ __global__ void __launch_bounds__(THREADS, 1) k_gemv_mma(const __grid_constant__
 
 // GEMV over batch tiles.  A stage is TPS consecutive tiles of one K tile
 // (about 18 KB: 2 tiles of q8_0, 4 of q4_0), one bulk copy.  Warps 2j and
-// 2j+1 own tile j of the current chunk of 8 and take the two K halves of
+// 2j+1 own tile j of the current chunk of CN / 2 and take the two K halves of
 // each stage; a warp copies its quants and scales from the stage into
 // registers (ldmatrix) and releases the slot before it computes, so the ring
 // keeps nearly all its stages in flight.  The per-block arithmetic and its
 // order are those of k_gemv_mma (two warps per tile), so both give the same
 // bits for the same matrix.
-template <int FMT, int NT>
-__global__ void __launch_bounds__(THREADS, 1) k_gemv_tiles(const __grid_constant__ MmaArgs p) {
+template <int FMT, int NT, int CN>
+__global__ void __launch_bounds__(32 * (CN + 1), 1) k_gemv_tiles(const __grid_constant__ MmaArgs p) {
   using F = MmaFmt<FMT>;
   constexpr int KSP = 2;                   // warps per tile (K halves)
-  constexpr int CT = CONS / KSP;           // tiles per chunk
+  constexpr int CT = CN / KSP;             // tiles per chunk
   constexpr int TPS = FMT == 8 ? 2 : 4;    // tiles per stage
   constexpr int SLOT = (TPS * F::BLK + 1023) / 1024 * 1024;
   constexpr int HB = KC / QK / KSP;        // K blocks per warp per stage (8)
@@ -766,7 +766,7 @@ __global__ void __launch_bounds__(THREADS, 1) k_gemv_tiles(const __grid_constant
     }
     for (int s = 0; s < XSL; ++s) {
       asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(saddr(&xfull[s])));
-      asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(saddr(&xempty[s])), "r"(CONS));
+      asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(saddr(&xempty[s])), "r"(CN));
     }
     asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(saddr(&redfull)), "r"(CT));
     asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(saddr(&redempty)), "r"(CT));
@@ -1130,14 +1130,21 @@ struct MmaPlan {
 };
 std::map<std::tuple<const void*, int, int64_t>, MmaPlan> g_plans;
 
+// Consumer warps of the batch-tile kernel: 14 (15 warps with the producer,
+// at most 4 per SM sub-partition, so 128 registers a thread) measured faster
+// than 16 (17 warps, capped at 96 registers, small spills) at every batch
+// width -- N = 16: 82.0 -> 75.9 us (q8_0) at 28672 x 8192 -- and than 12.
+constexpr int TILE_CONS = 14;
+
 template <int FMT, int NT, int TW, int KSPLIT, bool TILED>
 int launch_mma(const GemvCall& c, const DeviceInfo& dev, cudaStream_t st) {
   using F = MmaFmt<FMT>;
   constexpr int SLOT = TILED ? ((FMT == 8 ? 2 : 4) * F::BLK + 1023) / 1024 * 1024 : F::SLOT;
-  constexpr size_t RED = TILED ? (size_t)(CONS / 2) * NT * 4 * 32 * sizeof(float)
+  constexpr int CN = TILED ? TILE_CONS : CONS;
+  constexpr size_t RED = TILED ? (size_t)(CN / 2) * NT * 4 * 32 * sizeof(float)
                                : (size_t)(CONS / KSPLIT) * (KSPLIT - 1) * TW * NT * 4 * 32 *
                                      sizeof(float);
-  auto kern = TILED ? k_gemv_tiles<FMT, NT> : k_gemv_mma<FMT, NT, TW, KSPLIT>;
+  auto kern = TILED ? k_gemv_tiles<FMT, NT, CN> : k_gemv_mma<FMT, NT, TW, KSPLIT>;
   const void* kp = reinterpret_cast<const void*>(kern);
   MmaPlan pl;
   bool have = false;
@@ -1194,7 +1201,7 @@ int launch_mma(const GemvCall& c, const DeviceInfo& dev, cudaStream_t st) {
                                      static_cast<uint8_t*>(c.ws));
   if (e != cudaSuccess) return set_error(ERR_CUDA, "k_xprep launch: %s", cudaGetErrorString(e));
   cfg.gridDim = dim3(c.grid_override > 0 ? c.grid_override : pl.grid);
-  cfg.blockDim = dim3(THREADS);
+  cfg.blockDim = dim3(32 * (CN + 1));
   cfg.dynamicSmemBytes = pl.smem;
   e = cudaLaunchKernelEx(&cfg, kern, a);
   if (e != cudaSuccess) return set_error(ERR_CUDA, "k_gemv_mma launch: %s", cudaGetErrorString(e));
