@@ -8,8 +8,10 @@
 //    tiles of TR consecutive rows (quant bytes and fp16 scales, each tile
 //    two contiguous 1-D bulk copies, cp.async.bulk) into an S-stage
 //    shared-memory ring; completion is tracked by per-stage "full" mbarriers
-//    (expect_tx) and stages are recycled through "empty" mbarriers.  Each CTA
-//    owns a contiguous row range, so it streams one contiguous region.
+//    (expect_tx) and stages are recycled through "empty" mbarriers.  With one
+//    CTA per SM each CTA owns a contiguous row range (one contiguous
+//    stream); with two, the CTAs claim tiles of rows at run time from a
+//    per-stream counter (TmaArgs::tctr), so faster CTAs take more tiles.
 //  * Warps 1..16 consume.  Consumer warp w owns K slice (w % KS) and row
 //    group (w / KS); lane l of it owns one 32-weight block of that slice.
 //    In the default mode (MODE 1) the lane converts its 32 x values once per
@@ -52,6 +54,10 @@
 namespace qg {
 
 __device__ int g_device_error = 0;
+
+// The tile counter of a launch on stream st (device memory, no allocation),
+// or null when none is free; defined with the counter pool below.
+unsigned* tile_counter(int device, cudaStream_t st);
 
 namespace {
 
@@ -501,6 +507,13 @@ struct TmaArgs {
   // and 2, S >= 3, K * 4 <= stage bytes, no fused all-gather); 0: per-lane
   // loads after the dependency wait
   int xstage;
+  // Tile counter of this launch (zero at entry, zero again at exit), or null:
+  // null -> each CTA streams its own contiguous row range; else the matrix is
+  // cut into global tiles of TR rows, CTA b takes tiles b and b + G (G CTAs)
+  // and then claims tiles 2G, 2G + 1, ... with atomicAdd, so CTAs that stream
+  // faster take more tiles (a shorter tail of slow CTAs).  The launch's last
+  // claim (each CTA makes exactly one failing claim) resets the counter.
+  unsigned* tctr;
   FuseArgs f;  // all-gather of y into peer buffers (f.nranks == 0: none)
 };
 
@@ -561,6 +574,7 @@ k_gemv_tma(const TmaArgs p) {
   __shared__ __align__(8) unsigned long long xempty;  // every consumer has read it
   __shared__ int abort_flag;
   __shared__ uint32_t x_ready;
+  __shared__ int stage_nr[MAX_STAGES];  // rows of the tile in each stage; 0: no more tiles
 
   const int K = KF ? KF : p.K, TR = p.TR, S = p.S;
   const int KS = KF ? slices_of<FMT, MODE>(KF) : p.KS;
@@ -597,15 +611,24 @@ k_gemv_tma(const TmaArgs p) {
   if (warp == 0) {
     // ------------------------------------------------------------ producer
     int last_issued[MAX_STAGES];
+    int fin_r0[MAX_STAGES];  // first row and rows of the tile in each stage
+    int fin_nr[MAX_STAGES];
     for (int s = 0; s < MAX_STAGES; ++s) last_issued[s] = -1;
     bool ok = true;
     bool x_issued = false;
-    int s = 0;         // stage of tile t (t % S)
+    int s = 0;         // stage of step t (t % S)
     uint32_t cyc = 0;  // t / S
+    int end_t = -1;    // step of the end marker
+    // claimed global tiles (p.tctr): static tiles b, b + G, then tiles 2G + j
+    // claimed one atomic each, one step ahead of use
+    const int G = gridDim.x, T = (p.M + TR - 1) / TR;
+    const unsigned nclaims = (unsigned)(max(0, T - 2 * G) + G);  // each CTA fails once
+    bool have_claim = false;
+    unsigned claim = 0u;
     if (p.xstage && lane == 0)  // x into L2 while the previous kernel drains (a hint only)
       asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p.x), "r"((uint32_t)K * 4u)
                    : "memory");
-    for (int t = 0; t < ntiles + S && ok; ++t) {
+    for (int t = 0; ok && (end_t < 0 || t < end_t + S); ++t) {
       // Tile 0 (weights only) is prefetched before the dependency wait, the
       // rest after it.  One tile, not the whole ring: x is loaded right after
       // the wait, and a CTA that starts late (its SM freed at the end of the
@@ -628,40 +651,84 @@ k_gemv_tma(const TmaArgs p) {
           x_issued = true;
         }
       }
-      if (x_issued && t == S - 1 && t < ntiles) {
+      // the tile of step t: first row r0 and rows nr (nr == 0: no more)
+      int r0 = 0, nr = 0;
+      if (end_t < 0) {
+        if (p.tctr == nullptr) {
+          r0 = a + t * TR;
+          nr = t < ntiles ? min(TR, nrows - t * TR) : 0;
+        } else {
+          if (lane == 0) {
+            int k = t < 2 ? (int)blockIdx.x + t * G : T;
+            if (k >= T) {
+              // claims start after the dependency wait (t >= 1): the previous
+              // launch on this counter has then reset it
+              const unsigned tk = have_claim ? claim : atomicAdd(p.tctr, 1u);
+              have_claim = false;
+              if (tk == nclaims - 1u) atomicExch(p.tctr, 0u);  // the launch's last claim
+              k = 2 * G + (int)tk;
+            }
+            r0 = k * TR;
+            nr = k < T ? min(TR, p.M - r0) : 0;
+          }
+          r0 = __shfl_sync(0xffffffffu, r0, 0);
+          nr = __shfl_sync(0xffffffffu, nr, 0);
+        }
+      }
+      if (x_issued && t == S - 1 && nr > 0) {
         ok = __all_sync(0xffffffffu, mbar_wait(saddr(&xempty), 0u, &abort_flag));
         if (!ok) break;
       }
       if (t >= S) {
-        const int tt = t - S;  // tile whose stage is recycled now (cycle cyc - 1)
+        // the stage of step t - S (cycle cyc - 1) is released: write its rows of y;
         // every lane waits (acquire), since every lane reads the partials
         ok = __all_sync(0xffffffffu, mbar_wait(saddr(&empty[s]), (cyc - 1u) & 1u, &abort_flag));
         if (!ok) break;
-        const int r0 = tt * TR, nr = min(TR, nrows - r0);
+        const int fr0 = fin_r0[s], fnr = fin_nr[s];
         const float* ps = part + (size_t)s * TR * KS;
-        for (int i = lane; i < nr; i += 32) {
+        for (int i = lane; i < fnr; i += 32) {
           float v = 0.0f;
           for (int k = 0; k < KS; ++k) v += ps[i * KS + k];
-          p.y[a + r0 + i] = v;
-          for (int k = 0; k < p.f.npeer; ++k) p.f.peer_y[k][a + r0 + i] = v;  // NVLink stores
+          p.y[fr0 + i] = v;
+          for (int k = 0; k < p.f.npeer; ++k) p.f.peer_y[k][fr0 + i] = v;  // NVLink stores
         }
         __syncwarp();
+        fin_nr[s] = 0;
       }
-      if (t < ntiles) {
-        if (lane == 0) {
-          const int r0 = t * TR, nr = min(TR, nrows - r0);
-          const uint32_t qb = (uint32_t)nr * QB, db = (uint32_t)nr * DB;
-          const uint32_t bar = saddr(&full[s]);
-          uint8_t* st = sm + (size_t)s * STG;
-          asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar),
-                       "r"(qb + db)
-                       : "memory");
-          bulk_g2s(saddr(st), p.q + (int64_t)(a + r0) * QB, qb, bar);
-          if (!AOS)
-            bulk_g2s(saddr(st + (size_t)TR * QB),
-                     reinterpret_cast<const uint8_t*>(p.d) + (int64_t)(a + r0) * DB, db, bar);
+      if (end_t < 0) {
+        if (nr > 0) {
+          if (lane == 0) {
+            const uint32_t qb = (uint32_t)nr * QB, db = (uint32_t)nr * DB;
+            const uint32_t bar = saddr(&full[s]);
+            uint8_t* st = sm + (size_t)s * STG;
+            stage_nr[s] = nr;  // published by the arrive (release)
+            asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar),
+                         "r"(qb + db)
+                         : "memory");
+            bulk_g2s(saddr(st), p.q + (int64_t)r0 * QB, qb, bar);
+            if (!AOS)
+              bulk_g2s(saddr(st + (size_t)TR * QB),
+                       reinterpret_cast<const uint8_t*>(p.d) + (int64_t)r0 * DB, db, bar);
+            // claim the tile of step t + 1 now, so its latency overlaps the
+            // wait for a free stage (after the dependency wait only)
+            if (p.tctr != nullptr && t >= 1) {
+              claim = atomicAdd(p.tctr, 1u);
+              have_claim = true;
+            }
+          }
+          fin_r0[s] = r0;
+          fin_nr[s] = nr;
+          last_issued[s] = t;
+        } else {
+          // no more tiles: an empty stage ends the consumers' loop
+          if (lane == 0) {
+            stage_nr[s] = 0;
+            asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(saddr(&full[s]))
+                         : "memory");
+          }
+          fin_nr[s] = 0;
+          end_t = t;
         }
-        last_issued[s] = t;
       }
       if (++s == S) {
         s = 0;
@@ -796,12 +863,13 @@ k_gemv_tma(const TmaArgs p) {
     }
   }
 
-  int s = 0;         // stage of tile t
+  int s = 0;         // stage of the next tile
   uint32_t ph = 0u;  // its phase parity
-  for (int t = 0; t < ntiles; ++t) {
+  for (;;) {
     // every lane waits on the barrier, so the bulk-copied bytes are visible to it
     if (!__all_sync(0xffffffffu, mbar_wait(saddr(&full[s]), ph, &abort_flag))) break;
-    const int nr = min(TR, nrows - t * TR);
+    const int nr = *(volatile int*)&stage_nr[s];  // rows of this stage's tile (0: done)
+    if (nr <= 0) break;
     const uint8_t* st = sm + (size_t)s * STG;
     const uint8_t* sd = st + (size_t)TR * QB;
     float* ps = part + (size_t)s * TR * KS;
@@ -1275,7 +1343,12 @@ int launch_tma(const GemvCall& c, const DeviceInfo& dev, cudaStream_t st) {
   // the same moment), from 4096 to 98304 rows of K = 4096
   const int xstage = MODE != 0 && c.f.nranks == 0 && pl.S >= 3 && (int64_t)K * 4 <= stage_bytes;
   TmaArgs a{static_cast<const uint8_t*>(c.q), static_cast<const unsigned short*>(c.d), c.x, c.y,
-            M, K, pl.TR, pl.S, pl.KS, xstage, c.f};
+            M, K, pl.TR, pl.S, pl.KS, xstage,
+            // claimed tiles with two CTAs per SM (measured 2-5 % less per call
+            // at 12288-49152 rows, decode stack q4_0 -6 %); with one CTA per SM
+            // its lone producer stalls on the claims' latency (q8_0 98304 x 4096
+            // 65.3 -> 68.9 us), so those launches keep contiguous ranges
+            CONSUMERS < 16 ? tile_counter(dev.device, st) : nullptr, c.f};
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(grid);
   cfg.blockDim = dim3(tma_threads(CONSUMERS));
@@ -1292,6 +1365,68 @@ int launch_tma(const GemvCall& c, const DeviceInfo& dev, cudaStream_t st) {
 }
 
 }  // namespace
+
+// ------------------------------------------------------ tile counters
+// One counter per stream (by its unique stream id) and one per launch made
+// under stream capture (baked into the graph; replays of one executable
+// graph are ordered), from a fixed device array: no allocation.  A launch
+// claims tiles only after its dependency wait, when the previous launch
+// on the same counter has finished and reset it.  Without a free counter
+// the launch streams contiguous row ranges (static).
+namespace {
+constexpr int kTileCounters = 16384;
+__device__ unsigned g_tile_ctr[kTileCounters];
+struct CounterPool {
+  unsigned* base = nullptr;
+  std::map<unsigned long long, int> by_stream;
+  int next = 0;
+};
+std::mutex g_ctr_mu;
+CounterPool g_ctr_pool[64];
+}  // namespace
+
+unsigned* tile_counter(int device, cudaStream_t st) {
+  if (device < 0 || device >= 64) return nullptr;
+  cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+  if (cudaStreamIsCapturing(st, &cs) != cudaSuccess) {
+    cudaGetLastError();  // not sticky; the launch itself reports real errors
+    return nullptr;
+  }
+  unsigned long long id = 0;
+  if (cs == cudaStreamCaptureStatusNone && cudaStreamGetId(st, &id) != cudaSuccess) {
+    cudaGetLastError();
+    return nullptr;
+  }
+  std::lock_guard<std::mutex> lk(g_ctr_mu);
+  CounterPool& pool = g_ctr_pool[device];
+  if (!pool.base) {
+    if (cs != cudaStreamCaptureStatusNone) return nullptr;  // set up outside capture
+    void* b = nullptr;
+    if (cudaGetSymbolAddress(&b, g_tile_ctr) != cudaSuccess || !b) {
+      cudaGetLastError();
+      return nullptr;
+    }
+    pool.base = static_cast<unsigned*>(b);
+  }
+  if (cs == cudaStreamCaptureStatusNone) {
+    auto it = pool.by_stream.find(id);
+    if (it != pool.by_stream.end()) return pool.base + it->second;
+    if (pool.next >= kTileCounters) return nullptr;
+    pool.by_stream[id] = pool.next;
+    return pool.base + pool.next++;
+  }
+  if (pool.next >= kTileCounters) return nullptr;
+  return pool.base + pool.next++;
+}
+
+// After a timeout a launch may leave its counter non-zero: zero them all.
+int reset_tile_counters(cudaStream_t st) {
+  static const unsigned zeros[kTileCounters] = {};
+  const cudaError_t e =
+      cudaMemcpyToSymbolAsync(g_tile_ctr, zeros, sizeof(zeros), 0, cudaMemcpyHostToDevice, st);
+  if (e == cudaSuccess) return OK;
+  return set_error(ERR_CUDA, "resetting the tile counters: %s", cudaGetErrorString(e));
+}
 
 bool tma_eligible(const GemvCall& c) {
   return c.N == 1 && c.K >= 256 && c.K % 256 == 0 && c.K <= 16384 && c.M >= 1 &&
@@ -1522,6 +1657,7 @@ int read_device_error(int clear, cudaStream_t st, int* out) {
   if (e != cudaSuccess) return set_error(ERR_CUDA, "reading the device error word: %s", cudaGetErrorString(e));
   if (clear && v) {
     const int zero = 0;
+    if (int rc = reset_tile_counters(st)) return rc;
     e = cudaMemcpyToSymbolAsync(g_device_error, &zero, sizeof(int), 0, cudaMemcpyHostToDevice, st);
     if (e == cudaSuccess) e = cudaStreamSynchronize(st);
     if (e != cudaSuccess) return set_error(ERR_CUDA, "clearing the device error word: %s", cudaGetErrorString(e));
