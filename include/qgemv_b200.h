@@ -93,7 +93,19 @@ QGEMV_API int qgemv_q8_0_soa(const void* q, const void* d, const float* x, float
 /* q4_0 SoA GEMV.  Replaces qgemv_q4_v5_soa_smem (best), qgemv_q4_v3_soa_vec and
  * qgemv_q4_v6_fastunpack (src/qgemv_kernels.cuh:228-254, 323-352, 373-414;
  * launches src/bench.cu:430-440).  The v6 kernel also took per-block sums of
- * x (src/bench.cu:341-349); no such input is needed here.  q: uint8 [M][K/2]. */
+ * x (src/bench.cu:341-349); no such input is needed here.  q: uint8 [M][K/2].
+ *
+ * Single-column calls on matrices that the kernel runs with two CTAs per SM
+ * share the rows out at run time through a tile counter (a fixed device array
+ * inside the library, no allocation): one counter per stream, keyed by the
+ * stream's unique id, and a fresh one for each call made under stream capture.
+ * Calls on one stream are ordered and calls on different streams use
+ * different counters; a captured graph must not be replayed concurrently
+ * with itself on two streams (CUDA orders launches of one executable graph).
+ * The first call on a device looks up the array's address; make it outside
+ * stream capture (a call captured before that streams contiguous row ranges,
+ * with the same results).  qgemv_check_device_error(clear = 1) zeroes the
+ * counters after a timeout. */
 QGEMV_API int qgemv_q4_0_soa(const void* q, const void* d, const float* x, float* y,
                              int64_t M, int64_t K, int32_t ncols, int64_t ldx, int64_t ldy,
                              void* stream);
