@@ -100,8 +100,9 @@ QGEMV_API int qgemv_q8_0_soa(const void* q, const void* d, const float* x, float
  * inside the library, no allocation): one counter per stream, keyed by the
  * stream's unique id, and a fresh one for each call made under stream capture.
  * Calls on one stream are ordered and calls on different streams use
- * different counters; a captured graph must not be replayed concurrently
- * with itself on two streams (CUDA orders launches of one executable graph).
+ * different counters; launches of one executable graph are ordered by CUDA,
+ * but two executable graphs instantiated from the same capture share its
+ * counters: replay those one at a time.
  * The first call on a device looks up the array's address; make it outside
  * stream capture (a call captured before that streams contiguous row ranges,
  * with the same results).  qgemv_check_device_error(clear = 1) zeroes the
