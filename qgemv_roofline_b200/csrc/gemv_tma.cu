@@ -1347,8 +1347,12 @@ int launch_tma(const GemvCall& c, const DeviceInfo& dev, cudaStream_t st) {
             // claimed tiles with two CTAs per SM (measured 2-5 % less per call
             // at 12288-49152 rows, decode stack q4_0 -6 %); with one CTA per SM
             // its lone producer stalls on the claims' latency (q8_0 98304 x 4096
-            // 65.3 -> 68.9 us), so those launches keep contiguous ranges
-            CONSUMERS < 16 ? tile_counter(dev.device, st) : nullptr, c.f};
+            // 65.3 -> 68.9 us), so those launches keep contiguous ranges.  A grid
+            // forced above the tile count (qgemv_soa_variant) is static too: a
+            // CTA without a first tile would claim before its dependency wait.
+            CONSUMERS < 16 && grid <= (M + pl.TR - 1) / pl.TR ? tile_counter(dev.device, st)
+                                                             : nullptr,
+            c.f};
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(grid);
   cfg.blockDim = dim3(tma_threads(CONSUMERS));
