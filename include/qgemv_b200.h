@@ -105,7 +105,12 @@ QGEMV_API int qgemv_q8_0_soa(const void* q, const void* d, const float* x, float
  * counters: replay those one at a time.
  * The first call on a device looks up the array's address; make it outside
  * stream capture (a call captured before that streams contiguous row ranges,
- * with the same results).  qgemv_check_device_error(clear = 1) zeroes the
+ * with the same results).  The pool holds 16384 counters per device; counters
+ * are never returned (a stream keeps its counter, a captured call keeps its
+ * counter for the life of the process), so a process that captures many
+ * graphs can use them all: later calls then stream contiguous row ranges,
+ * with the same results and 2-5 % slower.  qgemv_tile_counters_used() reports
+ * how many are taken.  qgemv_check_device_error(clear = 1) zeroes the
  * counters after a timeout. */
 QGEMV_API int qgemv_q4_0_soa(const void* q, const void* d, const float* x, float* y,
                              int64_t M, int64_t K, int32_t ncols, int64_t ldx, int64_t ldy,
@@ -161,10 +166,13 @@ QGEMV_API int qgemv_release_workspaces(void);
  * K = 32256 at 16 columns) fail with QGEMV_ERR_UNSUPPORTED before anything
  * is launched.  The first call on a device looks up the array's address
  * (cudaGetSymbolAddress) and caches it; make that call before any stream
- * capture.  Nothing in the array needs to start at zero.  The array is
- * shared: calls that overlap in time on one device (two streams or two
- * threads) race on it; calls on one stream are ordered and safe.  No
- * counterpart in the reference. */
+ * capture.  The cached address assumes the device's primary context lives
+ * as long as the process: after cudaDeviceReset the array moves, so a caller
+ * that resets a device must not call this entry point on it again.  Nothing
+ * in the array needs to start at zero.  The array is shared: calls that
+ * overlap in time on one device (two streams or two threads) race on it;
+ * calls on one stream are ordered and safe.  No counterpart in the
+ * reference. */
 QGEMV_API int qgemv_soa_static_ws(int format, const void* q, const void* d, const float* x,
                                   float* y, int64_t M, int64_t K, int32_t ncols, int64_t ldx,
                                   int64_t ldy, void* stream);
@@ -210,6 +218,11 @@ QGEMV_API int qgemv_stack_destroy(void* handle);
  * waits are bounded (~1 s; QGEMV_ERR_TIMEOUT in qgemv_check_device_error).
  * Buffers and counters must be mapped on every rank (e.g. symmetric memory);
  * counters start at zero; cta_count is a zeroed local counter per call site.
+ * A call that times out (or any call while this device's error word is set)
+ * sends no signal, so the other ranks time out in their own waits instead of
+ * reading an incomplete slice; to recover, clear the error word on every rank
+ * (qgemv_check_device_error(1, ...)) and zero every counter, cta_count and
+ * tok before the next token.
  * Replaces the NCCL all-gather after a GEMV (the reference was single-GPU). */
 #define QGEMV_MAX_RANKS 8
 typedef struct qgemv_fuse {
@@ -275,11 +288,27 @@ QGEMV_API int qgemv_soa_variant(int format, int variant, int32_t grid, const voi
                                 void* stream);
 
 /* Device-side error word of the current device: kernels whose waits are
- * bounded (the TMA-fed GEMV, whose mbarrier waits give up after ~1 s) record
- * QGEMV_ERR_TIMEOUT there instead of hanging.  Returns QGEMV_OK when it is
- * clear, else the recorded status; clear = 1 resets it.  Synchronises
- * `stream`. */
+ * bounded (the TMA-fed and tensor-core GEMVs, the fused all-gather, the
+ * persistent stack and the token fence, which give up after the wait limit)
+ * record QGEMV_ERR_TIMEOUT there instead of hanging.  Returns QGEMV_OK when
+ * it is clear, else the recorded status; clear = 1 resets it and the tile
+ * counters, after waiting until the whole device is idle (no other thread may
+ * launch work on the device meanwhile).  Synchronises `stream`.  The
+ * reference had no device-side error path: its harness exits on any CUDA
+ * error (src/bench.cu:19-27). */
 QGEMV_API int qgemv_check_device_error(int clear, void* stream);
+
+/* Limit of every bounded device-side wait on the current device, in
+ * microseconds at the device's maximum SM clock (converted to clock64
+ * cycles, so a wait at a lower clock lasts longer); <= 0 restores the
+ * default of about 1 s.  Takes effect for kernels launched afterwards.
+ * Synchronous; call it outside stream capture. */
+QGEMV_API int qgemv_set_wait_limit(int64_t microseconds);
+
+/* Tile counters (see qgemv_q4_0_soa) handed out on `device` so far, and the
+ * size of the pool; -1 for a device index out of range. */
+QGEMV_API int32_t qgemv_tile_counters_used(int device);
+QGEMV_API int32_t qgemv_tile_counters_capacity(void);
 
 /* ------------------------------------------------------- quantize / repack --- */
 

@@ -16,7 +16,9 @@ It restates, in numpy, the reference's algorithm for the path:
   ``d = mx / -8``, ``id = 1/d`` when ``d != 0`` else 0,
   ``q = clamp(trunc(fp32(fp32(w * id) + 8.5)), 0, 15)`` (two roundings, no
   fused multiply-add), packed byte ``i`` of a block = ``q[i] | q[i+16] << 4``.
-* ``dequant_q8_0`` / ``dequant_q4_0`` follow python/qformats.py:43-56.
+* ``dequant_q8_0`` / ``dequant_q4_0`` follow python/qformats.py:43-56
+  (``dequant_torch`` restates them in torch on the CPU, the reference's own
+  CPU GEMV path, for the timed CPU baseline only).
 * ``matvec_ref``      is the float64 dequant-matvec of src/bench.cu:75-111,
   the ground truth every kernel is checked against.
 * ``check_rowwise`` / ``check_gate`` are the two tolerances: the per-row
@@ -253,6 +255,24 @@ def block_bytes(fmt: str) -> int:
 def weight_bytes(fmt: str, M: int, K: int) -> int:
     """Bytes of a quantized [M, K] matrix: M*K*(34|18)/32."""
     return M * (K // QK) * block_bytes(fmt)
+
+
+def dequant_torch(fmt: str, q, d):
+    """The reference's CPU GEMV operand, ``dequant_q8_0 / dequant_q4_0`` of
+    python/qformats.py:43-56, restated with torch CPU tensors (fp32): the
+    quants times their block's fp16 scale, q4_0 nibbles (low -> j, high ->
+    j + 16) minus 8.  ``dequant_torch(fmt, q, d) @ x`` is the reference's CPU
+    path (python/triton_qgemv.py:135,154); used only as a timed baseline."""
+    import torch
+    q = torch.as_tensor(q)
+    d = torch.as_tensor(d)
+    M = q.shape[0]
+    if fmt == "q8_0":
+        w = q.reshape(M, -1, QK).to(torch.float32)
+    else:
+        b = q.reshape(M, -1, QK // 2)
+        w = torch.cat([b & 0x0F, b >> 4], dim=2).to(torch.float32) - 8.0
+    return (w * d.to(torch.float32).unsqueeze(2)).reshape(M, -1)
 
 
 def quantize(fmt: str, W: np.ndarray):

@@ -98,6 +98,9 @@ SIGNATURES = {
     "qgemv_soa_variant": ([ctypes.c_int, ctypes.c_int, _i32, _vp, _vp, _vp, _vp, _i64, _i64, _vp],
                           ctypes.c_int),
     "qgemv_check_device_error": ([ctypes.c_int, _vp], ctypes.c_int),
+    "qgemv_set_wait_limit": ([_i64], ctypes.c_int),
+    "qgemv_tile_counters_used": ([ctypes.c_int], _i32),
+    "qgemv_tile_counters_capacity": ([], _i32),
     "qgemv_soa_workspace_bytes": ([ctypes.c_int, _i64, _i64, _i32], ctypes.c_size_t),
     "qgemv_soa_ws": ([ctypes.c_int, _vp, _vp, _vp, _vp, _i64, _i64, _i32, _i64, _i64, _vp,
                       ctypes.c_size_t, _vp], ctypes.c_int),

@@ -5,7 +5,8 @@ from __future__ import annotations
 
 import shutil
 import subprocess
-import tempfile
+import threading
+import time
 
 QUERY = ("index,uuid,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
          "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
@@ -14,25 +15,56 @@ REASON_COLS = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_
 
 
 class ClockSampler:
-    """``with ClockSampler(uuid) as s: ...`` then ``s.summary()``."""
+    """``with ClockSampler(uuid) as s: ...`` then ``s.summary()``.
 
-    def __init__(self, uuid: str | None = None, period_ms: int = 100):
+    A reader thread collects the samples as nvidia-smi prints them, so
+    ``count()`` tells a caller whether the region seen so far has enough of
+    them (``keep_busy`` runs more work until it does)."""
+
+    def __init__(self, uuid: str | None = None, period_ms: int = 50):
         self.uuid = uuid
         self.period_ms = period_ms
         self.proc = None
-        self.out = None
         self.rows = []
+        self._lock = threading.Lock()
+        self._thread = None
 
     def __enter__(self):
         if shutil.which("nvidia-smi") is None:
             return self
-        self.out = tempfile.TemporaryFile(mode="w+")
         cmd = ["nvidia-smi", f"--query-gpu={QUERY}", "--format=csv,noheader,nounits",
                f"-lms={self.period_ms}"]
         if self.uuid:
             cmd.append(f"--id={self.uuid}")
-        self.proc = subprocess.Popen(cmd, stdout=self.out, stderr=subprocess.DEVNULL)
+        self.proc = subprocess.Popen(cmd, stdout=subprocess.PIPE, stderr=subprocess.DEVNULL,
+                                     text=True, bufsize=1)
+        self._thread = threading.Thread(target=self._read, daemon=True)
+        self._thread.start()
         return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) == 10:
+                with self._lock:
+                    self.rows.append(parts)
+
+    def count(self) -> int:
+        with self._lock:
+            return len(self.rows)
+
+    def keep_busy(self, work, min_samples: int = 5, max_seconds: float = 5.0) -> int:
+        """Runs ``work()`` (untimed, e.g. more calls of the timed workload)
+        until ``min_samples`` samples exist or ``max_seconds`` pass; returns
+        how many times it ran.  A timed region of a few milliseconds ends
+        before nvidia-smi prints its first sample."""
+        if self.proc is None:
+            return 0
+        n, t0 = 0, time.perf_counter()
+        while self.count() < min_samples and time.perf_counter() - t0 < max_seconds:
+            work()
+            n += 1
+        return n
 
     def __exit__(self, *exc):
         if self.proc is None:
@@ -42,21 +74,19 @@ class ClockSampler:
             self.proc.wait(timeout=5)
         except subprocess.TimeoutExpired:
             self.proc.kill()
-        self.out.seek(0)
-        for line in self.out.read().splitlines():
-            parts = [p.strip() for p in line.split(",")]
-            if len(parts) == 10:
-                self.rows.append(parts)
-        self.out.close()
+        if self._thread is not None:
+            self._thread.join(timeout=5)
         return False
 
     def summary(self) -> dict | None:
-        if not self.rows:
+        with self._lock:
+            rows = list(self.rows)
+        if not rows:
             return None
         sm = []
         mx = 0.0
         reasons = set()
-        for r in self.rows:
+        for r in rows:
             try:
                 sm.append(float(r[2]))
                 mx = max(mx, float(r[3]))

@@ -352,6 +352,25 @@ QGEMV_API int qgemv_check_device_error(int clear, void* stream) {
   return OK;
 }
 
+QGEMV_API int qgemv_set_wait_limit(int64_t microseconds) {
+  long long cycles = kDefaultSpinLimit;
+  if (microseconds > 0) {
+    int dev = 0, khz = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e == cudaSuccess) e = cudaDeviceGetAttribute(&khz, cudaDevAttrClockRate, dev);
+    if (e != cudaSuccess) return set_error(ERR_CUDA, "reading the SM clock: %s", cudaGetErrorString(e));
+    if (microseconds > (int64_t)1 << 40) return set_error(ERR_ARG, "wait limit too large");
+    cycles = (long long)microseconds * (khz > 0 ? khz : 2000000) / 1000;
+    if (cycles < 1) cycles = 1;
+  }
+  if (int rc = set_spin_limit(cycles)) return rc;
+  return set_mma_spin_limit(cycles);
+}
+
+QGEMV_API int32_t qgemv_tile_counters_used(int device) { return tile_counters_used(device); }
+
+QGEMV_API int32_t qgemv_tile_counters_capacity(void) { return tile_counters_capacity(); }
+
 QGEMV_API size_t qgemv_soa_workspace_bytes(int format, int64_t M, int64_t K, int32_t ncols) {
   if (check_fmt(format) || check_mk(M, K) || ncols < 2 || M == 0) return 0;
   GemvCall probe;

@@ -51,6 +51,9 @@
 namespace qg {
 
 __device__ int g_mma_error = 0;
+// Limit of every bounded wait of the kernels in this file, in clock64 cycles
+// (about 1 s by default); qgemv_set_wait_limit changes it per device.
+__device__ long long g_mma_spin_limit = 2000000000LL;
 
 namespace {
 
@@ -63,9 +66,11 @@ constexpr int HDR = 128;                    // workspace header: 2 floats per co
 constexpr int MAXC = 16;                    // columns per launch
 constexpr int MAX_STAGES = 48;
 constexpr int DST = TILE * (KC / QK) * 2;   // bytes of one tile's scales (512)
-constexpr long long SPIN_LIMIT = 2000000000LL;  // clock64 cycles, ~1 s
 
 // ------------------------------------------------------------ PTX helpers
+// The current wait limit, read once per wait (only on its slow path).
+__device__ __forceinline__ long long spin_limit() { return *(volatile long long*)&g_mma_spin_limit; }
+
 __device__ __forceinline__ uint32_t saddr(const void* p) {
   return (uint32_t)__cvta_generic_to_shared(p);
 }
@@ -95,12 +100,13 @@ __device__ __forceinline__ bool mbar_test(uint32_t bar, uint32_t parity) {
 // Bounded wait; gives up early when another thread raised the abort flag.
 __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort_flag) {
   if (mbar_try(bar, parity)) return true;
-  const long long t0 = clock64();
+  const long long t0 = clock64(), lim = spin_limit();
   while (!mbar_try(bar, parity)) {
     if (*abort_flag) return false;
-    if (clock64() - t0 > SPIN_LIMIT) {
-      *abort_flag = 1;
+    if (clock64() - t0 > lim) {
       atomicExch(&g_mma_error, (int)ERR_TIMEOUT);
+      __threadfence();
+      *abort_flag = 1;
       return false;
     }
   }
@@ -108,8 +114,8 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatil
 }
 
 __device__ __forceinline__ void mbar_wait_drain(uint32_t bar, uint32_t parity) {
-  const long long t0 = clock64();
-  while (!mbar_try(bar, parity) && clock64() - t0 < SPIN_LIMIT) {
+  const long long t0 = clock64(), lim = spin_limit();
+  while (!mbar_try(bar, parity) && clock64() - t0 < lim) {
   }
 }
 
@@ -125,12 +131,13 @@ __device__ __forceinline__ uint32_t ld_acquire(uint32_t addr) {
 // Bounded wait until a ring slot's tag names stage `g` (see the consumers).
 __device__ __forceinline__ bool tag_wait(uint32_t addr, uint32_t g, volatile int* abort_flag) {
   if (ld_acquire(addr) == g) return true;
-  const long long t0 = clock64();
+  const long long t0 = clock64(), lim = spin_limit();
   while (ld_acquire(addr) != g) {
     if (*abort_flag) return false;
-    if (clock64() - t0 > SPIN_LIMIT) {
-      *abort_flag = 1;
+    if (clock64() - t0 > lim) {
       atomicExch(&g_mma_error, (int)ERR_TIMEOUT);
+      __threadfence();
+      *abort_flag = 1;
       return false;
     }
   }
@@ -1279,6 +1286,12 @@ int tile_weights(int fmt, bool aos, const void* q, const void* d, int64_t M, int
 int gemv_tiled(int fmt, const GemvCall& c, cudaStream_t st) {
   if (int rc = check_ws(c)) return rc;
   return dispatch_mma<true>(fmt, c, st);
+}
+
+int set_mma_spin_limit(long long cycles) {
+  const cudaError_t e = cudaMemcpyToSymbol(g_mma_spin_limit, &cycles, sizeof(cycles));
+  if (e == cudaSuccess) return OK;
+  return set_error(ERR_CUDA, "setting the wait limit: %s", cudaGetErrorString(e));
 }
 
 int read_mma_error(int clear, cudaStream_t st, int* out) {

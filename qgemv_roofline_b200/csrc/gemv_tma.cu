@@ -54,6 +54,9 @@
 namespace qg {
 
 __device__ int g_device_error = 0;
+// Limit of every bounded wait of the kernels in this file, in clock64 cycles
+// (about 1 s by default); qgemv_set_wait_limit changes it per device.
+__device__ long long g_spin_limit = 2000000000LL;
 
 // The tile counter of a launch on stream st (device memory, no allocation),
 // or null when none is free; defined with the counter pool below.
@@ -69,7 +72,8 @@ constexpr int tma_threads(int cw) { return 32 * (cw + 1); }
 constexpr int tma_ctas_per_sm(int cw) { return cw >= 16 ? 1 : 16 / cw; }
 constexpr int MAX_STAGES = 8;
 constexpr int kPrefetchTiles = 1;  // weight tiles issued before the dependency wait (<= S - 1)
-constexpr long long SPIN_LIMIT = 2000000000LL;  // clock64 cycles, ~1 s
+// The current wait limit, read once per wait (only on its slow path).
+__device__ __forceinline__ long long spin_limit() { return *(volatile long long*)&g_spin_limit; }
 
 __device__ __forceinline__ uint32_t saddr(const void* p) {
   return (uint32_t)__cvta_generic_to_shared(p);
@@ -111,12 +115,15 @@ __device__ __forceinline__ bool mbar_try_sleep(uint32_t bar, uint32_t parity) {
 // Bounded wait; gives up early when another thread raised the abort flag.
 __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort_flag) {
   if (mbar_try_sleep(bar, parity)) return true;
-  const long long t0 = clock64();
+  const long long t0 = clock64(), lim = spin_limit();
   while (!mbar_try_sleep(bar, parity)) {
     if (*abort_flag) return false;
-    if (clock64() - t0 > SPIN_LIMIT) {
-      *abort_flag = 1;
+    if (clock64() - t0 > lim) {
+      // the error word first, then the CTA's abort flag: whoever sees the
+      // flag (and fences) also sees the error word
       atomicExch(&g_device_error, (int)ERR_TIMEOUT);
+      __threadfence();
+      *abort_flag = 1;
       return false;
     }
   }
@@ -124,8 +131,8 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatil
 }
 
 __device__ __forceinline__ void mbar_wait_drain(uint32_t bar, uint32_t parity) {
-  const long long t0 = clock64();
-  while (!mbar_try(bar, parity) && clock64() - t0 < SPIN_LIMIT) {
+  const long long t0 = clock64(), lim = spin_limit();
+  while (!mbar_try(bar, parity) && clock64() - t0 < lim) {
   }
 }
 
@@ -526,15 +533,16 @@ __device__ __forceinline__ void red_release_sys(unsigned* p, unsigned v) {
   asm volatile("red.release.sys.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
 
-// Bounded wait (~1 s) until the counter at `c` reaches `target` (mod 2^32).
+// Bounded wait until the counter at `c` reaches `target` (mod 2^32).
 __device__ __forceinline__ bool wait_count(const unsigned* c, unsigned target,
                                            volatile int* abort_flag) {
-  const long long t0 = clock64();
+  const long long t0 = clock64(), lim = spin_limit();
   while ((int)(ld_acquire_sys(c) - target) < 0) {
     if (abort_flag && *abort_flag) return false;
-    if (clock64() - t0 > SPIN_LIMIT) {
-      if (abort_flag) *abort_flag = 1;
+    if (clock64() - t0 > lim) {
       atomicExch(&g_device_error, (int)ERR_TIMEOUT);
+      __threadfence();
+      if (abort_flag) *abort_flag = 1;
       return false;
     }
   }
@@ -745,14 +753,20 @@ k_gemv_tma(const TmaArgs p) {
     if (p.f.nranks > 0) {
       // The CTA that finishes last tells every rank that this rank's slice of
       // y is in its buffer: each CTA orders its stores (system scope) before
-      // its count; the last one orders all of them before the signals.
+      // its count; the last one orders all of them before the signals.  Every
+      // CTA counts, aborted or not, so the count stays a multiple of the grid
+      // per launch.  A launch that timed out (any CTA of it, or any kernel
+      // since the error word was last cleared) sends no signal: the other
+      // ranks then time out in their own bounded waits and report it too,
+      // instead of reading a slice that was never completely written.
       __threadfence_system();
       __syncwarp();
       if (lane == 0) {
         const unsigned old = atomicAdd(p.f.cta_count, 1u);
         if (old % gridDim.x == gridDim.x - 1) {
           __threadfence_system();
-          for (int k = 0; k < p.f.nranks; ++k) red_release_sys(p.f.sig_out[k], 1u);
+          if (*(volatile int*)&g_device_error == 0)
+            for (int k = 0; k < p.f.nranks; ++k) red_release_sys(p.f.sig_out[k], 1u);
         }
       }
     }
@@ -833,12 +847,12 @@ k_gemv_tma(const TmaArgs p) {
           asm volatile("st.release.cta.shared::cta.u32 [%0], %1;" ::"r"(saddr(&x_ready)), "r"(1u)
                        : "memory");
       }
-      const long long t0 = clock64();
+      const long long t0 = clock64(), lim = 2 * spin_limit();
       for (;;) {
         uint32_t r;
         asm volatile("ld.acquire.cta.shared::cta.u32 %0, [%1];" : "=r"(r) : "r"(saddr(&x_ready))
                      : "memory");
-        if (r || abort_flag || clock64() - t0 > 2 * SPIN_LIMIT) break;
+        if (r || abort_flag || clock64() - t0 > lim) break;
       }
     }
     if (MODE == 2) {
@@ -1021,17 +1035,20 @@ __device__ __forceinline__ unsigned ld_acquire_gpu(const unsigned* p) {
   return v;
 }
 
-// Bounded wait (~1 s) for a grid-wide counter of this device, polling with a
-// short sleep so the CTAs that increment it are not slowed by the polls.
+// Bounded wait for a grid-wide counter of this device, polling with a short
+// sleep so the CTAs that increment it are not slowed by the polls.
 __device__ __forceinline__ bool wait_grid(const unsigned* c, unsigned target,
                                           volatile int* abort_flag) {
   if ((int)(ld_acquire_gpu(c) - target) >= 0) return true;
-  const long long t0 = clock64();
+  const long long t0 = clock64(), lim = spin_limit();
   while ((int)(ld_acquire_gpu(c) - target) < 0) {
     if (*abort_flag) return false;
-    if (clock64() - t0 > SPIN_LIMIT) {
-      *abort_flag = 1;
+    if (clock64() - t0 > lim) {
+      // the error word first, then the CTA's abort flag: whoever sees the
+      // flag (and fences) also sees the error word
       atomicExch(&g_device_error, (int)ERR_TIMEOUT);
+      __threadfence();
+      *abort_flag = 1;
       return false;
     }
     __nanosleep(64);
@@ -1653,6 +1670,20 @@ int stack_destroy(void* handle) {
   return OK;
 }
 
+int set_spin_limit(long long cycles) {
+  const cudaError_t e = cudaMemcpyToSymbol(g_spin_limit, &cycles, sizeof(cycles));
+  if (e == cudaSuccess) return OK;
+  return set_error(ERR_CUDA, "setting the wait limit: %s", cudaGetErrorString(e));
+}
+
+int tile_counters_used(int device) {
+  if (device < 0 || device >= 64) return -1;
+  std::lock_guard<std::mutex> lk(g_ctr_mu);
+  return g_ctr_pool[device].next;
+}
+
+int tile_counters_capacity() { return kTileCounters; }
+
 int read_device_error(int clear, cudaStream_t st, int* out) {
   int v = 0;
   cudaError_t e = cudaMemcpyFromSymbolAsync(&v, g_device_error, sizeof(int), 0,
@@ -1660,6 +1691,12 @@ int read_device_error(int clear, cudaStream_t st, int* out) {
   if (e == cudaSuccess) e = cudaStreamSynchronize(st);
   if (e != cudaSuccess) return set_error(ERR_CUDA, "reading the device error word: %s", cudaGetErrorString(e));
   if (clear && v) {
+    // A launch that timed out may have left its tile counter non-zero; a
+    // launch still running on another stream is using its own.  Wait until
+    // the device is idle, then zero them all (clearing needs an idle device:
+    // no other thread may launch work meanwhile).
+    e = cudaDeviceSynchronize();
+    if (e != cudaSuccess) return set_error(ERR_CUDA, "waiting for the device: %s", cudaGetErrorString(e));
     const int zero = 0;
     if (int rc = reset_tile_counters(st)) return rc;
     e = cudaMemcpyToSymbolAsync(g_device_error, &zero, sizeof(int), 0, cudaMemcpyHostToDevice, st);

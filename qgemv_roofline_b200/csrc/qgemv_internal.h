@@ -90,6 +90,15 @@ int gemv_soa_mma(int fmt, const GemvCall& c, cudaStream_t st);
 bool mma_eligible(const GemvCall& c);
 size_t mma_workspace_bytes(int64_t K, int N);
 int read_mma_error(int clear, cudaStream_t st, int* out);
+// Limits (clock64 cycles) of the bounded waits in the kernels of gemv_tma.cu
+// and gemv_mma.cu, on the current device.
+int set_spin_limit(long long cycles);
+int set_mma_spin_limit(long long cycles);
+constexpr long long kDefaultSpinLimit = 2000000000LL;  // ~1 s at ~2 GHz
+// Tile counters handed out on `device` so far (one per stream that launched,
+// one per captured launch; never returned) and the pool's size.
+int tile_counters_used(int device);
+int tile_counters_capacity();
 // Batch tiles: the weights re-laid for the tensor-core kernel (one contiguous
 // block per 16 rows x 512 columns); any K % 32 == 0.
 size_t tiled_bytes(int fmt, int64_t M, int64_t K);

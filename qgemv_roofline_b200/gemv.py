@@ -52,6 +52,28 @@ def _xy(x: torch.Tensor, M: int, K: int, y: torch.Tensor | None, device):
     return X, Y, y, N, ldx, ldy
 
 
+# Workspaces of the batched calls, one per (device, torch stream), grown on
+# demand: calls on one stream are ordered, so they may share it.
+_WS: dict = {}
+
+
+def _workspace(device, nbytes: int, stream) -> torch.Tensor:
+    """A device buffer of at least ``nbytes`` for a call on the current torch
+    stream (``stream`` None).  Under stream capture, or for a raw stream
+    handle, a fresh buffer from torch's caching allocator (stream-ordered; a
+    captured graph keeps its own)."""
+    nbytes = max(int(nbytes), 16)
+    cur = torch.cuda.current_stream(device)
+    if stream is not None or torch.cuda.is_current_stream_capturing():
+        return torch.empty(nbytes, dtype=torch.uint8, device=device)
+    key = (device.index, cur.stream_id, cur.cuda_stream)
+    ws = _WS.get(key)
+    if ws is None or ws.numel() < nbytes:
+        ws = torch.empty(nbytes, dtype=torch.uint8, device=device)
+        _WS[key] = ws
+    return ws
+
+
 def _check_act(activations: str, N: int):
     if activations not in ("exact", "q8_1"):
         raise ValueError(f"activations must be 'exact' or 'q8_1', got {activations!r}")
@@ -85,11 +107,9 @@ def qgemv(fmt: str, q: torch.Tensor, d: torch.Tensor, x: torch.Tensor,
                   X.data_ptr(), Y.data_ptr(), M, K, st)
         return y
     if N >= 2:
-        # batched calls: the workspace comes from torch's caching allocator
-        # (stream-ordered, usable under CUDA graph capture)
         fid = 8 if fmt == "q8_0" else 4
         nbytes = _lib.lib().qgemv_soa_workspace_bytes(fid, M, K, N)
-        ws = torch.empty(max(nbytes, 1), dtype=torch.uint8, device=q.device)
+        ws = _workspace(q.device, nbytes, stream)
         _lib.call("qgemv_soa_ws", fid, q.data_ptr(), d.data_ptr(), X.data_ptr(), Y.data_ptr(),
                   M, K, N, ldx, ldy, ws.data_ptr(), nbytes, st)
         return y
@@ -158,7 +178,7 @@ def qgemv_tiled(fmt: str, tiled: torch.Tensor, M: int, K: int, x: torch.Tensor,
     X, Y, y, N, ldx, ldy = _xy(x, M, K, y, tiled.device)
     st = torch.cuda.current_stream(tiled.device).cuda_stream if stream is None else stream
     nbytes = _lib.lib().qgemv_tiled_workspace_bytes(K, N)
-    ws = torch.empty(max(nbytes, 16), dtype=torch.uint8, device=tiled.device)
+    ws = _workspace(tiled.device, nbytes, stream)
     _lib.call("qgemv_tiled_gemv", fid, tiled.data_ptr(), M, K, X.data_ptr(), Y.data_ptr(), N,
               ldx, ldy, ws.data_ptr(), ws.numel(), st)
     return y

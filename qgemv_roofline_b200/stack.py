@@ -239,6 +239,25 @@ class _FusedGather:
         self.done_local = self.sig.data_ptr() + 4 * n
         self.fid = _lib.FORMAT_CODE[st.fmt]
 
+    def reset(self):
+        """Recovery after a timed-out token (QGEMV_ERR_TIMEOUT): clears this
+        device's error word and zeroes the counters, the per-call CTA counts
+        and the token count on every rank (a collective: every rank calls it,
+        with no fused call in flight)."""
+        from . import _lib
+
+        st = self.st
+        group = st.group or dist.group.WORLD
+        torch.cuda.synchronize(st.device)
+        dist.barrier(group)
+        self.lib.qgemv_check_device_error(1, None)
+        self.sig.zero_()
+        self.cta.zero_()
+        self.tok.zero_()
+        torch.cuda.synchronize(st.device)
+        dist.barrier(group)
+        _lib.call("qgemv_check_device_error", 0, None)
+
     def forward(self, x, trace=None):
         """One token; returns this rank's full output buffer of the last GEMV
         (complete once the token fence has run)."""

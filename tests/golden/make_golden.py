@@ -1,7 +1,8 @@
 """Generate the golden q8_0 / q4_0 fixtures from the reference itself.
 
-Run in a checkout where the reference project is present (default
-/root/reference, override with QGEMV_REFERENCE):
+Run in a checkout where the reference project is present (by default the
+directory ``reference`` beside this repository's root; set QGEMV_REFERENCE to
+point elsewhere):
 
     python tests/golden/make_golden.py
 
@@ -31,7 +32,7 @@ import torch
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 REPO = os.path.dirname(os.path.dirname(HERE))
-REF = os.environ.get("QGEMV_REFERENCE", "/root/reference")
+REF = os.environ.get("QGEMV_REFERENCE", os.path.join(REPO, os.pardir, "reference"))
 sys.path.insert(0, os.path.join(REF, "python"))
 sys.path.insert(0, REPO)
 

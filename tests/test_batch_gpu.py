@@ -225,25 +225,6 @@ def test_graph_capture_python_api(fmt):
     check(fmt, q, d, X, Y.cpu().numpy())
 
 
-@pytest.mark.parametrize("fmt", ["q8_0", "q4_0"])
-def test_small_batch_decode_shape_spot_rows(fmt):
-    """28672 x 8192 with N = 16 (the small-batch decode shape): the oracle on
-    sampled rows, plus linearity in X."""
-    M, K, N = 28672, 8192, 16
-    gen = torch.Generator(device=DEV).manual_seed(4)
-    W = torch.randn(M, K, generator=gen, device=DEV) * 0.02
-    qt, dt = (qg.quantize_q8_0 if fmt == "q8_0" else qg.quantize_q4_0)(W)
-    del W
-    X = torch.randn(N, K, generator=gen, device=DEV)
-    Y = qg.qgemv(fmt, qt, dt, X)
-    rows = np.random.default_rng(0).choice(M, 96, replace=False)
-    rows = np.sort(np.concatenate([rows, [0, 15, 16, M - 17, M - 1]]))
-    check(fmt, qt[rows].cpu().numpy(), dt[rows].cpu().numpy().view(np.uint16).view(np.float16),
-          X.cpu().numpy(), Y[:, rows].cpu().numpy())
-    Y2 = qg.qgemv(fmt, qt, dt, 2.0 * X)
-    assert torch.equal(Y2, 2.0 * Y)   # power-of-two scaling is exact end to end
-
-
 # ------------------------------------------------------------ batch tiles
 def tiles_np(fmt, q, d, M, K):
     """numpy restatement of the batch-tile layout (qgemv_tile_weights)."""

@@ -65,6 +65,22 @@ def test_oracle_dequant_matches_reference_fp32_path(golden, fmt):
         assert ok, (name, rel)
 
 
+@pytest.mark.parametrize("fmt", ["q8_0", "q4_0"])
+def test_torch_cpu_dequant_matches_reference(golden, fmt):
+    """The torch restatement of the reference's CPU path (the timed CPU
+    baseline): dequantized weights equal the numpy oracle's bit for bit, and
+    dequant(q, d) @ x agrees with the reference's own torch fp32 outputs."""
+    import torch
+    key = "8" if fmt == "q8_0" else "4"
+    for name, g in golden.items():
+        q, d = g["q" + key], g["d" + key].view(np.float16)
+        Wt = o.dequant_torch(fmt, torch.from_numpy(q), torch.from_numpy(d))
+        assert np.array_equal(Wt.numpy(), o.dequant(fmt, q, d)), name
+        y = (Wt @ torch.from_numpy(g["X"]).T).T.numpy()
+        ok, _, rel = o.check_gate(y, g["y%s_f32" % key], 1e-6)
+        assert ok, (name, rel)
+
+
 def test_reference_cpu_checks_on_oracle(golden):
     """tests/test_quant_cpu.py:59-110 of the reference, run on the oracle with
     the reference's own input (torch seed 1234, U(-1, 1), [64, 512])."""

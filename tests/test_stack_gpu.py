@@ -1,6 +1,7 @@
 """The decode layer stack on one GPU: every GEMV of a step against the
 float64 oracle (given the input that GEMV actually received), the CUDA-graph
-replay against the eager step, and the full 7B layer shapes on sampled rows."""
+replay against the eager step, the fused and persistent paths on one rank
+(every row of a full 7B layer is in test_full_rows_gpu.py)."""
 
 import numpy as np
 import pytest
@@ -48,17 +49,6 @@ def test_graph_replay_matches_eager(fmt):
     g.replay()
     torch.cuda.synchronize()
     assert torch.equal(out, y_eager)
-
-
-@pytest.mark.parametrize("fmt", ["q8_0", "q4_0"])
-def test_7b_layer_shapes_spot_rows(fmt):
-    st = stack.DecodeStack.from_random(fmt, n_layers=1, seed=5, device="cuda", keep_full=True)
-    x = torch.randn(4096, device="cuda")
-    trace = []
-    st(x, trace=trace)
-    rows = np.random.default_rng(0).choice(4096, 64, replace=False)
-    check_trace(fmt, st, trace, rows=np.sort(rows))
-    assert st.weight_bytes == stack.weight_bytes(fmt, n_layers=1)
 
 
 def _init_single_rank_group():
