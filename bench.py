@@ -3,17 +3,15 @@
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 
-Workload (the large, L2-safe configuration the headline target is quoted on):
-W [98304, 4096] ~ N(0, 0.02) fp32, quantized on the GPU to q8_0 and to q4_0
-(SoA planes), x fp32 [4096] ~ N(0, 1), batch 1.  One *step* = one q8_0 GEMV
-plus one q4_0 GEMV.  With N GPUs (one process per GPU, torchrun) the rows of a
-[N * 98304, 4096] matrix are sharded: rank g owns rows [g*98304, (g+1)*98304)
-of both formats, resident in its HBM; x is replicated; the step needs no
-collective.  Work per GPU is fixed as N grows ("weak" scaling, the default;
-rows are independent, so the path partitions).  Beside it, under N > 1, the
-line reports the same 98304-row matrix sharded N ways (98304 / N rows per
-rank, "row_sharded_fixed_M": total work fixed) and an NCCL all-gather of y,
-each timed separately.  --scaling strong makes the fixed-M sharding the value.
+Workload of the headline value (the large, L2-safe configuration the target is
+quoted on): W [98304, 4096] ~ N(0, 0.02) fp32, quantized on the GPU to q8_0 and
+to q4_0 (SoA planes), x fp32 [4096] ~ N(0, 1), batch 1.  One *step* = one q8_0
+GEMV plus one q4_0 GEMV.  With N GPUs (one process per GPU, torchrun) the rows
+of a [N * 98304, 4096] matrix are sharded: rank g owns rows [g*98304,
+(g+1)*98304) of both formats, resident in its HBM; x is replicated; the step
+needs no collective.  Work per GPU is fixed as N grows ("weak" scaling, the
+default; rows are independent, so the path partitions).  --scaling strong
+makes the 98304-row matrix sharded N ways the value.
 
 Every rank keeps C_f copies of each format's weight slice and call i of that
 format reads copy i % C_f, with C_f chosen so that the bytes streamed between
@@ -26,8 +24,13 @@ launch's tail the way a caller's stream of GEMVs does.
 Printed (rank 0, one JSON line): the whole-job algorithmic GB/s (weights
 M*K*(34|18)/32 + x 4*K + y 4*M per call) over the max-over-ranks device time
 of the K timed steps, with the roofline of the dominant kernel, the CPU
-baseline, the end-to-end figure through the public API with host buffers, and
-the SM clocks sampled during the timed region.
+baselines, the end-to-end figure through the public API with host buffers,
+and the SM clocks sampled during the timed region; beside it (not the value):
+the headline shape timed in three sessions (fresh weight copies each) with
+their spread, and every other configuration of the benchmark set, rows
+sharded over the N GPUs -- S 4096x4096 and L 11008x4096 (one column), SB
+28672x8192 with 1..16 columns, the 98304x4096 matrix itself sharded N ways
+with the all-gather of its y, and the 32-layer 7B decode stack (us/token).
 """
 
 from __future__ import annotations
@@ -75,7 +78,23 @@ def parse():
     ap.add_argument("--fused", action="store_true",
                     help="stack workload: all-gather inside the GEMV kernels (peer stores, "
                          "symmetric memory) instead of NCCL")
+    ap.add_argument("--stack-mode", choices=["auto", "persistent", "plain", "fused"], default="auto",
+                    help="decode stack: one persistent launch per token (rows stored into every "
+                         "rank's buffer by the kernel), one launch per GEMV with NCCL all-gathers "
+                         "(plain), or one launch per GEMV storing into the peers (fused); auto "
+                         "(default) = plain on one GPU, persistent on several")
+    ap.add_argument("--no-configs", action="store_true",
+                    help="skip the records of the other configurations (S, L, SB, stack, "
+                         "sessions)")
+    ap.add_argument("--sessions", type=int, default=3,
+                    help="timed sessions of the headline shape (fresh weight copies each)")
     args = ap.parse_args()
+    if args.fused:
+        args.stack_mode = "fused"
+    if args.persistent:
+        args.stack_mode = "persistent"
+    if args.stack_mode == "auto":
+        args.stack_mode = "persistent" if int(os.environ.get("WORLD_SIZE", "1")) > 1 else "plain"
     if args.workload != "xl" and args.steps == 20000:
         args.steps = 30 if args.workload == "stack" else 200
     return args
@@ -87,6 +106,12 @@ def wbytes(fmt, M, K):
 
 def alg_bytes(fmt, M, K, N=1):
     return wbytes(fmt, M, K) + 4 * K * N + 4 * M * N
+
+
+def xl_copies(rows, K):
+    """Rotated weight copies per format of the headline shape: >= 4x L2
+    streamed between two reads of one copy."""
+    return {f: max(2, math.ceil(4 * L2_BYTES / wbytes(f, rows, K))) for f in ("q8_0", "q4_0")}
 
 
 def workload_config(args, world, rows, copies=None):
@@ -149,54 +174,73 @@ def _timed(torch, dist, dev, world, fn, warmup, steps):
     return t.item()
 
 
-def stack_workload(args, rank, world, dev):
+def _ensure_group(dev):
+    """The fused and persistent multi-rank paths address buffers through a
+    process group; on one GPU without torchrun, a group of one."""
+    import torch.distributed as dist
+    if dist.is_initialized():
+        return
+    import socket
+    sk = socket.socket()
+    sk.bind(("127.0.0.1", 0))
+    os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+    os.environ["MASTER_PORT"] = str(sk.getsockname()[1])
+    sk.close()
+    dist.init_process_group("nccl", rank=0, world_size=1, device_id=dev)
+
+
+def stack_records(args, rank, world, dev, mode, tokens, warmup):
     """32 decode layers x {QKV 12288x4096, O 4096x4096, gate+up 22016x4096,
-    down 4096x11008}, batch 1, q8_0 then q4_0; rows sharded over the ranks
-    with an NCCL all-gather of every y; one step = one token through all
-    layers, replayed from a CUDA graph."""
+    down 4096x11008}, batch 1, q8_0 then q4_0, rows sharded over the ranks;
+    one step = one token through all layers (a CUDA graph replay).  mode:
+    persistent (one launch per token, rows stored into every rank's buffer
+    by the kernel), plain (one launch per GEMV, NCCL all-gather of every y),
+    fused (one launch per GEMV storing into the peers).  Returns
+    {fmt: record}, total weight bytes per token of both formats, total ms."""
     import torch
     import torch.distributed as dist
 
-    import qgemv_roofline_b200 as qg
     from qgemv_roofline_b200 import stack
+
+    if mode == "fused" and world == 1:
+        _ensure_group(dev)
+    x = torch.randn(4096, generator=torch.Generator(device=dev).manual_seed(SEED), device=dev)
+    res, total_bytes, total_ms = {}, 0, 0.0
+    for fmt in ("q8_0", "q4_0"):
+        st = stack.DecodeStack.from_random(fmt, n_layers=args.layers, seed=SEED, device=dev,
+                                           fused=mode == "fused",
+                                           persistent=mode == "persistent")
+        g, out = st.capture(x)
+        ms = _timed(torch, dist, dev, world, g.replay, warmup, tokens)
+        per = ms / tokens
+        res[fmt] = {"us_per_token": per * 1e3, "weight_bytes": st.weight_bytes,
+                    "gbps_aggregate": st.weight_bytes / (per * 1e-3) / 1e9,
+                    "gemv_launches_per_token": 1 if mode == "persistent" else len(st.mats),
+                    "allgathers_per_token": len(st.mats) if (world > 1 and mode == "plain") else 0}
+        total_bytes += st.weight_bytes * tokens
+        total_ms += ms
+        del g, out, st  # graphs holding NCCL calls go before the process group
+        torch.cuda.synchronize(dev)
+        torch.cuda.empty_cache()
+    return res, total_bytes, total_ms
+
+
+STACK_MODES = {
+    "persistent": "one persistent launch per token per GPU; each GEMV's rows stored into every "
+                  "rank's buffer by the kernel (NVLink peer stores) and per-GEMV counters",
+    "plain": "one launch per GEMV, NCCL all-gather of every y",
+    "fused": "one launch per GEMV, rows stored into every rank's buffer by the kernel",
+}
+
+
+def stack_workload(args, rank, world, dev):
+    """The decode stack as the benchmark's value (--workload stack)."""
     from qgemv_roofline_b200.clocks import ClockSampler
 
-    res, graphs, total_bytes, total_ms = {}, [], 0, 0.0
-    if args.fused and not dist.is_initialized():
-        # the fused path addresses buffers through a process group, even of one
-        import socket
-        sk = socket.socket()
-        sk.bind(("127.0.0.1", 0))
-        os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
-        os.environ["MASTER_PORT"] = str(sk.getsockname()[1])
-        sk.close()
-        dist.init_process_group("nccl", rank=0, world_size=1, device_id=dev)
-    x = torch.randn(4096, generator=torch.Generator(device=dev).manual_seed(SEED), device=dev)
-    uuid = None
-    try:
-        uuid = str(torch.cuda.get_device_properties(dev).uuid)
-        uuid = uuid if uuid.startswith("GPU-") else "GPU-" + uuid
-    except Exception:
-        pass
+    uuid = _gpu_uuid(dev)
     with ClockSampler(uuid) as sampler:
-        for fmt in ("q8_0", "q4_0"):
-            st = stack.DecodeStack.from_random(fmt, n_layers=args.layers, seed=SEED, device=dev,
-                                               fused=args.fused,
-                                               persistent=args.persistent and world == 1)
-            g, out = st.capture(x)
-            graphs.append(g)
-            ms = _timed(torch, dist, dev, world, g.replay, args.warmup, args.steps)
-            per = ms / args.steps
-            res[fmt] = {"us_per_token": per * 1e3, "weight_bytes": st.weight_bytes,
-                        "gbps_aggregate": st.weight_bytes / (per * 1e-3) / 1e9,
-                        "gemv_launches_per_token": 1 if st.persistent is not None else len(st.mats),
-                        "allgathers_per_token": (0 if args.fused else len(st.mats))
-                        if world > 1 else 0}
-            total_bytes += st.weight_bytes * args.steps
-            total_ms += ms
-            del st, out
-            torch.cuda.empty_cache()
-    graphs.clear()  # graphs holding NCCL calls go before the process group
+        res, total_bytes, total_ms = stack_records(args, rank, world, dev, args.stack_mode,
+                                                   args.steps, args.warmup)
     value = total_bytes / (total_ms * 1e-3) / 1e9
     peak, note = measured_peak()
     if rank == 0:
@@ -207,12 +251,8 @@ def stack_workload(args, rank, world, dev):
                 "dtype": "fp32", "data": "synthetic (seeded N(0, 0.02) weights, N(0, 1) x)",
                 "config": {"workload": f"{args.layers} layers x (QKV 12288x4096, O 4096x4096, "
                                        f"gate+up 22016x4096, down 4096x11008), batch 1",
-                           "parallelism": (f"row-shard x{world} + " +
-                                           ("all-gather of every y inside the GEMV kernels "
-                                            "(peer stores, counters)" if args.fused else
-                                            "NCCL all-gather of every y"))
-                           if world > 1 else "single GPU" + (", fused path" if args.fused else "")
-                           + (", one persistent launch per token" if args.persistent else ""),
+                           "parallelism": (f"row-shard x{world}, " if world > 1 else "single GPU, ")
+                           + STACK_MODES[args.stack_mode],
                            "step": "one token through all layers, q8_0 stack then q4_0 stack, "
                                    "each a CUDA graph replay",
                            "l2": "inputs larger than L2 (3.6-6.9 GB of weights per stack)"},
@@ -224,9 +264,19 @@ def stack_workload(args, rank, world, dev):
     return 0
 
 
-def batch_workload(args, rank, world, dev):
-    """W [28672, 8192] (rows sharded) with X [N, 8192], N in 1..16, from SoA
-    planes and from batch tiles."""
+def _gpu_uuid(dev):
+    import torch
+    try:
+        u = str(torch.cuda.get_device_properties(dev).uuid)
+        return u if u.startswith("GPU-") else "GPU-" + u
+    except Exception:
+        return None
+
+
+def batch_records(args, rank, world, dev, steps, warmup):
+    """W [28672, 8192] (rows sharded) with X [N, 8192], N in 1..16, from batch
+    tiles (the fast path) and from SoA planes; weights rotated over >= 4x L2.
+    Returns a list of records (us per call, aggregate GB/s)."""
     import torch
     import torch.distributed as dist
 
@@ -267,14 +317,21 @@ def batch_workload(args, rank, world, dev):
                 _lib.call("qgemv_tiled_gemv", fid, t.data_ptr(), rows, K, X.data_ptr(),
                           Y.data_ptr(), N, K, rows, ws.data_ptr(), nb, sp)
 
-            for layout, fn in (("soa", soa_call), ("tiled", tiled_call)):
-                ms = _timed(torch, dist, dev, world, fn, args.warmup, args.steps)
-                per = ms / args.steps
+            for layout, fn in (("tiled", tiled_call), ("soa", soa_call)):
+                ms = _timed(torch, dist, dev, world, fn, warmup, steps)
+                per = ms / steps
                 b = alg_bytes(fmt, rows, K, N)
                 out.append({"fmt": fmt, "layout": layout, "N": N, "us_per_call": per * 1e3,
-                            "gbps_aggregate": world * b / (per * 1e-3) / 1e9})
+                            "gbps_aggregate": world * b / (per * 1e-3) / 1e9,
+                            "copies_rotated": copies})
         del soa, tiles, q, d
         torch.cuda.empty_cache()
+    return out
+
+
+def batch_workload(args, rank, world, dev):
+    """The small-batch shape as the benchmark's value (--workload batch)."""
+    out = batch_records(args, rank, world, dev, args.steps, args.warmup)
     if rank == 0:
         peak, note = measured_peak()
         print(json.dumps({"metric": "small-batch GEMV 28672x8192, N columns: GB/s",
@@ -284,9 +341,54 @@ def batch_workload(args, rank, world, dev):
                           "vs_baseline": None, "dtype": "fp32",
                           "data": "synthetic (seeded N(0, 0.02) weights, N(0, 1) X)",
                           "config": {"workload": "W [28672, 8192], X [N, 8192], N in 1..16",
-                                     "rows_per_gpu": rows, "l2": "rotated weight copies, >= 4x L2"},
+                                     "rows_per_gpu": 28672 // world,
+                                     "l2": "rotated weight copies, >= 4x L2"},
                           "peak": peak, "peak_note": note, "results": out}), flush=True)
     return 0
+
+
+def single_column_records(args, rank, world, dev, M, K, calls, read_roof, peak,
+                          min_copies=16):
+    """One q8_0 and one q4_0 GEMV of W [M, K] (rows sharded over the ranks, x
+    replicated), weights rotated over max(min_copies, >= 4x L2) copies;
+    `calls` timed calls per format.  us per call (max over ranks), aggregate
+    GB/s, and the per-GPU fraction of the read roof and of the measured peak."""
+    import torch
+    import torch.distributed as dist
+
+    import qgemv_roofline_b200 as qg
+    from qgemv_roofline_b200.timing import time_steps
+
+    rows = M * (rank + 1) // world - M * rank // world
+    g = torch.Generator(device=dev).manual_seed(SEED + 31 * M + 7919 * rank)
+    W = torch.randn(rows, K, generator=g, device=dev) * 0.02
+    x = torch.randn(K, generator=torch.Generator(device=dev).manual_seed(SEED), device=dev)
+    cl, copies = [], {}
+    for fmt in ("q8_0", "q4_0"):
+        c = max(min_copies, math.ceil(4 * L2_BYTES / wbytes(fmt, rows, K)))
+        q, d = (qg.quantize_q8_0 if fmt == "q8_0" else qg.quantize_q4_0)(W)
+        copies[fmt] = c
+        cl.append({"fmt": fmt, "layout": "soa", "M": rows, "K": K, "x": x,
+                   "y": torch.empty(rows, device=dev),
+                   "copies": [(q, d)] + [(q.clone(), d.clone()) for _ in range(c - 1)]})
+    del W
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize(dev)
+    _, per = time_steps(cl, 20, calls, grouped=True)
+    t = torch.tensor(per, dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    rec = {"M": M, "K": K, "rows_per_gpu": rows, "calls": calls}
+    for fmt, ms in zip(("q8_0", "q4_0"), t.tolist()):
+        us = ms / calls * 1e3
+        gb = alg_bytes(fmt, rows, K) / (us * 1e-6) / 1e9
+        rec[fmt] = {"us_per_call": us, "gbps_per_gpu": gb, "gbps_aggregate": world * gb,
+                    "frac_of_read_roof": gb / read_roof if read_roof else None,
+                    "frac_of_peak": gb / peak, "copies_rotated": copies[fmt]}
+    del cl
+    torch.cuda.empty_cache()
+    return rec
 
 
 # ----------------------------------------------------------------- reference arm
@@ -305,6 +407,9 @@ def reference_arm(args, rank, world):
 
     from oracle import qformats_oracle as o
     from oracle import ref_lib
+
+    # the same configuration as our arm's line
+    xl_rows = args.M if args.scaling == "weak" else args.M * (rank + 1) // world - args.M * rank // world
 
     cores = len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else os.cpu_count()
     rng = np.random.default_rng(SEED)
@@ -350,8 +455,7 @@ def reference_arm(args, rank, world):
         "ms_per_step": dt / args.steps * 1e3, "higher_is_better": True,
         "scaling": args.scaling, "vs_baseline": None, "dtype": "fp64" if have_ref else "fp32",
         "data": "synthetic (seeded)",
-        "config": workload_config(args, world,
-                                  args.M if args.scaling == "weak" else args.M // world),
+        "config": workload_config(args, world, xl_rows, xl_copies(xl_rows, args.K)),
         "cpu_baseline": {"value": value, "unit": "GB/s", "cores": cores, "kind": kind,
                          "sample": sample},
         "e2e": {"value": value, "unit": "GB/s", "h2d_bytes_per_step": 0,
@@ -414,6 +518,49 @@ def cpu_baseline(qg, mats, x, K, seconds):
                       if have_ref else "oracle restatement of dequant(q, d) @ x")),
         "us_per_step_full_shape_est": dt * 1e6 * M / rows,
     }
+
+
+def cpu_baseline_torch(mats, x, K, seconds):
+    """The reference's own CPU GEMV path, ``dequant_*(q, d) @ x`` in torch on
+    the host cores (python/qformats.py:43-56, as python/triton_qgemv.py:135
+    uses it), restated in the oracle (``dequant_torch``), on a row sample."""
+    import torch
+
+    from oracle import qformats_oracle as o
+
+    cores = len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else os.cpu_count()
+    threads = torch.get_num_threads()
+    torch.set_num_threads(cores)
+    xc = x.cpu()
+    M = mats["q8_0"][0][0].shape[0]
+
+    def runner(rows):
+        qd = [(f, mats[f][0][0][:rows].cpu(), mats[f][0][1][:rows].cpu()) for f in ("q8_0", "q4_0")]
+        return lambda: [o.dequant_torch(f, q, d) @ xc for f, q, d in qd]
+
+    try:
+        probe = runner(1024)
+        probe()
+        t0 = time.perf_counter()
+        probe()
+        t1 = max(time.perf_counter() - t0, 1e-6)
+        reps = 3
+        rows = int(min(M, max(1024, 1024 * seconds / (reps * t1))))
+        rows -= rows % 32
+        fn = runner(rows)
+        fn()
+        t0 = time.perf_counter()
+        for _ in range(reps):
+            fn()
+        dt = (time.perf_counter() - t0) / reps
+    finally:
+        torch.set_num_threads(threads)
+    step_bytes = alg_bytes("q8_0", rows, K) + alg_bytes("q4_0", rows, K)
+    return {"value": step_bytes / dt / 1e9, "unit": "GB/s", "cores": cores, "kind": "port",
+            "sample": (f"{rows} of {M} rows x {K}, one q8_0 + one q4_0, {reps} reps: "
+                       "dequant(q, d) @ x in torch fp32 on the CPU (the reference's CPU GEMV "
+                       "path, python/qformats.py:43-56, restated)"),
+            "us_per_step_full_shape_est": dt * 1e6 * M / rows}
 
 
 # ---------------------------------------------------------------------- our arm
@@ -494,17 +641,18 @@ def main():
         extras["roofs"]["cublas_fp16_mv_shape"] = [rows, K]
 
     # ------------------------------------------------------------- timed region
-    uuid = None
-    try:
-        uuid = str(torch.cuda.get_device_properties(dev).uuid)
-        uuid = uuid if uuid.startswith("GPU-") else "GPU-" + uuid
-    except Exception:
-        pass
+    uuid = _gpu_uuid(dev)
     barrier()
     with ClockSampler(uuid) as sampler:
         total_ms, per_ms = time_steps(calls, args.warmup, args.steps, grouped=True)
+        # a short timed region ends before nvidia-smi prints a sample: the same
+        # calls keep running (untimed) until a few samples exist
+        extra_steps = sampler.keep_busy(lambda: time_steps(calls, 0, 200, grouped=True))
         barrier()
     clocks = sampler.summary()
+    if clocks is not None:
+        clocks["window"] = (f"the timed region plus {extra_steps * 200} untimed steps of the same "
+                            "calls right after it" if extra_steps else "the timed region")
     total_ms, q8_ms, q4_ms = max_over_ranks([total_ms, per_ms[0], per_ms[1]])
 
     # ------------------------- the fixed 98304-row matrix sharded N ways (N > 1)
@@ -529,6 +677,44 @@ def main():
         barrier()
         s_total, s_q8, s_q4 = max_over_ranks([s_total, s_per[0], s_per[1]])
         s_bytes = alg_bytes("q8_0", rs, K) + alg_bytes("q4_0", rs, K)
+        # the all-gather of that y (M floats, rs from each rank), alone and as
+        # part of a gathered step (GEMV, all-gather, per format)
+        yfull = {f: torch.empty(M, device=dev) for f in ("q8_0", "q4_0")}
+        ysl = {f: ys[f][:rs] for f in ("q8_0", "q4_0")}
+        for _ in range(5):
+            dist.all_gather_into_tensor(yfull["q8_0"], ysl["q8_0"])
+        barrier()
+        n_ag = max(50, min(args.steps, 500))
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(n_ag):
+            dist.all_gather_into_tensor(yfull["q8_0"], ysl["q8_0"])
+        b.record()
+        b.synchronize()
+        (ag_ms,) = max_over_ranks([a.elapsed_time(b) / n_ag])
+        mqs = {f: [qg.QuantizedMatrix(f, rs, K, "soa", q=v[0], d=v[1]) for v in c["copies"]]
+               for f, c in zip(("q8_0", "q4_0"), scalls)} if args.layout == "soa" else None
+
+        def gathered_step(i):
+            for f in ("q8_0", "q4_0"):
+                m = mqs[f][i % len(mqs[f])]
+                m.matvec(x, ysl[f])
+                dist.all_gather_into_tensor(yfull[f], ysl[f])
+
+        gs = None
+        if mqs is not None:
+            for i in range(10):
+                gathered_step(i)
+            barrier()
+            a.record()
+            for i in range(n_ag):
+                gathered_step(i)
+            b.record()
+            b.synchronize()
+            (gs_ms,) = max_over_ranks([a.elapsed_time(b) / n_ag])
+            gs = {"us_per_step": gs_ms * 1e3, "steps": n_ag,
+                  "gbps_aggregate": world * s_bytes / (gs_ms * 1e-3) / 1e9,
+                  "what": "q8_0 GEMV + NCCL all-gather of its y, then q4_0 GEMV + all-gather"}
         extras["row_sharded_fixed_M"] = {
             "M": M, "rows_per_gpu": rs, "scaling": "strong",
             "value": world * s_bytes * args.steps / (s_total * 1e-3) / 1e9, "unit": "GB/s",
@@ -537,7 +723,11 @@ def main():
             "per_format": {f: {"us_per_call": ms / args.steps * 1e3,
                                "gbps_aggregate": world * alg_bytes(f, rs, K)
                                / (ms / args.steps * 1e-3) / 1e9}
-                           for f, ms in (("q8_0", s_q8), ("q4_0", s_q4))}}
+                           for f, ms in (("q8_0", s_q8), ("q4_0", s_q4))},
+            "allgather_y": {"us_per_call": ag_ms * 1e3, "bytes": M * 4, "backend": "nccl",
+                            "calls": n_ag},
+            "gathered_step": gs}
+        del yfull, mqs
     K_steps = args.steps
     value = world * step_bytes_rank * K_steps / (total_ms * 1e-3) / 1e9
     peak, peak_note = measured_peak()
@@ -551,10 +741,10 @@ def main():
                 "frac_of_peak": b / (per * 1e-3) / 1e9 / peak}
 
     per_format = {"q8_0": fmt_stats("q8_0", q8_ms), "q4_0": fmt_stats("q4_0", q4_ms)}
-    if "roofs" in extras:
-        sr = extras["roofs"]["stream_read_gbps"]
+    read_roof = extras["roofs"]["read_roof_gbps"] if "roofs" in extras else None
+    if read_roof:
         for f in per_format:
-            per_format[f]["frac_of_stream_read_roof"] = per_format[f]["gbps_per_gpu"] / sr
+            per_format[f]["frac_of_read_roof"] = per_format[f]["gbps_per_gpu"] / read_roof
     dom = "q8_0" if q8_ms >= q4_ms else "q4_0"
     # the configuration the library dispatches for this slice (csrc/gemv_tma.cu)
     if dom == "q4_0":
@@ -567,8 +757,11 @@ def main():
     traffic = dram_traffic(f"{dom}_{args.layout}_{rows}x{K}")
     roofline = {"bound": "hbm", "achieved": ach, "peak": peak, "unit": "GB/s",
                 "frac": ach / peak, "traffic": traffic, "kernel": kname,
+                "frac_of_read_roof": ach / read_roof if read_roof else None,
                 "note": f"peak {peak_note}; achieved = algorithmic bytes per launch "
-                        f"({alg_bytes(dom, rows, K)}) / mean launch time (CUDA events)"}
+                        f"({alg_bytes(dom, rows, K)}) / mean launch time (CUDA events); "
+                        "frac_of_read_roof: against the better of this run's two read probes "
+                        "(roofs.read_roof_gbps)"}
 
     # ------------------------------------- opt-in q8_1 activations (not the metric)
     # x rounded to int8 per 32-element block inside the kernel (ggml's q8_1
@@ -585,24 +778,6 @@ def main():
     extras["opt_in_q8_1"]["numerics"] = ("x rounded to int8 per 32-element block (q8_1); "
                                          "outside the exact path's 1e-5 bound; "
                                          f"{n81} calls per format, after the timed region")
-
-    # ---------------------------------------------------------- NCCL all-gather
-    if world > 1:
-        yfull = torch.empty(rows * world, device=dev)
-        yl = ys["q8_0"]
-        for _ in range(5):
-            dist.all_gather_into_tensor(yfull, yl)
-        barrier()
-        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        a.record()
-        n_ag = 200
-        for _ in range(n_ag):
-            dist.all_gather_into_tensor(yfull, yl)
-        b.record()
-        b.synchronize()
-        (ag_ms,) = max_over_ranks([a.elapsed_time(b) / n_ag])
-        extras["allgather_y"] = {"us_per_call": ag_ms * 1e3, "bytes": rows * world * 4,
-                                 "backend": "nccl"}
 
     # --------------------------------------------------------------- end to end
     e2e = None
@@ -661,8 +836,88 @@ def main():
         cpu = cpu_baseline(qg, mats if args.layout == "soa" else
                            {f: [qg.from_aos(f, mats[f][0])] for f in mats}, x, K, args.cpu_seconds)
 
+    cpu_torch = None
+    if rank == 0 and world == 1 and not args.no_extras and args.layout == "soa":
+        cpu_torch = cpu_baseline_torch(mats, x, K, args.cpu_seconds)
+
+    # ---------------------------------------- sessions of the headline shape
+    # The timed region above is session 1; each further session re-allocates
+    # every rotated weight copy (fresh placement in HBM) and times the same
+    # steps again.  The spread across sessions is reported beside the value.
+    sessions = None
+    if not args.no_configs and args.sessions > 1:
+        sess = [{"q8_0_us": q8_ms / K_steps * 1e3, "q4_0_us": q4_ms / K_steps * 1e3,
+                 "gbps_aggregate": value}]
+        for _ in range(1, args.sessions):
+            for f in mats:
+                mats[f] = [(c[0].clone(), c[1].clone()) if args.layout == "soa" else c.clone()
+                           for c in mats[f]]
+            calls = [dict(c, copies=mats[c["fmt"]]) for c in calls]
+            torch.cuda.empty_cache()
+            barrier()
+            t_s, p_s = time_steps(calls, args.warmup, args.steps, grouped=True)
+            barrier()
+            t_s, a8, a4 = max_over_ranks([t_s, p_s[0], p_s[1]])
+            sess.append({"q8_0_us": a8 / K_steps * 1e3, "q4_0_us": a4 / K_steps * 1e3,
+                         "gbps_aggregate": world * step_bytes_rank * K_steps / (t_s * 1e-3) / 1e9})
+
+        def spread(key):
+            v = sorted(r[key] for r in sess)
+            return (v[-1] - v[0]) / v[len(v) // 2]
+
+        sessions = {"runs": sess, "steps_each": K_steps,
+                    "spread": {k: spread(k) for k in ("q8_0_us", "q4_0_us", "gbps_aggregate")},
+                    "note": "spread = (max - min) / median across sessions; each session "
+                            "re-allocates the rotated weight copies"}
+    mats = calls = calls81 = mq = scalls = None  # free the headline's weight copies
+    torch.cuda.empty_cache()
+
+    # ------------------------------- every other configuration of the set
+    configs = None
+    if not args.no_configs:
+        configs = {}
+
+        def guarded(name, fn):
+            try:
+                configs[name] = fn()
+            except Exception as e:  # recorded, not hidden
+                configs[name] = {"error": f"{type(e).__name__}: {e}"}
+
+        guarded("S_4096x4096", lambda: single_column_records(
+            args, rank, world, dev, 4096, 4096, 2000, read_roof, peak))
+        guarded("L_11008x4096", lambda: single_column_records(
+            args, rank, world, dev, 11008, 4096, 2000, read_roof, peak))
+
+        def sb():
+            recs = batch_records(args, rank, world, dev, 200, 10)
+            for r in recs:
+                b = alg_bytes(r["fmt"], 28672, 8192, r["N"])
+                r["frac_of_read_roof"] = (r["gbps_aggregate"] / world / read_roof
+                                          if read_roof else None)
+                r["frac_of_peak"] = r["gbps_aggregate"] / world / peak
+                r["bytes_per_call"] = b
+            return {"M": 28672, "K": 8192, "rows_per_gpu": 28672 // world, "calls": 200,
+                    "results": recs}
+
+        guarded("SB_28672x8192", sb)
+
+        def stk():
+            res, tb, tm = stack_records(args, rank, world, dev, args.stack_mode, 30, 3)
+            err = qg._lib.lib().qgemv_check_device_error(0, None)
+            return {"layers": args.layers, "mode": args.stack_mode,
+                    "how": STACK_MODES[args.stack_mode], "tokens": 30,
+                    "device_error": err, **res}
+
+        guarded("STACK_32x7B", stk)
+
     if rank == 0:
         dinfo = qg.device_info(local)
+        if sessions is not None:
+            extras["sessions"] = sessions
+        if configs is not None:
+            extras["configs"] = configs
+        if cpu_torch is not None:
+            extras["cpu_baseline_torch"] = cpu_torch
         line = {
             "metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": total_ms / K_steps,

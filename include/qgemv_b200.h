@@ -52,6 +52,9 @@ typedef enum qgemv_status {
 
 typedef enum qgemv_format { QGEMV_Q8_0 = 8, QGEMV_Q4_0 = 4 } qgemv_format;
 
+/* Ranks (one GPU each) of the multi-GPU entry points. */
+#define QGEMV_MAX_RANKS 8
+
 typedef struct qgemv_device_info {
   char name[256];
   int device;
@@ -180,30 +183,57 @@ QGEMV_API int qgemv_soa_static_ws(int format, const void* q, const void* d, cons
 /* ------------------------------------------------ persistent decode stack --- */
 
 /* A sequence of single-column SoA GEMVs run by one cooperative launch per
- * call of qgemv_stack_run (e.g. the 4 x n_layers GEMVs of a decode token):
- * GEMV j may read GEMV j-1's y as its x; one CTA per SM keeps a row slice of
- * every matrix and streams the next matrix's weights while the current one
- * drains, so the per-launch completion and pipeline fill are paid once per
- * sequence instead of once per GEMV.  Each GEMV needs the TMA kernel's shapes
- * (256 <= K <= 16384, K % 256 == 0, q and x 16-byte aligned).  The pointers
- * are fixed at creation (copy a new input into the first x buffer before a
- * run); qgemv_stack_create allocates the handle's small device state (not on
- * the GEMV path).  Grid-wide waits are bounded (~1 s; QGEMV_ERR_TIMEOUT in
- * qgemv_check_device_error).  On the 32 layers of a 7B-shaped decode token it
- * measured slower than one PDL launch per GEMV (a CTA holds only a few tiles
- * of each matrix, so the grid-wide wait and the refill after it dominate);
- * the per-launch path stays the default.  No reference counterpart (the
+ * call of qgemv_stack_run (the 4 x n_layers GEMVs of a decode token): GEMV j
+ * reads the first K outputs of GEMV j-1 as its x.  One CTA per SM keeps a row
+ * slice of every matrix and streams the next matrices' weights while the
+ * current GEMV waits for its input, so the per-launch completion and
+ * pipeline fill are paid once per token instead of once per GEMV.
+ *
+ * Outputs are 8-byte slots: slot r holds the fp32 bits of y[r] in its low 32
+ * bits and a tag in its high 32 bits (one 64-bit store).  A reader waits
+ * (bounded) until a slot carries the tag of the current token and GEMV, so
+ * no fence, flag or collective separates the GEMVs, on one GPU or across
+ * ranks; the call completes once every slot of the last GEMV's output on this
+ * rank holds this token's value.  Read y[r] as the low word of slot r.
+ *
+ * qgemv_stack_create: one GPU (r0 = 0, M = M_total).
+ * qgemv_stack_create_ranks: P ranks, one process and one GPU each, all
+ * running the same sequence.  Rank k holds rows [r0, r0 + M) of every matrix
+ * and stores them into its own slots and into every other rank's (peer_y,
+ * e.g. symmetric memory mapped over NVLink): the all-gather of every y is
+ * done by the kernel's own stores (no NCCL call, no qgemv_soa_fused).
+ *
+ * Each GEMV needs 256 <= K <= 16384, K % 256 == 0, K <= M_total of the GEMV
+ * before it, an even M_total, q, d and y (and x of GEMV 0) 16-byte aligned.
+ * The launch uses at most min(SMs, smallest M) CTAs.  The pointers are fixed
+ * at creation (copy a new input into GEMV 0's x before a run); creation
+ * allocates the handle's small device state (not on the GEMV path).  Output
+ * slots start zeroed.  All waits are bounded (QGEMV_ERR_TIMEOUT in
+ * qgemv_check_device_error; then clear it, zero the slots on every rank and
+ * call qgemv_stack_reset before the next run).  No reference counterpart (the
  * reference timed one GEMV at a time). */
 typedef struct qgemv_stack_gemv {
-  const void* q;  /* quant plane */
-  const void* d;  /* scale plane */
-  const float* x; /* K inputs */
-  float* y;       /* M outputs */
-  int64_t M, K;
+  const void* q;   /* quant plane of this rank's rows */
+  const void* d;   /* scale plane */
+  const float* x;  /* GEMV 0: its K input floats; the others read GEMV j-1's slots */
+  uint64_t* y;     /* this GEMV's M_total output slots on this rank */
+  int64_t r0, M;   /* this rank's rows [r0, r0 + M) */
+  int64_t M_total; /* rows of the whole matrix */
+  int64_t K;
 } qgemv_stack_gemv;
+typedef struct qgemv_stack_ranks {
+  int32_t nranks;           /* 1..QGEMV_MAX_RANKS */
+  int32_t rank;             /* this rank */
+  uint64_t* const* peer_y;  /* n x (nranks - 1): GEMV j's output slots on the other ranks,
+                               rank order without this rank */
+} qgemv_stack_ranks;
 QGEMV_API int qgemv_stack_create(int format, const qgemv_stack_gemv* gemvs, int32_t n,
                                  void** handle);
+QGEMV_API int qgemv_stack_create_ranks(int format, const qgemv_stack_gemv* gemvs, int32_t n,
+                                       const qgemv_stack_ranks* ranks, void** handle);
 QGEMV_API int qgemv_stack_run(void* handle, void* stream);
+/* Token count back to zero (after a timeout, once the slots are zeroed). */
+QGEMV_API int qgemv_stack_reset(void* handle, void* stream);
 QGEMV_API int qgemv_stack_destroy(void* handle);
 
 /* -------------------------------------------- fused all-gather (P GPUs) --- */
@@ -224,7 +254,6 @@ QGEMV_API int qgemv_stack_destroy(void* handle);
  * (qgemv_check_device_error(1, ...)) and zero every counter, cta_count and
  * tok before the next token.
  * Replaces the NCCL all-gather after a GEMV (the reference was single-GPU). */
-#define QGEMV_MAX_RANKS 8
 typedef struct qgemv_fuse {
   float* peer_y[QGEMV_MAX_RANKS];     /* other ranks' buffers, at this rank's first row */
   unsigned* sig_out[QGEMV_MAX_RANKS]; /* every rank's counter for this call (this rank's too) */

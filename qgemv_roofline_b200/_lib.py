@@ -36,7 +36,13 @@ class FuseDesc(ctypes.Structure):
 class StackGemvDesc(ctypes.Structure):
     """qgemv_stack_gemv of include/qgemv_b200.h."""
     _fields_ = [("q", ctypes.c_void_p), ("d", ctypes.c_void_p), ("x", ctypes.c_void_p),
-                ("y", ctypes.c_void_p), ("M", ctypes.c_int64), ("K", ctypes.c_int64)]
+                ("y", ctypes.c_void_p), ("r0", ctypes.c_int64), ("M", ctypes.c_int64),
+                ("M_total", ctypes.c_int64), ("K", ctypes.c_int64)]
+
+
+class StackRanksDesc(ctypes.Structure):
+    """qgemv_stack_ranks of include/qgemv_b200.h."""
+    _fields_ = [("nranks", ctypes.c_int32), ("rank", ctypes.c_int32), ("peer_y", ctypes.c_void_p)]
 
 
 class QGemvError(RuntimeError):
@@ -111,7 +117,10 @@ SIGNATURES = {
     "qgemv_token_fence": ([_vp, _i32, _vp, _vp, _vp], ctypes.c_int),
     "qgemv_stack_create": ([ctypes.c_int, _vp, _i32, ctypes.POINTER(ctypes.c_void_p)],
                            ctypes.c_int),
+    "qgemv_stack_create_ranks": ([ctypes.c_int, _vp, _i32, _vp, ctypes.POINTER(ctypes.c_void_p)],
+                                 ctypes.c_int),
     "qgemv_stack_run": ([_vp, _vp], ctypes.c_int),
+    "qgemv_stack_reset": ([_vp, _vp], ctypes.c_int),
     "qgemv_stack_destroy": ([_vp], ctypes.c_int),
     "qgemv_soa_static_ws": ([ctypes.c_int, _vp, _vp, _vp, _vp, _i64, _i64, _i32, _i64, _i64, _vp],
                             ctypes.c_int),

@@ -481,27 +481,66 @@ QGEMV_API int qgemv_aos_q8_1(int format, const void* blocks, const float* x, flo
   return q81_entry(format, true, blocks, nullptr, x, y, M, K, stream);
 }
 
-QGEMV_API int qgemv_stack_create(int format, const qgemv_stack_gemv* gemvs, int32_t n,
-                                 void** handle) {
+namespace {
+int stack_entry(int format, const qgemv_stack_gemv* gemvs, int32_t n,
+                const qgemv_stack_ranks* ranks, void** handle) {
   if (int rc = check_fmt(format)) return rc;
   if (!gemvs || !handle) return set_error(ERR_NULL, "gemvs and handle must not be NULL");
   if (n < 1 || n > 65536) return set_error(ERR_ARG, "n=%d out of range [1, 65536]", n);
+  StackRanks rk;
+  if (ranks) {
+    if (ranks->nranks < 1 || ranks->nranks > kMaxRanks || ranks->rank < 0 ||
+        ranks->rank >= ranks->nranks)
+      return set_error(ERR_ARG, "nranks must be in [1, %d] and rank in [0, nranks)", kMaxRanks);
+    if (ranks->nranks > 1 && !ranks->peer_y)
+      return set_error(ERR_NULL, "peer_y must not be NULL with more than one rank");
+    rk.nranks = ranks->nranks;
+    rk.rank = ranks->rank;
+  }
   std::vector<StackCall> calls(n);
   for (int j = 0; j < n; ++j) {
     const qgemv_stack_gemv& g = gemvs[j];
     if (int rc = check_mk(g.M, g.K)) return rc;
-    if (!g.q || !g.d || !g.x || !g.y) return set_error(ERR_NULL, "stack GEMV %d: NULL pointer", j);
-    if (misaligned(g.d, 2) || misaligned(g.y, 4))
-      return set_error(ERR_ALIGN, "stack GEMV %d: d must be 2-byte and y 4-byte aligned", j);
-    calls[j] = StackCall{g.q, g.d, g.x, g.y, g.M, g.K};
+    if (!g.q || !g.d || !g.y || (j == 0 && !g.x))
+      return set_error(ERR_NULL, "stack GEMV %d: NULL pointer", j);
+    StackCall c;
+    c.q = g.q;
+    c.d = g.d;
+    c.x = g.x;
+    c.y = reinterpret_cast<unsigned long long*>(g.y);
+    c.r0 = g.r0;
+    c.M = g.M;
+    c.M_total = g.M_total;
+    c.K = g.K;
+    for (int k = 0; k < rk.nranks - 1; ++k)
+      c.peer_y[k] = reinterpret_cast<unsigned long long*>(
+          ranks->peer_y[(size_t)j * (rk.nranks - 1) + k]);
+    calls[j] = c;
   }
   *handle = nullptr;
-  return stack_create(format, calls.data(), n, handle);
+  return stack_create(format, calls.data(), n, ranks ? &rk : nullptr, handle);
+}
+}  // namespace
+
+QGEMV_API int qgemv_stack_create(int format, const qgemv_stack_gemv* gemvs, int32_t n,
+                                 void** handle) {
+  return stack_entry(format, gemvs, n, nullptr, handle);
+}
+
+QGEMV_API int qgemv_stack_create_ranks(int format, const qgemv_stack_gemv* gemvs, int32_t n,
+                                       const qgemv_stack_ranks* ranks, void** handle) {
+  if (!ranks) return set_error(ERR_NULL, "ranks must not be NULL");
+  return stack_entry(format, gemvs, n, ranks, handle);
 }
 
 QGEMV_API int qgemv_stack_run(void* handle, void* stream) {
   if (!handle) return set_error(ERR_NULL, "handle must not be NULL");
   return stack_run(handle, static_cast<cudaStream_t>(stream));
+}
+
+QGEMV_API int qgemv_stack_reset(void* handle, void* stream) {
+  if (!handle) return set_error(ERR_NULL, "handle must not be NULL");
+  return stack_reset(handle, static_cast<cudaStream_t>(stream));
 }
 
 QGEMV_API int qgemv_stack_destroy(void* handle) { return stack_destroy(handle); }

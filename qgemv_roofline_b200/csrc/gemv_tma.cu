@@ -1004,80 +1004,164 @@ k_gemv_tma(const TmaArgs p) {
 }
 
 // ------------------------------------------------- persistent decode stack
-// One cooperative launch runs a whole sequence of single-column GEMVs (a
-// decode token: QKV, O, gate+up, down per layer), GEMV j reading GEMV j-1's
-// output.  One CTA per SM keeps a row slice of every matrix; its producer
-// warp streams the tiles of GEMV j, j+1, ... through one ring without
-// pausing at GEMV boundaries (weights never depend on x), so the next
-// matrix's first tiles are in shared memory while the current one drains.
-// The consumers of GEMV j+1 wait until every CTA has written its rows of
-// GEMV j (a grid-wide counter, bounded wait), read x from L2 and convert it
-// to planes, then run the arithmetic of k_gemv_tma.  What the per-launch
-// chain paid at every GEMV -- grid completion, the next launch, its
-// pipeline fill -- is paid once per token.
+// One cooperative launch per decode token runs a whole sequence of
+// single-column GEMVs (QKV, O, gate+up, down per layer), GEMV j reading GEMV
+// j-1's full output, on each of P ranks (one GPU each; P = 1 on one GPU).
+// Every rank holds rows of every matrix; one CTA per SM holds a row slice of
+// each rank-slice.  Warps of a CTA:
+//  * warp 0, producer: streams the weight tiles of GEMV 0, 1, 2, ... through
+//    one shared-memory ring without pausing at GEMV boundaries (weights never
+//    depend on x), so the next matrices' tiles are in shared memory while the
+//    current GEMV waits for its input; when the consumers release a tile it
+//    sums the slice partials of each row and stores the row into this rank's
+//    output and into every other rank's (peer pointers, NVLink);
+//  * warps 1..16, consumers: load x (waiting for it, see below) into shared
+//    memory, then run the arithmetic of k_gemv_tma (x in three byte planes,
+//    exact dp4a block dots).
+// Outputs are 8-byte slots: the row's fp32 bits in the low word and a tag in
+// the high word, tag = token * n + j + 1 for GEMV j, written by one 64-bit
+// store (single-copy atomic).  A reader of GEMV j's output polls each slot
+// until its tag is the expected one, so the slot's value is the one written
+// with that tag: no fence, flag or counter is needed between ranks or CTAs
+// (the scheme of NCCL's low-latency protocol).  Every CTA has rows in every
+// GEMV (the host keeps the grid at most the smallest per-rank row count), so
+// a complete input of GEMV j+1 also shows that every CTA of every rank has
+// finished reading the inputs of GEMV j and earlier: a buffer is rewritten
+// only after every reader is done with it.  The last CTA of the launch to
+// finish waits until the last GEMV's output is complete on this rank and
+// advances the token count.  All waits are bounded (QGEMV_ERR_TIMEOUT).
 struct StackGemv {
-  const uint8_t* q;
-  const unsigned short* d;
-  const float* x;
-  float* y;
-  int M, K, TR, KS;
+  const uint8_t* q;                   // this rank's rows: quant plane
+  const unsigned short* d;            // scale plane
+  const float* x;                     // GEMV 0: its input floats (other GEMVs: unused)
+  unsigned long long* y;              // this GEMV's output slots on this rank (M_total)
+  unsigned long long* peer_y[kMaxRanks - 1];  // the same slots on the other ranks
+  int r0, M, M_total, K, TR, KS;      // this rank's rows [r0, r0 + M) of M_total
 };
 struct StackArgs {
   const StackGemv* g;
   int n;
-  unsigned* bar;  // per GEMV: CTAs that have written their rows (zeroed at the end)
-  int S, SB, PB;  // ring stages, bytes per stage, partial floats per stage
+  unsigned* ctr;  // this rank's [token count, CTAs done]
+  int npeer;
+  int S, SB, PB, XB;  // ring stages, bytes per stage, partial floats per stage, x bytes
 };
 
-__device__ __forceinline__ unsigned ld_acquire_gpu(const unsigned* p) {
-  unsigned v;
-  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+constexpr int kStackConsumers = 16;
+constexpr int kStackXChunk = 4096;  // x elements staged in shared memory at a time
+constexpr int kStackThreads = 32 * (kStackConsumers + 1);
+
+__device__ __forceinline__ void st_slot(unsigned long long* p, float v, unsigned tag) {
+  const unsigned long long s = ((unsigned long long)tag << 32) | __float_as_uint(v);
+  asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(s) : "memory");
+}
+__device__ __forceinline__ ulonglong2 ld_slots2(const unsigned long long* p) {
+  ulonglong2 v;
+  asm volatile("ld.relaxed.sys.global.v2.u64 {%0, %1}, [%2];" : "=l"(v.x), "=l"(v.y) : "l"(p)
+               : "memory");
   return v;
 }
 
-// Bounded wait for a grid-wide counter of this device, polling with a short
-// sleep so the CTAs that increment it are not slowed by the polls.
-__device__ __forceinline__ bool wait_grid(const unsigned* c, unsigned target,
+// Bounded wait until slots [i, i + 2) carry `tag` (no copy).
+__device__ __forceinline__ bool wait_tag2(const unsigned long long* src, int i, unsigned tag,
                                           volatile int* abort_flag) {
-  if ((int)(ld_acquire_gpu(c) - target) >= 0) return true;
-  const long long t0 = clock64(), lim = spin_limit();
-  while ((int)(ld_acquire_gpu(c) - target) < 0) {
+  long long t0 = -1, lim = 0;
+  for (;;) {
+    const ulonglong2 v = ld_slots2(src + i);
+    if ((unsigned)(v.x >> 32) == tag && (unsigned)(v.y >> 32) == tag) return true;
     if (*abort_flag) return false;
-    if (clock64() - t0 > lim) {
-      // the error word first, then the CTA's abort flag: whoever sees the
-      // flag (and fences) also sees the error word
+    if (t0 < 0) {
+      t0 = clock64();
+      lim = spin_limit();
+    } else if (clock64() - t0 > lim) {
       atomicExch(&g_device_error, (int)ERR_TIMEOUT);
       __threadfence();
       *abort_flag = 1;
       return false;
     }
-    __nanosleep(64);
+  }
+}
+
+// One consumer thread's share of x from slots: pairs i = i0, i0 + step, ...
+// below K (at most kMaxPairs of them), each stored into xs once its tag is
+// `tag`.  Every pass issues all pending loads at once; between passes the
+// thread sleeps briefly, so the waiting CTAs do not flood L2 with polls while
+// the producers' rows are still on their way.  Bounded.
+constexpr int kMaxPairs = 16;  // K <= 16384 with 512 consumer threads
+__device__ __forceinline__ bool load_slots(const unsigned long long* src, int i0, int step, int K,
+                                           unsigned tag, float* xs, volatile int* abort_flag) {
+  uint32_t pending = 0;
+#pragma unroll
+  for (int v = 0; v < kMaxPairs; ++v)
+    if (i0 + v * step < K) pending |= 1u << v;
+  long long t0 = -1, lim = 0;
+  while (pending) {
+#pragma unroll
+    for (int v = 0; v < kMaxPairs; ++v) {
+      if (pending & (1u << v)) {
+        const int i = i0 + v * step;
+        const ulonglong2 w = ld_slots2(src + i);
+        if ((unsigned)(w.x >> 32) == tag && (unsigned)(w.y >> 32) == tag) {
+          xs[i] = __uint_as_float((unsigned)w.x);
+          xs[i + 1] = __uint_as_float((unsigned)w.y);
+          pending &= ~(1u << v);
+        }
+      }
+    }
+    if (!pending) break;
+    if (*abort_flag) return false;
+    if (t0 < 0) {
+      t0 = clock64();
+      lim = spin_limit();
+    } else if (clock64() - t0 > lim) {
+      atomicExch(&g_device_error, (int)ERR_TIMEOUT);
+      __threadfence();
+      *abort_flag = 1;
+      return false;
+    }
+    __nanosleep(200);
   }
   return true;
 }
 
-// x planes from memory written by other CTAs of this grid: L2 loads (.cg)
-__device__ __forceinline__ void make_planes_l2(const float* __restrict__ xb, XPlanes& o) {
-  float v[32];
+// R rows of one lane's block from SoA planes in shared memory (quants at
+// 32-bit address qa, scale at da, row strides QB / DB): the exact dot of each
+// row's block with the lane's x planes, scaled.
+template <int FMT, int R, bool FAST>
+__device__ __forceinline__ void soa_rows(uint32_t qa, uint32_t da, int QB, int DB,
+                                         const XPlanes& xp, const XScale& xq, float (&acc)[R]) {
 #pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    const float4 f = __ldcg(reinterpret_cast<const float4*>(xb + 4 * i));
-    v[4 * i] = f.x; v[4 * i + 1] = f.y; v[4 * i + 2] = f.z; v[4 * i + 3] = f.w;
+  for (int r = 0; r < R; ++r) {
+    constexpr int QW = FMT == 8 ? 8 : 4;
+    uint32_t wq[QW];
+    const float dvr = half_bits_to_float(lds_u16(da));
+    da += DB;
+    const uint4 u0 = lds_v4(qa);
+    wq[0] = u0.x; wq[1] = u0.y; wq[2] = u0.z; wq[3] = u0.w;
+    if (FMT == 8) {
+      const uint4 u1 = lds_v4(qa + 16);
+      wq[4 % QW] = u1.x; wq[5 % QW] = u1.y; wq[6 % QW] = u1.z; wq[7 % QW] = u1.w;
+    }
+    qa += QB;
+    int lo, hi;
+    block_sums<FMT>(wq, xp, lo, hi);
+    acc[r] = block_value<FMT, FAST>(lo, hi, dvr, xq, xp);
   }
-  make_planes_from(v, o);
 }
 
 template <int FMT, int R>
-__global__ void __launch_bounds__(tma_threads(16), 1) k_gemv_stack(const __grid_constant__ StackArgs p) {
-  constexpr int CONSUMERS = 16;
+__global__ void __launch_bounds__(kStackThreads, 1) k_gemv_stack(const __grid_constant__ StackArgs p) {
+  constexpr int CONSUMERS = kStackConsumers;
   using F = Fmt<FMT>;
   extern __shared__ __align__(128) uint8_t sm[];
   __shared__ __align__(8) unsigned long long full[MAX_STAGES];
   __shared__ __align__(8) unsigned long long empty[MAX_STAGES];
+  __shared__ __align__(8) unsigned long long xload;  // every consumer warp has stored its part of x
+  __shared__ __align__(8) unsigned long long xconv;  // every consumer warp has its planes
   __shared__ int abort_flag;
 
   const int S = p.S, G = gridDim.x, b = blockIdx.x;
   float* part = reinterpret_cast<float*>(sm + (size_t)S * p.SB);
+  float* xs = reinterpret_cast<float*>(sm + (size_t)S * p.SB + (size_t)S * p.PB * 4);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
@@ -1085,95 +1169,133 @@ __global__ void __launch_bounds__(tma_threads(16), 1) k_gemv_stack(const __grid_
       asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(saddr(&empty[s])),
                    "r"(CONSUMERS));
     }
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(saddr(&xload)), "r"(CONSUMERS));
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(saddr(&xconv)), "r"(CONSUMERS));
     abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   __syncthreads();
+  // tag of GEMV j of this token
+  const unsigned tok = *(volatile const unsigned*)&p.ctr[0];
+  const unsigned tag0 = tok * (unsigned)p.n + 1u;
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
-    // issue cursor (ji, ti) and finalize cursor (jf, tf) over (GEMV, tile)
-    int ji = 0, ti = 0, jf = 0, tf = 0;
+    // issue cursor (ji, ti) and finalize cursor (jf, tf) over (GEMV, tile).
+    // Each cursor keeps its GEMV's parameters in registers, read once (through
+    // the read-only path) when the cursor moves to the next GEMV: the
+    // descriptors live in global memory, and reloading them for every tile
+    // put a global-memory round trip on the producer's per-tile path.
+    struct Cur {
+      int j, t, a, nrows, ntiles, TR, KS, K, r0;
+      const uint8_t* q;
+      const uint8_t* d;
+      unsigned long long* y;
+    };
+    auto load_cur = [&](Cur& c, int j) {
+      c.j = j;
+      c.t = 0;
+      if (j >= p.n) return;
+      const StackGemv* g = p.g + j;
+      const int M = __ldg(&g->M);
+      c.TR = __ldg(&g->TR);
+      c.KS = __ldg(&g->KS);
+      c.K = __ldg(&g->K);
+      c.r0 = __ldg(&g->r0);
+      c.q = reinterpret_cast<const uint8_t*>(__ldg(reinterpret_cast<const unsigned long long*>(&g->q)));
+      c.d = reinterpret_cast<const uint8_t*>(__ldg(reinterpret_cast<const unsigned long long*>(&g->d)));
+      c.y = reinterpret_cast<unsigned long long*>(__ldg(reinterpret_cast<const unsigned long long*>(&g->y)));
+      c.a = (int)((int64_t)M * b / G);
+      c.nrows = (int)((int64_t)M * (b + 1) / G) - c.a;
+      c.ntiles = (c.nrows + c.TR - 1) / c.TR;
+    };
+    Cur ci, cf;
+    load_cur(ci, 0);
+    load_cur(cf, 0);
+    unsigned long long* peer_base[kMaxRanks - 1];  // finalize cursor's peer slots
+    const int npeer = p.npeer;
+    for (int k = 0; k < npeer; ++k)
+      peer_base[k] = reinterpret_cast<unsigned long long*>(
+          __ldg(reinterpret_cast<const unsigned long long*>(&p.g[0].peer_y[k])));
     uint32_t u = 0, f = 0;
     int last_issued[MAX_STAGES];
     for (int s = 0; s < MAX_STAGES; ++s) last_issued[s] = -1;
-    auto rows_of = [&](int j, int& a, int& nrows) {
-      const int M = p.g[j].M;
-      a = (int)((int64_t)M * b / G);
-      nrows = (int)((int64_t)M * (b + 1) / G) - a;
-    };
     bool ok = true;
     for (;;) {
       // issue while the ring has room
-      while (ji < p.n && u - f < (uint32_t)S) {
-        int a, nrows;
-        rows_of(ji, a, nrows);
-        const StackGemv g = p.g[ji];
-        const int ntiles = (nrows + g.TR - 1) / g.TR;
-        if (ti >= ntiles) {
-          ++ji;
-          ti = 0;
+      while (ci.j < p.n && u - f < (uint32_t)S) {
+        if (ci.t >= ci.ntiles) {
+          load_cur(ci, ci.j + 1);
           continue;
         }
         if (lane == 0) {
           const int s = (int)(u % (uint32_t)S);
-          const int QB = g.K / F::ROW_DIV, DB = g.K / 16;
-          const int r0 = ti * g.TR, nr = min(g.TR, nrows - r0);
+          const int QB = ci.K / F::ROW_DIV, DB = ci.K / 16;
+          const int r0 = ci.t * ci.TR, nr = min(ci.TR, ci.nrows - r0);
           const uint32_t bar = saddr(&full[s]);
           uint8_t* st = sm + (size_t)s * p.SB;
           asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar),
                        "r"((uint32_t)nr * (QB + DB))
                        : "memory");
-          bulk_g2s(saddr(st), g.q + (int64_t)(a + r0) * QB, (uint32_t)nr * QB, bar);
-          bulk_g2s(saddr(st + (size_t)g.TR * QB),
-                   reinterpret_cast<const uint8_t*>(g.d) + (int64_t)(a + r0) * DB,
+          bulk_g2s(saddr(st), ci.q + (int64_t)(ci.a + r0) * QB, (uint32_t)nr * QB, bar);
+          bulk_g2s(saddr(st + (size_t)ci.TR * QB), ci.d + (int64_t)(ci.a + r0) * DB,
                    (uint32_t)nr * DB, bar);
           last_issued[s] = (int)u;
         }
-        ++ti;
+        ++ci.t;
         ++u;
       }
-      if (jf >= p.n) break;
-      int a, nrows;
-      rows_of(jf, a, nrows);
-      const StackGemv g = p.g[jf];
-      const int ntiles = (nrows + g.TR - 1) / g.TR;
-      if (tf < ntiles) {
-        // finalize tile f: the consumers are done with it; write its rows of y
+      if (cf.j >= p.n) break;
+      if (cf.t < cf.ntiles) {
+        // finalize tile f: the consumers are done with it; store its rows
         const int s = (int)(f % (uint32_t)S);
         ok = __all_sync(0xffffffffu, mbar_wait(saddr(&empty[s]), (f / (uint32_t)S) & 1u,
                                                &abort_flag));
         if (!ok) break;
-        const int r0 = tf * g.TR, nr = min(g.TR, nrows - r0);
+        const int TR = cf.TR, KS = cf.KS;
+        const int r0 = cf.t * TR, nr = min(TR, cf.nrows - r0);
+        const int row0 = cf.r0 + cf.a + r0;
         const float* ps = part + (size_t)s * p.PB;
+        const unsigned tag = tag0 + (unsigned)cf.j;
         for (int i = lane; i < nr; i += 32) {  // partials [KS][TR]: conflict-free
           float v = 0.0f;
-          for (int k = 0; k < g.KS; ++k) v += ps[k * g.TR + i];
-          g.y[a + r0 + i] = v;
+          for (int k = 0; k < KS; ++k) v += ps[k * TR + i];
+          st_slot(cf.y + row0 + i, v, tag);
+          for (int k = 0; k < npeer; ++k) st_slot(peer_base[k] + row0 + i, v, tag);  // NVLink
         }
         __syncwarp();
-        ++tf;
+        ++cf.t;
         ++f;
       }
-      if (tf >= ntiles) {
-        // this CTA's rows of GEMV jf are written: count it for the grid
-        __threadfence();
-        __syncwarp();
-        if (lane == 0) atomicAdd(&p.bar[jf], 1u);
-        ++jf;
-        tf = 0;
+      if (cf.t >= cf.ntiles) {
+        load_cur(cf, cf.j + 1);
+        if (cf.j < p.n)
+          for (int k = 0; k < npeer; ++k)
+            peer_base[k] = reinterpret_cast<unsigned long long*>(
+                __ldg(reinterpret_cast<const unsigned long long*>(&p.g[cf.j].peer_y[k])));
       }
     }
-    if (!ok && lane == 0) {
-      for (int s = 0; s < S; ++s)
-        if (last_issued[s] >= 0)
-          mbar_wait_drain(saddr(&full[s]), (uint32_t)((last_issued[s] / S) & 1));
+    if (!ok) {
+      if (lane == 0)
+        for (int s = 0; s < S; ++s)
+          if (last_issued[s] >= 0)
+            mbar_wait_drain(saddr(&full[s]), (uint32_t)((last_issued[s] / S) & 1));
+      return;
     }
-    if (b == 0 && lane == 0 && ok) {
-      // every CTA has passed every wait once all have counted the last GEMV:
-      // reset the counters for the next token
-      if (wait_grid(&p.bar[p.n - 1], (unsigned)G, &abort_flag)) {
-        for (int j = 0; j < p.n; ++j) atomicExch(&p.bar[j], 0u);
+    // end of the token: the last CTA of this launch waits until the last
+    // GEMV's output is complete on this rank, then advances the token count
+    unsigned old = 0;
+    if (lane == 0) old = atomicAdd(&p.ctr[1], 1u);
+    old = __shfl_sync(0xffffffffu, old, 0);
+    if (old == (unsigned)G - 1u) {
+      const StackGemv& g = p.g[p.n - 1];
+      const unsigned tag = tag0 + (unsigned)(p.n - 1);
+      bool done = true;
+      for (int i = 2 * lane; i < g.M_total && done; i += 64)
+        done = wait_tag2(g.y, i, tag, &abort_flag);
+      if (__all_sync(0xffffffffu, done) && lane == 0) {
+        atomicExch(&p.ctr[1], 0u);
+        atomicExch(&p.ctr[0], tok + 1u);
         __threadfence();
       }
     }
@@ -1181,91 +1303,88 @@ __global__ void __launch_bounds__(tma_threads(16), 1) k_gemv_stack(const __grid_
   }
 
   // -------------------------------------------------------------- consumers
-  const int cw = warp - 1;
-  uint32_t u = 0;
-  bool dead = false;  // after an abort: still reach every named barrier, do no work
+  const int cw = warp - 1, ct = threadIdx.x - 32;  // consumer warp / thread
+  uint32_t u = 0, xph = 0;  // tiles consumed; x chunks staged (xload / xconv phases)
   for (int j = 0; j < p.n; ++j) {
-    const StackGemv g = p.g[j];
-    const int KS = g.KS, ks = cw % KS, rg = cw / KS, RG = CONSUMERS / KS;
-    const int QB = g.K / F::ROW_DIV, DB = g.K / 16;
-    const int a = (int)((int64_t)g.M * b / G);
-    const int nrows = (int)((int64_t)g.M * (b + 1) / G) - a;
-    const int ntiles = (nrows + g.TR - 1) / g.TR;
+    // this GEMV's parameters in registers (the asm statements below clobber
+    // memory, so fields read through p.g would be reloaded in every pass)
+    const int K = p.g[j].K, TR = p.g[j].TR, KS = p.g[j].KS, Mj = p.g[j].M;
+    const float* gx = p.g[j].x;
+    const unsigned long long* gsrc = j > 0 ? p.g[j - 1].y : nullptr;
+    const int ks = cw % KS, rg = cw / KS, RG = CONSUMERS / KS;
+    const int QB = K / F::ROW_DIV, DB = K / 16;
+    const int a = (int)((int64_t)Mj * b / G);
+    const int nrows = (int)((int64_t)Mj * (b + 1) / G) - a;
+    const int ntiles = (nrows + TR - 1) / TR;
     const int c = ks * 32 + lane;
-    const bool cval = c < g.K / QK;
+    const bool cval = c < K / QK;
     const int cidx = cval ? c : 0;
-    if (j > 0) {
-      // x = GEMV j-1's y: one thread waits (bounded) until every CTA has
-      // written its rows; the other consumers wait for it at a named barrier
-      // (the producer warp is not part of it), which the waiting thread
-      // always reaches.
-      if (cw == 0 && lane == 0 && !dead) wait_grid(&p.bar[j - 1], (unsigned)G, &abort_flag);
-      asm volatile("bar.sync 1, %0;" ::"r"(CONSUMERS * 32) : "memory");
-      if (abort_flag) dead = true;
-    }
-    if (dead) continue;
+    // x of GEMV j into shared memory, kStackXChunk elements at a time (a small
+    // staging area leaves room for a deeper weight ring): GEMV 0 reads its
+    // input floats; GEMV j > 0 reads GEMV j-1's output slots, each once its
+    // tag shows this token's value.  Each lane converts its block when the
+    // chunk holding it is staged.  (mbarriers with bounded waits, not named
+    // barriers: a warp that gives up must not leave the others waiting
+    // without limit.)
     XPlanes xp;
-    if (cval) {
-      if (j > 0) make_planes_l2(g.x + cidx * 32, xp);
-      else make_planes(g.x + cidx * 32, xp);
-    } else {
-      for (int w = 0; w < 8; ++w)
-        for (int pl = 0; pl < NPL; ++pl) xp.pl[w][pl] = 0u;
-      xp.e = -149;
-      xp.bias = 0.0f;
-      xp.finite = true;
+    for (int w = 0; w < 8; ++w)
+      for (int pl = 0; pl < NPL; ++pl) xp.pl[w][pl] = 0u;
+    xp.e = -149;
+    xp.bias = 0.0f;
+    xp.finite = true;
+    for (int k0 = 0; k0 < K; k0 += kStackXChunk, ++xph) {
+      const int kn = min(kStackXChunk, K - k0);
+      bool ok = true;
+      if (j == 0) {
+        for (int i = 4 * ct; i < kn; i += 4 * 32 * CONSUMERS)
+          *reinterpret_cast<float4*>(xs + i) = *reinterpret_cast<const float4*>(gx + k0 + i);
+      } else {
+        ok = load_slots(gsrc + k0, 2 * ct, 2 * 32 * CONSUMERS, kn, tag0 + (unsigned)(j - 1), xs,
+                        &abort_flag);
+      }
+      if (!__all_sync(0xffffffffu, ok)) return;
+      if (lane == 0)
+        asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(saddr(&xload)) : "memory");
+      if (!__all_sync(0xffffffffu, mbar_wait(saddr(&xload), xph & 1u, &abort_flag))) return;
+      const int e0 = cidx * QK - k0;  // the lane's block inside this chunk?
+      if (cval && e0 >= 0 && e0 < kn) make_planes_smem(saddr(xs) + (uint32_t)(e0 * 4), lane, xp);
+      // every consumer has its planes before the next chunk overwrites xs
+      __syncwarp();
+      if (lane == 0)
+        asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(saddr(&xconv)) : "memory");
+      if (!__all_sync(0xffffffffu, mbar_wait(saddr(&xconv), xph & 1u, &abort_flag))) return;
     }
     const XScale xq = x_scale<FMT>(xp);
     const bool fast = __all_sync(0xffffffffu, !cval || xq.fast);  // as in k_gemv_tma
-    bool ok = true;
     for (int t = 0; t < ntiles; ++t, ++u) {
       const int s = (int)(u % (uint32_t)S);
       if (!__all_sync(0xffffffffu, mbar_wait(saddr(&full[s]), (u / (uint32_t)S) & 1u,
-                                             &abort_flag))) {
-        ok = false;
-        break;
-      }
-      const int nr = min(g.TR, nrows - t * g.TR);
-      const uint8_t* st = sm + (size_t)s * p.SB;
-      const uint8_t* sd = st + (size_t)g.TR * QB;
+                                             &abort_flag)))
+        return;
+      const int nr = min(TR, nrows - t * TR);
+      const uint32_t sbase = saddr(sm) + (uint32_t)(s * p.SB);
       float* ps = part + (size_t)s * p.PB;
       for (int r0 = rg * R; r0 < nr; r0 += RG * R) {
         float acc[R];
 #pragma unroll
         for (int r = 0; r < R; ++r) acc[r] = 0.0f;
         if (cval) {
-          // rows beyond nr read stale in-bounds bytes; never stored
-#pragma unroll
-          for (int r = 0; r < R; ++r) {
-            const uint8_t* rowp = st + (size_t)(r0 + r) * QB;
-            const float dv = half_bits_to_float(
-                *reinterpret_cast<const unsigned short*>(sd + (size_t)(r0 + r) * DB + cidx * 2));
-            uint32_t wq[FMT == 8 ? 8 : 4];
-            if (FMT == 8) {
-              const uint4 u0 = *reinterpret_cast<const uint4*>(rowp + cidx * 32);
-              const uint4 u1 = *reinterpret_cast<const uint4*>(rowp + cidx * 32 + 16);
-              wq[0] = u0.x; wq[1] = u0.y; wq[2] = u0.z; wq[3] = u0.w;
-              wq[4 % (FMT == 8 ? 8 : 4)] = u1.x; wq[5 % (FMT == 8 ? 8 : 4)] = u1.y;
-              wq[6 % (FMT == 8 ? 8 : 4)] = u1.z; wq[7 % (FMT == 8 ? 8 : 4)] = u1.w;
-            } else {
-              const uint4 uq = *reinterpret_cast<const uint4*>(rowp + cidx * 16);
-              wq[0] = uq.x; wq[1] = uq.y; wq[2] = uq.z; wq[3] = uq.w;
-            }
-            int lo, hi;
-            block_sums<FMT>(wq, xp, lo, hi);
-            acc[r] = fast ? block_value<FMT, true>(lo, hi, dv, xq, xp)
-                          : block_value<FMT, false>(lo, hi, dv, xq, xp);
-          }
+          // rows beyond nr read stale in-bounds bytes; never stored.  The
+          // lane's quants and scale of row r0 + r as 32-bit shared addresses
+          // stepped by the row strides, as in k_gemv_tma.
+          const uint32_t qa = sbase + (uint32_t)(r0 * QB + cidx * (FMT == 8 ? 32 : 16));
+          const uint32_t da = sbase + (uint32_t)(TR * QB + r0 * DB + cidx * 2);
+          if (fast) soa_rows<FMT, R, true>(qa, da, QB, DB, xp, xq, acc);
+          else soa_rows<FMT, R, false>(qa, da, QB, DB, xp, xq, acc);
         }
         const float v = reduce_rows<R>(acc, lane);
         const int r = row_of_lane<R>(lane);
-        if ((lane & (32 / R - 1)) == 0 && r0 + r < nr) ps[ks * g.TR + r0 + r] = v;
+        if ((lane & (32 / R - 1)) == 0 && r0 + r < nr) ps[ks * TR + r0 + r] = v;
       }
       __syncwarp();
       if (lane == 0)
         asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(saddr(&empty[s])) : "memory");
     }
-    if (!ok) dead = true;
   }
 }
 
@@ -1450,8 +1569,11 @@ int reset_tile_counters(cudaStream_t st) {
 }
 
 bool tma_eligible(const GemvCall& c) {
+  // bulk copies start on 16-byte boundaries: x, and the scale plane of SoA
+  // calls (its rows are K / 16 bytes, a multiple of 16, so the base decides)
   return c.N == 1 && c.K >= 256 && c.K % 256 == 0 && c.K <= 16384 && c.M >= 1 &&
-         (reinterpret_cast<uintptr_t>(c.x) & 15) == 0;
+         (reinterpret_cast<uintptr_t>(c.x) & 15) == 0 &&
+         (reinterpret_cast<uintptr_t>(c.d) & 15) == 0;
 }
 
 // Returns OK, an error status, or -1 when the shape is not handled here.
@@ -1575,59 +1697,107 @@ struct StackHandle {
   StackArgs args;
   size_t smem;
   StackGemv* dev_g;
-  unsigned* dev_bar;
+  unsigned* ctr;  // [token count, CTAs done]
 };
+template <int FMT>
+constexpr int stack_rows() { return 4; }  // rows per warp pass
+auto stack_kernel(int fmt) {
+  return fmt == 8 ? k_gemv_stack<8, stack_rows<8>()> : k_gemv_stack<4, stack_rows<4>()>;
+}
 }  // namespace
 
-int stack_create(int fmt, const StackCall* calls, int n, void** out) {
+int stack_create(int fmt, const StackCall* calls, int n, const StackRanks* ranks, void** out) {
   DeviceInfo dev;
   if (int rc = current_device_info(dev)) return rc;
   if (n < 1) return set_error(ERR_ARG, "a stack needs at least one GEMV");
-  const int R = fmt == 8 ? 4 : 8;  // rows per warp pass, as in the per-launch kernel
+  const int nranks = ranks ? ranks->nranks : 1;
+  if (nranks < 1 || nranks > kMaxRanks)
+    return set_error(ERR_ARG, "nranks must be in [1, %d]", kMaxRanks);
+  const int R = fmt == 8 ? stack_rows<8>() : stack_rows<4>();
   std::vector<StackGemv> g(n);
-  int SB = 0, PB = 0;
+  int SB = 0, PB = 0, XB = 0;
+  int64_t min_rows = INT64_MAX;
+  auto a16 = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
   for (int j = 0; j < n; ++j) {
     const StackCall& c = calls[j];
     if (c.K < 256 || c.K % 256 || c.K > 16384 || c.M < 1)
-      return set_error(ERR_UNSUPPORTED, "stack GEMV %d: needs 256 <= K <= 16384, K %% 256 == 0", j);
-    if ((reinterpret_cast<uintptr_t>(c.x) & 15) || (reinterpret_cast<uintptr_t>(c.q) & 15))
-      return set_error(ERR_ALIGN, "stack GEMV %d: q and x must be 16-byte aligned", j);
+      return set_error(ERR_UNSUPPORTED,
+                       "stack GEMV %d: needs 256 <= K <= 16384, K %% 256 == 0 and rows", j);
+    if (c.r0 < 0 || c.r0 + c.M > c.M_total || c.M_total >= ((int64_t)1 << 31))
+      return set_error(ERR_SHAPE, "stack GEMV %d: rows [%lld, %lld) outside [0, %lld)", j,
+                       (long long)c.r0, (long long)(c.r0 + c.M), (long long)c.M_total);
+    if (!a16(c.q) || !a16(c.d) || !a16(c.y) || (j == 0 && !a16(c.x)))
+      return set_error(ERR_ALIGN, "stack GEMV %d: q, d, y (and x of GEMV 0) must be 16-byte aligned", j);
+    if (j > 0 && calls[j - 1].M_total < c.K)
+      return set_error(ERR_SHAPE, "stack GEMV %d: K = %lld exceeds the %lld outputs of GEMV %d", j,
+                       (long long)c.K, (long long)calls[j - 1].M_total, j - 1);
+    if (c.M_total % 2)
+      return set_error(ERR_SHAPE, "stack GEMV %d: M_total must be even", j);
+    min_rows = std::min(min_rows, c.M);
     const int QB = (int)(fmt == 8 ? c.K : c.K / 2), DB = (int)(c.K / 16), row = QB + DB;
     const int nunits = (int)(c.K / QK);
     int KS = 1;
     while (KS * 32 < nunits) KS *= 2;
-    const int unit = (16 / KS) * R;
+    const int unit = (kStackConsumers / KS) * R;
     const int TR = unit * std::max(1, (32 * 1024) / (unit * row));
-    g[j] = StackGemv{static_cast<const uint8_t*>(c.q), static_cast<const unsigned short*>(c.d),
-                     c.x, c.y, (int)c.M, (int)c.K, TR, KS};
+    StackGemv s{};
+    s.q = static_cast<const uint8_t*>(c.q);
+    s.d = static_cast<const unsigned short*>(c.d);
+    s.x = c.x;
+    s.y = c.y;
+    for (int k = 0; k < nranks - 1; ++k) {
+      s.peer_y[k] = c.peer_y[k];
+      if (!s.peer_y[k] || !a16(s.peer_y[k]))
+        return set_error(ERR_ALIGN, "stack GEMV %d: peer_y[%d] must be a 16-byte aligned pointer",
+                         j, k);
+    }
+    s.r0 = (int)c.r0;
+    s.M = (int)c.M;
+    s.M_total = (int)c.M_total;
+    s.K = (int)c.K;
+    s.TR = TR;
+    s.KS = KS;
+    g[j] = s;
     SB = std::max(SB, (TR * row + 15) / 16 * 16);
-    PB = std::max(PB, TR * KS);
+    PB = std::max(PB, (TR * KS + 3) / 4 * 4);  // keeps the x area 16-byte aligned
+    XB = std::max(XB, (int)std::min<int64_t>(c.K, kStackXChunk) * 4);
   }
-  auto kern = fmt == 8 ? k_gemv_stack<8, 4> : k_gemv_stack<4, 8>;
-  const void* kp = reinterpret_cast<const void*>(kern);
+  const void* kp = reinterpret_cast<const void*>(stack_kernel(fmt));
   if (int rc = allow_max_smem(kp, dev)) return rc;
   cudaFuncAttributes fa;
   if (cudaFuncGetAttributes(&fa, kp) != cudaSuccess) return check_launch("cudaFuncGetAttributes");
-  const int avail = dev.smem_optin - (int)fa.sharedSizeBytes;
+  const int avail = dev.smem_optin - (int)fa.sharedSizeBytes - XB;
   const int S = std::min(MAX_STAGES, avail / (SB + 4 * PB));
   if (S < 2) return set_error(ERR_UNSUPPORTED, "stack tiles of %d bytes do not fit twice", SB);
   StackHandle* h = new StackHandle();
   h->fmt = fmt;
   h->device = dev.device;
   h->n = n;
-  h->grid = dev.sms;
-  h->smem = (size_t)S * (SB + 4 * PB);
+  // every CTA has rows in every GEMV (so a complete input also shows that
+  // every CTA has finished with the buffers before it)
+  h->grid = (int)std::min<int64_t>(dev.sms, min_rows);
+  h->smem = (size_t)S * (SB + 4 * PB) + XB;
+  h->ctr = nullptr;
   cudaError_t e = cudaMalloc(&h->dev_g, sizeof(StackGemv) * n);
-  if (e == cudaSuccess) e = cudaMalloc(&h->dev_bar, sizeof(unsigned) * n);
+  if (e == cudaSuccess) e = cudaMalloc(&h->ctr, sizeof(unsigned) * 2);
   if (e == cudaSuccess) e = cudaMemcpy(h->dev_g, g.data(), sizeof(StackGemv) * n, cudaMemcpyHostToDevice);
-  if (e == cudaSuccess) e = cudaMemset(h->dev_bar, 0, sizeof(unsigned) * n);
+  if (e == cudaSuccess) e = cudaMemset(h->ctr, 0, sizeof(unsigned) * 2);
   if (e != cudaSuccess) {
     cudaFree(h->dev_g);
-    cudaFree(h->dev_bar);
+    cudaFree(h->ctr);
     delete h;
     return set_error(ERR_CUDA, "stack set-up: %s", cudaGetErrorString(e));
   }
-  h->args = StackArgs{h->dev_g, n, h->dev_bar, S, SB, PB};
+  StackArgs a{};
+  a.g = h->dev_g;
+  a.n = n;
+  a.ctr = h->ctr;
+  a.npeer = nranks - 1;
+  a.S = S;
+  a.SB = SB;
+  a.PB = PB;
+  a.XB = XB;
+  h->args = a;
   *out = h;
   return OK;
 }
@@ -1641,18 +1811,26 @@ int stack_run(void* handle, cudaStream_t st) {
                      h->device, cur);
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(h->grid);
-  cfg.blockDim = dim3(tma_threads(16));
+  cfg.blockDim = dim3(kStackThreads);
   cfg.dynamicSmemBytes = h->smem;
   cfg.stream = st;
   cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeCooperative;  // every CTA resident: grid-wide waits
+  attr[0].id = cudaLaunchAttributeCooperative;  // every CTA resident: cross-CTA waits
   attr[0].val.cooperative = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  const cudaError_t e = h->fmt == 8 ? cudaLaunchKernelEx(&cfg, k_gemv_stack<8, 4>, h->args)
-                                    : cudaLaunchKernelEx(&cfg, k_gemv_stack<4, 8>, h->args);
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, stack_kernel(h->fmt), h->args);
   if (e != cudaSuccess) return set_error(ERR_CUDA, "k_gemv_stack launch: %s", cudaGetErrorString(e));
   return check_launch("k_gemv_stack");
+}
+
+int stack_reset(void* handle, cudaStream_t st) {
+  // token count and CTA count back to zero; the caller zeroes the output
+  // slots (stale tags of an aborted token could otherwise match again)
+  StackHandle* h = static_cast<StackHandle*>(handle);
+  const cudaError_t e = cudaMemsetAsync(h->ctr, 0, sizeof(unsigned) * 2, st);
+  if (e != cudaSuccess) return set_error(ERR_CUDA, "stack reset: %s", cudaGetErrorString(e));
+  return OK;
 }
 
 int stack_destroy(void* handle) {
@@ -1663,7 +1841,7 @@ int stack_destroy(void* handle) {
   cudaSetDevice(h->device);
   cudaError_t e = cudaDeviceSynchronize();
   cudaFree(h->dev_g);
-  cudaFree(h->dev_bar);
+  cudaFree(h->ctr);
   cudaSetDevice(cur);
   delete h;
   if (e != cudaSuccess) return set_error(ERR_CUDA, "stack release: %s", cudaGetErrorString(e));

@@ -70,16 +70,24 @@ int gemv_soa_tma_mode(int fmt, int mode, const GemvCall& c, cudaStream_t st);
 int gemv_aos_tma(int fmt, const GemvCall& c, cudaStream_t st);
 int read_device_error(int clear, cudaStream_t st, int* out);
 // Persistent decode stack: a sequence of single-column SoA GEMVs in one
-// cooperative launch (GEMV j usually reads GEMV j-1's y).
+// cooperative launch (GEMV j reads GEMV j-1's output).  Outputs are 8-byte
+// slots (fp32 bits | tag << 32).  With P ranks (one GPU each) every GEMV's
+// rows are also stored into the other ranks' slots (peer_y, rank order
+// without this rank).
 struct StackCall {
   const void* q;
   const void* d;
-  const float* x;
-  float* y;
-  int64_t M, K;
+  const float* x;           // GEMV 0's input floats
+  unsigned long long* y;    // this GEMV's output slots on this rank (M_total)
+  int64_t r0, M, M_total, K;
+  unsigned long long* peer_y[kMaxRanks - 1] = {};
 };
-int stack_create(int fmt, const StackCall* calls, int n, void** out);
+struct StackRanks {
+  int nranks = 1, rank = 0;
+};
+int stack_create(int fmt, const StackCall* calls, int n, const StackRanks* ranks, void** out);
 int stack_run(void* handle, cudaStream_t st);
+int stack_reset(void* handle, cudaStream_t st);
 int stack_destroy(void* handle);
 // End of a token of fused calls: signal every rank's done[k], wait (bounded)
 // until done_local reaches (*tok + 1) * nranks, then advance *tok.

@@ -1,7 +1,7 @@
 """The HBM read roof, measured three ways on the device (src/bench.cu:162-206,
 python/triton_qgemv.py:171-185): a streaming-read kernel (128-bit loads; and
 a TMA bulk-copy variant), a device-to-device copy, and a cuBLAS fp16 matvec
-of the GEMV's shape.  The streaming read is the denominator.
+of the GEMV's shape.  The read roof is the better of the two read probes.
 """
 
 from __future__ import annotations
@@ -41,10 +41,16 @@ def measure(nbytes: int = 1 << 30, batches: int = 10, calls: int = 5,
     sink = torch.zeros(4, dtype=torch.int32, device=device)
     status = torch.zeros(1, dtype=torch.int32, device=device)
     out = {"bytes": nbytes}
-    ms = time_calls(lambda i: stream_read(buf, sink, blocks_per_sm), calls, batches)
-    s = summarize(ms)
-    out["stream_read_gbps"] = nbytes / (s["median"] * 1e-3) / 1e9
-    out["stream_read_gbps_best"] = nbytes / (s["min"] * 1e-3) / 1e9
+    # the 128-bit stream read at several CTAs per SM (more bytes in flight per
+    # SM with more CTAs); the best configuration is the probe's figure
+    sweep = {}
+    for bps in sorted({blocks_per_sm, 8, 16}):
+        ms = time_calls(lambda i, b=bps: stream_read(buf, sink, b), calls, batches)
+        sweep[bps] = nbytes / (summarize(ms)["median"] * 1e-3) / 1e9
+    best = max(sweep, key=sweep.get)
+    out["stream_read_gbps"] = sweep[best]
+    out["stream_read_blocks_per_sm"] = best
+    out["stream_read_sweep_gbps"] = {str(k): round(v, 1) for k, v in sweep.items()}
     ms = time_calls(lambda i: bulk_read(buf, sink, status), calls, batches)
     s = summarize(ms)
     torch.cuda.synchronize(device)
@@ -54,6 +60,8 @@ def measure(nbytes: int = 1 << 30, batches: int = 10, calls: int = 5,
     ms = time_calls(lambda i: d2d(buf[half:], buf[:half]), calls, batches)
     s = summarize(ms)
     out["d2d_gbps"] = 2 * half / (s["median"] * 1e-3) / 1e9  # read + write
+    # the read roof: the best of the two read probes
+    out["read_roof_gbps"] = max(out["stream_read_gbps"], out["bulk_read_gbps"])
     del buf
     return out
 

@@ -86,8 +86,8 @@ class DecodeStack:
             self.fused = _FusedGather(self)
         self.persistent = None
         if persistent:
-            if self.world != 1 or fused:
-                raise ValueError("the persistent stack runs on one GPU")
+            if fused:
+                raise ValueError("choose one of fused and persistent")
             self.persistent = _PersistentStack(self)
 
     @classmethod
@@ -285,12 +285,14 @@ class _FusedGather:
 
 
 class _PersistentStack:
-    """All GEMVs of a token in one cooperative launch (``qgemv_stack_run``):
-    one CTA per SM streams the next matrix while the current one drains, and
-    grid-wide counters order GEMV j+1's reads of x after GEMV j's writes.
-    Opt-in: on 7B-shaped layers it is slower than one launch per GEMV, since
-    each CTA holds only a few tiles of a matrix and waits for the whole grid
-    before the next one."""
+    """All GEMVs of a token in one cooperative launch per rank
+    (``qgemv_stack_create`` on one GPU, ``qgemv_stack_create_ranks`` on P):
+    one CTA per SM streams the next matrices' weights while the current GEMV
+    waits for its input.  Outputs are 8-byte slots (fp32 value, tag); with P
+    ranks every GEMV stores its rows into every rank's slots (symmetric
+    memory, NVLink) and readers wait for the tag of the current token, so no
+    collective call is left on the path.  The last GEMV's full output is on
+    every rank when the launch completes."""
 
     def __init__(self, st: "DecodeStack"):
         import ctypes
@@ -299,20 +301,50 @@ class _PersistentStack:
 
         self.st, self.lib = st, _lib.lib()
         nk = len(st.shapes)
+        n = len(st.mats)
         K0 = st.mats[0].K
-        self.x_in = torch.empty(K0, dtype=torch.float32, device=st.device)
-        descs = (_lib.StackGemvDesc * len(st.mats))()
+        dev, world, rank = st.device, st.world, st.rank
+        self.x_in = torch.empty(K0, dtype=torch.float32, device=dev)
+        for m in st.mats:
+            if m.local.layout != "soa":
+                raise ValueError("the persistent stack runs on SoA planes")
+        if world > 1:
+            import torch.distributed._symmetric_memory as symm_mem
+            try:
+                symm_mem.set_backend("CUDA")
+            except Exception:
+                pass
+            group = st.group or dist.group.WORLD
+            self.slots = [symm_mem.empty(M, dtype=torch.int64, device=dev) for _, M, _ in st.shapes]
+            for t in self.slots:
+                t.zero_()
+            handles = [symm_mem.rendezvous(t, group) for t in self.slots]
+            torch.cuda.synchronize(dev)
+            dist.barrier(group)
+        else:
+            self.slots = [torch.zeros(M, dtype=torch.int64, device=dev) for _, M, _ in st.shapes]
+        descs = (_lib.StackGemvDesc * n)()
+        peers = [k for k in range(world) if k != rank]
+        self._peer_y = (ctypes.c_void_p * max(1, n * (world - 1)))()
         for j, m in enumerate(st.mats):
             q = m.local
-            if q.layout != "soa":
-                raise ValueError("the persistent stack runs on SoA planes")
-            x = self.x_in if j == 0 else st.y_local[(j - 1) % nk]
-            descs[j] = _lib.StackGemvDesc(q.q.data_ptr(), q.d.data_ptr(), x.data_ptr(),
-                                          st.y_local[j % nk].data_ptr(), m.M, m.K)
+            y = self.slots[j % nk]
+            descs[j] = _lib.StackGemvDesc(q.q.data_ptr(), q.d.data_ptr(), self.x_in.data_ptr(),
+                                          y.data_ptr(), m.r0, m.r1 - m.r0, m.M, m.K)
+            for i, k in enumerate(peers):
+                self._peer_y[j * (world - 1) + i] = handles[j % nk].buffer_ptrs[k]
         h = ctypes.c_void_p()
-        _lib.call("qgemv_stack_create", _lib.FORMAT_CODE[st.fmt], descs, len(st.mats),
-                  ctypes.byref(h))
+        fid = _lib.FORMAT_CODE[st.fmt]
+        if world > 1:
+            rk = _lib.StackRanksDesc()
+            rk.nranks, rk.rank = world, rank
+            rk.peer_y = ctypes.cast(self._peer_y, ctypes.c_void_p)
+            _lib.call("qgemv_stack_create_ranks", fid, descs, n, ctypes.byref(rk), ctypes.byref(h))
+        else:
+            _lib.call("qgemv_stack_create", fid, descs, n, ctypes.byref(h))
         self.handle = h
+        # y of the last GEMV: the low 32-bit words of its slots
+        self.out = self.slots[(n - 1) % nk].view(torch.float32)[0::2]
 
     def forward(self, x, trace=None):
         from . import _lib
@@ -324,7 +356,25 @@ class _PersistentStack:
             self.x_in.copy_(x[:self.x_in.numel()])
         _lib.call("qgemv_stack_run", self.handle,
                   torch.cuda.current_stream(st.device).cuda_stream)
-        return st.y_local[(len(st.mats) - 1) % len(st.shapes)]
+        return self.out
+
+    def reset(self):
+        """Recovery after a timed-out token: clears the device error word,
+        zeroes the output slots and the token count (on every rank: a
+        collective when P > 1)."""
+        from . import _lib
+
+        st = self.st
+        torch.cuda.synchronize(st.device)
+        if st.world > 1:
+            dist.barrier(st.group or dist.group.WORLD)
+        self.lib.qgemv_check_device_error(1, None)
+        for t in self.slots:
+            t.zero_()
+        _lib.call("qgemv_stack_reset", self.handle, None)
+        torch.cuda.synchronize(st.device)
+        if st.world > 1:
+            dist.barrier(st.group or dist.group.WORLD)
 
     def __del__(self):
         h = getattr(self, "handle", None)

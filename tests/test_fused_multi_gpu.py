@@ -1,8 +1,9 @@
-"""The fused all-gather on several GPUs of one box (one process per GPU,
-NCCL process group, symmetric memory): every rank's output of a sharded
-decode stack whose GEMV kernels store their rows into the peers' buffers
+"""The all-gather inside the kernels on several GPUs of one box (one process
+per GPU, NCCL process group, symmetric memory): every rank's output of a
+sharded decode stack whose kernels store their rows into the peers' buffers
+-- one GEMV launch per matrix (fused) or one persistent launch per token --
 equals the stack that all-gathers with NCCL, eagerly and over CUDA-graph
-replays.  Skipped with fewer than two GPUs."""
+replays, token after token.  Skipped with fewer than two GPUs."""
 
 import os
 import socket
@@ -23,7 +24,7 @@ def _free_port():
     return p
 
 
-def _worker(rank, world, port, fmt, out_q):
+def _worker(rank, world, port, fmt, mode, out_q):
     import torch.distributed as dist
     from datetime import timedelta
     from qgemv_roofline_b200 import _lib, stack
@@ -39,12 +40,15 @@ def _worker(rank, world, port, fmt, out_q):
     try:
         plain = stack.DecodeStack.from_random(fmt, n_layers=2, shapes=SHAPES, seed=8, device=dev)
         fused = stack.DecodeStack.from_random(fmt, n_layers=2, shapes=SHAPES, seed=8, device=dev,
-                                              fused=True)
+                                              fused=mode == "fused",
+                                              persistent=mode == "persistent")
         x = torch.randn(1024, device=dev, generator=torch.Generator(device=dev).manual_seed(2))
         y_plain = plain(x).clone()
         y_fused = fused(x).clone()
         torch.cuda.synchronize()
         ok = torch.equal(y_plain, y_fused)
+        for _ in range(3):  # eager tokens: the counters keep growing
+            ok = ok and torch.equal(fused(x), y_plain)
         g, out = fused.capture(x)
         for _ in range(3):
             out.zero_()
@@ -61,14 +65,16 @@ def _worker(rank, world, port, fmt, out_q):
 
 
 @pytest.mark.parametrize("fmt", ["q8_0", "q4_0"])
-def test_fused_stack_matches_nccl_stack(fmt):
+@pytest.mark.parametrize("mode", ["fused", "persistent"])
+def test_fused_stack_matches_nccl_stack(fmt, mode):
     world = min(torch.cuda.device_count(), 8)
     if world < 2:
         pytest.skip("needs two or more GPUs")
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, world, port, fmt, q)) for r in range(world)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, fmt, mode, q))
+             for r in range(world)]
     for p in procs:
         p.start()
     for p in procs:

@@ -256,3 +256,22 @@ def test_sharded_wrapper_single_process():
     sh = ShardedQGemv.from_full(full, device=DEV)
     Y = sh(torch.from_numpy(X).to(DEV), gather=True).cpu().numpy()
     assert_parity("q8_0", q, d, X, Y)
+
+
+@pytest.mark.parametrize("fmt", ["q8_0", "q4_0"])
+@pytest.mark.parametrize("N", [1, 3])
+def test_scale_plane_2_byte_aligned(fmt, N):
+    """A scale plane that starts 2 bytes past a 16-byte boundary: bulk copies
+    need 16-byte aligned sources, so these calls run on the register-streaming
+    kernels, with the same parity."""
+    M, K = 300, 4096
+    q, d, X = make(fmt, M, K, N, seed=19 + N)
+    qt = torch.from_numpy(q).to(DEV)
+    nb = M * K // 32
+    dbuf = torch.zeros(nb + 8, dtype=torch.float16, device=DEV)
+    dv = dbuf[1:1 + nb].view(M, K // 32)
+    dv.copy_(torch.from_numpy(d.view(np.float16)))
+    assert dv.data_ptr() % 16 == 2
+    Y = qg.qgemv(fmt, qt, dv, torch.from_numpy(X if N > 1 else X[0]).to(DEV)).cpu().numpy()
+    assert_parity(fmt, q, d, X, Y)
+    qg._lib.call("qgemv_check_device_error", 0, None)
