@@ -1047,6 +1047,7 @@ struct StackArgs {
 };
 
 constexpr int kStackConsumers = 16;
+constexpr int kStackXChunk = 4096;  // x elements staged in shared memory at a time
 constexpr int kStackThreads = 32 * (kStackConsumers + 1);
 
 __device__ __forceinline__ void st_slot(unsigned long long* p, float v, unsigned tag) {
@@ -1080,27 +1081,33 @@ __device__ __forceinline__ bool wait_tag2(const unsigned long long* src, int i, 
   }
 }
 
-// A lane's 32 x elements from slots (16 pairs), polled until every tag is
-// `tag`: each pass issues all pending loads at once, and between passes the
-// lane sleeps briefly so the waiting CTAs do not flood L2 with polls while
+// One consumer thread's share of x from slots: pairs i = i0, i0 + step, ...
+// below K (at most kMaxPairs of them), each stored into xs once its tag is
+// `tag`.  Every pass issues all pending loads at once; between passes the
+// thread sleeps briefly, so the waiting CTAs do not flood L2 with polls while
 // the producers' rows are still on their way.  Bounded.
-__device__ __forceinline__ bool poll_block(const unsigned long long* src, unsigned tag,
-                                           float (&v)[32], volatile int* abort_flag) {
-  uint32_t pending = 0xFFFFu;
-  long long t0 = -1, lim = 0;
-  for (;;) {
+constexpr int kMaxPairs = 16;  // K <= 16384 with 512 consumer threads
+__device__ __forceinline__ bool load_slots(const unsigned long long* src, int i0, int step, int K,
+                                           unsigned tag, float* xs, volatile int* abort_flag) {
+  uint32_t pending = 0;
 #pragma unroll
-    for (int i = 0; i < 16; ++i) {
-      if (pending & (1u << i)) {
-        const ulonglong2 w = ld_slots2(src + 2 * i);
+  for (int v = 0; v < kMaxPairs; ++v)
+    if (i0 + v * step < K) pending |= 1u << v;
+  long long t0 = -1, lim = 0;
+  while (pending) {
+#pragma unroll
+    for (int v = 0; v < kMaxPairs; ++v) {
+      if (pending & (1u << v)) {
+        const int i = i0 + v * step;
+        const ulonglong2 w = ld_slots2(src + i);
         if ((unsigned)(w.x >> 32) == tag && (unsigned)(w.y >> 32) == tag) {
-          v[2 * i] = __uint_as_float((unsigned)w.x);
-          v[2 * i + 1] = __uint_as_float((unsigned)w.y);
-          pending &= ~(1u << i);
+          xs[i] = __uint_as_float((unsigned)w.x);
+          xs[i + 1] = __uint_as_float((unsigned)w.y);
+          pending &= ~(1u << v);
         }
       }
     }
-    if (!pending) return true;
+    if (!pending) break;
     if (*abort_flag) return false;
     if (t0 < 0) {
       t0 = clock64();
@@ -1111,42 +1118,9 @@ __device__ __forceinline__ bool poll_block(const unsigned long long* src, unsign
       *abort_flag = 1;
       return false;
     }
-    __nanosleep(100);
+    __nanosleep(200);
   }
-}
-
-// One block's x planes in shared memory: 24 plane words, e, bias, finite
-// (7 x 16 bytes; a 112-byte stride keeps 8 consecutive lanes on 8 different
-// 16-byte bank groups).
-constexpr int kPlaneWords = 28;
-__device__ __forceinline__ void store_planes(uint32_t* dst, const XPlanes& xp) {
-  uint32_t w[kPlaneWords];
-#pragma unroll
-  for (int i = 0; i < 8; ++i)
-#pragma unroll
-    for (int pl = 0; pl < NPL; ++pl) w[i * NPL + pl] = xp.pl[i][pl];
-  w[24] = (uint32_t)xp.e;
-  w[25] = __float_as_uint(xp.bias);
-  w[26] = xp.finite ? 1u : 0u;
-  w[27] = 0u;
-#pragma unroll
-  for (int i = 0; i < kPlaneWords / 4; ++i)
-    *reinterpret_cast<uint4*>(dst + 4 * i) = make_uint4(w[4 * i], w[4 * i + 1], w[4 * i + 2], w[4 * i + 3]);
-}
-__device__ __forceinline__ void load_planes(const uint32_t* src, XPlanes& xp) {
-  uint32_t w[kPlaneWords];
-#pragma unroll
-  for (int i = 0; i < kPlaneWords / 4; ++i) {
-    const uint4 q = *reinterpret_cast<const uint4*>(src + 4 * i);
-    w[4 * i] = q.x; w[4 * i + 1] = q.y; w[4 * i + 2] = q.z; w[4 * i + 3] = q.w;
-  }
-#pragma unroll
-  for (int i = 0; i < 8; ++i)
-#pragma unroll
-    for (int pl = 0; pl < NPL; ++pl) xp.pl[i][pl] = w[i * NPL + pl];
-  xp.e = (int)w[24];
-  xp.bias = __uint_as_float(w[25]);
-  xp.finite = w[26] != 0u;
+  return true;
 }
 
 // R rows of one lane's block from SoA planes in shared memory (quants at
@@ -1181,8 +1155,8 @@ __global__ void __launch_bounds__(kStackThreads, 1) k_gemv_stack(const __grid_co
   extern __shared__ __align__(128) uint8_t sm[];
   __shared__ __align__(8) unsigned long long full[MAX_STAGES];
   __shared__ __align__(8) unsigned long long empty[MAX_STAGES];
-  __shared__ __align__(8) unsigned long long pready;  // the x planes of this GEMV are published
-  __shared__ __align__(8) unsigned long long pread;   // every consumer warp has them
+  __shared__ __align__(8) unsigned long long xload;  // every consumer warp has stored its part of x
+  __shared__ __align__(8) unsigned long long xconv;  // every consumer warp has its planes
   __shared__ int abort_flag;
 
   const int S = p.S, G = gridDim.x, b = blockIdx.x;
@@ -1195,8 +1169,8 @@ __global__ void __launch_bounds__(kStackThreads, 1) k_gemv_stack(const __grid_co
       asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(saddr(&empty[s])),
                    "r"(CONSUMERS));
     }
-    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(saddr(&pready)), "r"(CONSUMERS));
-    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(saddr(&pread)), "r"(CONSUMERS));
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(saddr(&xload)), "r"(CONSUMERS));
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(saddr(&xconv)), "r"(CONSUMERS));
     abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
@@ -1330,7 +1304,7 @@ __global__ void __launch_bounds__(kStackThreads, 1) k_gemv_stack(const __grid_co
 
   // -------------------------------------------------------------- consumers
   const int cw = warp - 1, ct = threadIdx.x - 32;  // consumer warp / thread
-  uint32_t u = 0, pph = 0;  // tiles consumed; GEMVs whose planes were shared (pready / pread)
+  uint32_t u = 0, xph = 0;  // tiles consumed; x chunks staged (xload / xconv phases)
   for (int j = 0; j < p.n; ++j) {
     // this GEMV's parameters in registers (the asm statements below clobber
     // memory, so fields read through p.g would be reloaded in every pass)
@@ -1345,63 +1319,41 @@ __global__ void __launch_bounds__(kStackThreads, 1) k_gemv_stack(const __grid_co
     const int c = ks * 32 + lane;
     const bool cval = c < K / QK;
     const int cidx = cval ? c : 0;
-    // x of GEMV j as the lane's block planes.  The warps of row group 0 cover
-    // every block once: each of their lanes loads its 32 elements (GEMV 0:
-    // the input floats; GEMV j > 0: GEMV j-1's output slots, polled until
-    // their tags show this token's values) and converts them.  With more than
-    // one row group they publish the planes in shared memory and the other
-    // warps copy them from there, so every x element crosses L2 once per CTA.
-    // (mbarriers with bounded waits, not named barriers: a warp that gives up
-    // must not leave the others waiting without limit.)
+    // x of GEMV j into shared memory, kStackXChunk elements at a time (a small
+    // staging area leaves room for a deeper weight ring): GEMV 0 reads its
+    // input floats; GEMV j > 0 reads GEMV j-1's output slots, each once its
+    // tag shows this token's value.  Each lane converts its block when the
+    // chunk holding it is staged.  (mbarriers with bounded waits, not named
+    // barriers: a warp that gives up must not leave the others waiting
+    // without limit.)
     XPlanes xp;
     for (int w = 0; w < 8; ++w)
       for (int pl = 0; pl < NPL; ++pl) xp.pl[w][pl] = 0u;
     xp.e = -149;
     xp.bias = 0.0f;
     xp.finite = true;
-    const bool share = RG > 1;
-    uint32_t* pslot = reinterpret_cast<uint32_t*>(xs) + cidx * kPlaneWords;
-    if (rg == 0) {
+    for (int k0 = 0; k0 < K; k0 += kStackXChunk, ++xph) {
+      const int kn = min(kStackXChunk, K - k0);
       bool ok = true;
-      if (share && pph > 0)  // the other warps have copied the previous planes
-        ok = mbar_wait(saddr(&pread), (pph - 1u) & 1u, &abort_flag);
-      if (ok && cval) {
-        float v[32];
-        if (j == 0) {
-#pragma unroll
-          for (int i = 0; i < 8; ++i) {
-            const float4 f4 = *reinterpret_cast<const float4*>(gx + cidx * 32 + 4 * i);
-            v[4 * i] = f4.x; v[4 * i + 1] = f4.y; v[4 * i + 2] = f4.z; v[4 * i + 3] = f4.w;
-          }
-        } else {
-          ok = poll_block(gsrc + cidx * 32, tag0 + (unsigned)(j - 1), v, &abort_flag);
-        }
-        if (ok) make_planes_from(v, xp);
+      if (j == 0) {
+        for (int i = 4 * ct; i < kn; i += 4 * 32 * CONSUMERS)
+          *reinterpret_cast<float4*>(xs + i) = *reinterpret_cast<const float4*>(gx + k0 + i);
+      } else {
+        ok = load_slots(gsrc + k0, 2 * ct, 2 * 32 * CONSUMERS, kn, tag0 + (unsigned)(j - 1), xs,
+                        &abort_flag);
       }
       if (!__all_sync(0xffffffffu, ok)) return;
-      if (share) {
-        if (cval) store_planes(pslot, xp);
-        __syncwarp();
-        if (lane == 0) {
-          asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(saddr(&pready)) : "memory");
-          asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(saddr(&pread)) : "memory");
-        }
-        // Every warp leaves only once this phase is complete: a warp that ran
-        // ahead (its tiles of this GEMV already in the ring) would otherwise
-        // arrive for the next GEMV's phase before this one completes and be
-        // counted in it.
-        if (!__all_sync(0xffffffffu, mbar_wait(saddr(&pready), pph & 1u, &abort_flag))) return;
-      }
-    } else {
       if (lane == 0)
-        asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(saddr(&pready)) : "memory");
-      if (!__all_sync(0xffffffffu, mbar_wait(saddr(&pready), pph & 1u, &abort_flag))) return;
-      if (cval) load_planes(pslot, xp);
+        asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(saddr(&xload)) : "memory");
+      if (!__all_sync(0xffffffffu, mbar_wait(saddr(&xload), xph & 1u, &abort_flag))) return;
+      const int e0 = cidx * QK - k0;  // the lane's block inside this chunk?
+      if (cval && e0 >= 0 && e0 < kn) make_planes_smem(saddr(xs) + (uint32_t)(e0 * 4), lane, xp);
+      // every consumer has its planes before the next chunk overwrites xs
       __syncwarp();
       if (lane == 0)
-        asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(saddr(&pread)) : "memory");
+        asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(saddr(&xconv)) : "memory");
+      if (!__all_sync(0xffffffffu, mbar_wait(saddr(&xconv), xph & 1u, &abort_flag))) return;
     }
-    if (share) ++pph;
     const XScale xq = x_scale<FMT>(xp);
     const bool fast = __all_sync(0xffffffffu, !cval || xq.fast);  // as in k_gemv_tma
     for (int t = 0; t < ntiles; ++t, ++u) {
@@ -1808,8 +1760,7 @@ int stack_create(int fmt, const StackCall* calls, int n, const StackRanks* ranks
     g[j] = s;
     SB = std::max(SB, (TR * row + 15) / 16 * 16);
     PB = std::max(PB, (TR * KS + 3) / 4 * 4);  // keeps the x area 16-byte aligned
-    if (kStackConsumers / KS > 1)  // planes shared through shared memory
-      XB = std::max(XB, nunits * kPlaneWords * 4);
+    XB = std::max(XB, (int)std::min<int64_t>(c.K, kStackXChunk) * 4);
   }
   const void* kp = reinterpret_cast<const void*>(stack_kernel(fmt));
   if (int rc = allow_max_smem(kp, dev)) return rc;
