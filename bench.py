@@ -348,11 +348,12 @@ def batch_workload(args, rank, world, dev):
 
 
 def single_column_records(args, rank, world, dev, M, K, calls, read_roof, peak,
-                          min_copies=16):
+                          min_copies=16, layout="soa"):
     """One q8_0 and one q4_0 GEMV of W [M, K] (rows sharded over the ranks, x
     replicated), weights rotated over max(min_copies, >= 4x L2) copies;
-    `calls` timed calls per format.  us per call (max over ranks), aggregate
-    GB/s, and the per-GPU fraction of the read roof and of the measured peak."""
+    `calls` timed calls per format; layout "soa" (planes) or "aos" (GGUF
+    blocks, no repack).  us per call (max over ranks), aggregate GB/s, and the
+    per-GPU fraction of the read roof and of the measured peak."""
     import torch
     import torch.distributed as dist
 
@@ -366,11 +367,15 @@ def single_column_records(args, rank, world, dev, M, K, calls, read_roof, peak,
     cl, copies = [], {}
     for fmt in ("q8_0", "q4_0"):
         c = max(min_copies, math.ceil(4 * L2_BYTES / wbytes(fmt, rows, K)))
-        q, d = (qg.quantize_q8_0 if fmt == "q8_0" else qg.quantize_q4_0)(W)
         copies[fmt] = c
-        cl.append({"fmt": fmt, "layout": "soa", "M": rows, "K": K, "x": x,
-                   "y": torch.empty(rows, device=dev),
-                   "copies": [(q, d)] + [(q.clone(), d.clone()) for _ in range(c - 1)]})
+        if layout == "soa":
+            q, d = (qg.quantize_q8_0 if fmt == "q8_0" else qg.quantize_q4_0)(W)
+            cps = [(q, d)] + [(q.clone(), d.clone()) for _ in range(c - 1)]
+        else:
+            bl = (qg.quantize_q8_0_aos if fmt == "q8_0" else qg.quantize_q4_0_aos)(W)
+            cps = [bl] + [bl.clone() for _ in range(c - 1)]
+        cl.append({"fmt": fmt, "layout": layout, "M": rows, "K": K, "x": x,
+                   "y": torch.empty(rows, device=dev), "copies": cps})
     del W
     if world > 1:
         dist.barrier()
@@ -379,7 +384,7 @@ def single_column_records(args, rank, world, dev, M, K, calls, read_roof, peak,
     t = torch.tensor(per, dtype=torch.float64, device=dev)
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    rec = {"M": M, "K": K, "rows_per_gpu": rows, "calls": calls}
+    rec = {"M": M, "K": K, "rows_per_gpu": rows, "calls": calls, "layout": layout}
     for fmt, ms in zip(("q8_0", "q4_0"), t.tolist()):
         us = ms / calls * 1e3
         gb = alg_bytes(fmt, rows, K) / (us * 1e-6) / 1e9
@@ -887,6 +892,10 @@ def main():
             args, rank, world, dev, 4096, 4096, 2000, read_roof, peak))
         guarded("L_11008x4096", lambda: single_column_records(
             args, rank, world, dev, 11008, 4096, 2000, read_roof, peak))
+        # the headline shape straight from GGUF blocks (no repack), rows sharded
+        guarded("XL_ggml_blocks_98304x4096", lambda: single_column_records(
+            args, rank, world, dev, M_FULL, K_FULL, max(200, min(args.steps, 2000)), read_roof,
+            peak, min_copies=2, layout="aos"))
 
         def sb():
             recs = batch_records(args, rank, world, dev, 200, 10)
