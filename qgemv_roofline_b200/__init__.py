@@ -7,6 +7,7 @@ Public API (torch tensors as buffers; compute in libqgemv_b200.so):
   ``dequant_q4_0``, plus ``to_aos`` / ``from_aos`` and ``quantize_*_aos``;
 * GEMV: ``qgemv(fmt, q, d, x)``, ``qgemv_aos(fmt, blocks, x)``,
   ``qgemv_tiled(fmt, tile_weights(fmt, q, d), M, K, X)`` (batch tiles),
+  ``qgemv_tc(tile_weights_tc(q, d), M, K, X)`` (q8_0 on the tcgen05 tensor cores),
   ``QuantizedMatrix``;
 * GGUF files: ``gguf.GGUFReader`` (load q8_0 / q4_0 tensors onto a GPU), ``gguf.write_gguf``;
 * roof probes: ``roof.measure``, ``roof.cublas_fp16_mv``;
@@ -17,7 +18,7 @@ Public API (torch tensors as buffers; compute in libqgemv_b200.so):
 from . import _lib, gemv, gguf, qformats, roof, shard, stack, timing  # noqa: F401
 from ._lib import QGemvError, device_info  # noqa: F401
 from .gemv import (QuantizedMatrix, algorithmic_bytes, qgemv, qgemv_aos,  # noqa: F401
-                   qgemv_tiled, tile_weights)
+                   qgemv_tc, qgemv_tiled, tile_weights, tile_weights_tc)
 from .qformats import (QK, dequant_q4_0, dequant_q8_0, from_aos, quantize_q4_0,  # noqa: F401
                        quantize_q4_0_aos, quantize_q8_0, quantize_q8_0_aos, to_aos, weight_bytes)
 

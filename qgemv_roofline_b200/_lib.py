@@ -130,6 +130,11 @@ SIGNATURES = {
     "qgemv_tiled_workspace_bytes": ([_i64, _i32], ctypes.c_size_t),
     "qgemv_tiled_gemv": ([ctypes.c_int, _vp, _i64, _i64, _vp, _vp, _i32, _i64, _i64, _vp,
                           ctypes.c_size_t, _vp], ctypes.c_int),
+    "qgemv_q8_0_tc_bytes": ([_i64, _i64], ctypes.c_size_t),
+    "qgemv_q8_0_tc_tile": ([ctypes.c_int, _vp, _vp, _i64, _i64, _vp, _vp], ctypes.c_int),
+    "qgemv_q8_0_tc_workspace_bytes": ([_i64, _i64], ctypes.c_size_t),
+    "qgemv_q8_0_tc": ([_vp, _i64, _i64, _vp, _vp, _i32, _i64, _i64, _vp, ctypes.c_size_t, _vp],
+                      ctypes.c_int),
     "qgemv_quantize_soa": ([ctypes.c_int, _vp, _i64, _i64, _i64, _vp, _vp, _vp], ctypes.c_int),
     "qgemv_quantize_aos": ([ctypes.c_int, _vp, _i64, _i64, _i64, _vp, _vp], ctypes.c_int),
     "qgemv_dequant_soa": ([ctypes.c_int, _vp, _vp, _vp, _i64, _i64, _vp], ctypes.c_int),

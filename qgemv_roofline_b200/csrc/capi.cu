@@ -344,10 +344,12 @@ QGEMV_API int qgemv_soa_variant(int format, int variant, int32_t grid, const voi
 }
 
 QGEMV_API int qgemv_check_device_error(int clear, void* stream) {
-  int v = 0, w = 0;
+  int v = 0, w = 0, t = 0;
   if (int rc = read_device_error(clear, static_cast<cudaStream_t>(stream), &v)) return rc;
   if (int rc = read_mma_error(clear, static_cast<cudaStream_t>(stream), &w)) return rc;
+  if (int rc = read_tc_error(clear, static_cast<cudaStream_t>(stream), &t)) return rc;
   if (!v) v = w;
+  if (!v) v = t;
   if (v) return set_error(v, "a kernel reported %s on the device", qgemv_status_string(v));
   return OK;
 }
@@ -364,7 +366,8 @@ QGEMV_API int qgemv_set_wait_limit(int64_t microseconds) {
     if (cycles < 1) cycles = 1;
   }
   if (int rc = set_spin_limit(cycles)) return rc;
-  return set_mma_spin_limit(cycles);
+  if (int rc = set_mma_spin_limit(cycles)) return rc;
+  return set_tc_spin_limit(cycles);
 }
 
 QGEMV_API int32_t qgemv_tile_counters_used(int device) { return tile_counters_used(device); }
@@ -649,6 +652,73 @@ QGEMV_API int qgemv_tiled_gemv(int format, const void* tiled, int64_t M, int64_t
     c.x = x + (int64_t)n0 * ldx;
     c.y = y + (int64_t)n0 * ldy;
     if (int rc = gemv_tiled(format, c, st)) return rc;
+  }
+  return OK;
+}
+
+QGEMV_API size_t qgemv_q8_0_tc_bytes(int64_t M, int64_t K) {
+  if (check_mk(M, K)) return 0;
+  return tc_tiles_bytes(M, K);
+}
+
+QGEMV_API int qgemv_q8_0_tc_tile(int layout, const void* q, const void* d, int64_t M, int64_t K,
+                                 void* tiles, void* stream) {
+  if (int rc = check_mk(M, K)) return rc;
+  if (layout != 0 && layout != 1)
+    return set_error(ERR_ARG, "layout must be 0 (SoA planes) or 1 (ggml blocks), got %d", layout);
+  if (M == 0 || K == 0) return OK;
+  if (!q || !tiles || (layout == 0 && !d))
+    return set_error(ERR_NULL, "source and destination must not be NULL");
+  if (misaligned(tiles, 16)) return set_error(ERR_ALIGN, "tiles must be 16-byte aligned");
+  if (layout == 0 && (misaligned(q, 16) || misaligned(d, 2)))
+    return set_error(ERR_ALIGN, "q must be 16-byte and d 2-byte aligned");
+  return tile_weights_tc(layout == 1, q, d, M, K, tiles, static_cast<cudaStream_t>(stream));
+}
+
+QGEMV_API size_t qgemv_q8_0_tc_workspace_bytes(int64_t M, int64_t K) {
+  if (check_mk(M, K)) return 0;
+  DeviceInfo dev;
+  if (current_device_info(dev)) return 0;
+  return tc_workspace_bytes(M, K, dev.sms);
+}
+
+QGEMV_API int qgemv_q8_0_tc(const void* tiles, int64_t M, int64_t K, const float* x, float* y,
+                            int32_t ncols, int64_t ldx, int64_t ldy, void* workspace,
+                            size_t workspace_bytes, void* stream) {
+  if (int rc = check_mk(M, K)) return rc;
+  if (K > ((int64_t)1 << 20))
+    return set_error(ERR_UNSUPPORTED, "K=%lld above 2^20 for tc tiles", (long long)K);
+  if (ncols < 0) return set_error(ERR_SHAPE, "ncols=%d is negative", ncols);
+  if (M == 0 || ncols == 0) return OK;
+  if (!y || (K > 0 && (!x || !tiles))) return set_error(ERR_NULL, "tiles, x and y must not be NULL");
+  if (ncols > 1 && ldx < K) return set_error(ERR_SHAPE, "ldx=%lld < K=%lld", (long long)ldx, (long long)K);
+  if (ncols > 1 && ldy < M) return set_error(ERR_SHAPE, "ldy=%lld < M=%lld", (long long)ldy, (long long)M);
+  if (ncols == 1) {
+    ldx = K;
+    ldy = M;
+  }
+  if (K > 0 && misaligned(tiles, 16)) return set_error(ERR_ALIGN, "tiles must be 16-byte aligned");
+  if (misaligned(x, 4) || misaligned(y, 4)) return set_error(ERR_ALIGN, "x and y must be 4-byte aligned");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (K == 0) return fill_zero_rows(y, M, ncols, ldy, st);
+  DeviceInfo dev;
+  if (int rc = current_device_info(dev)) return rc;
+  const size_t need = tc_workspace_bytes(M, K, dev.sms);
+  if (workspace) {
+    if (workspace_bytes < need)
+      return set_error(ERR_ARG, "this call needs a workspace of %zu bytes, got %zu", need,
+                       workspace_bytes);
+    if (misaligned(workspace, 16)) return set_error(ERR_ALIGN, "workspace must be 16-byte aligned");
+  } else if (int rc = stream_workspace(st, need, &workspace)) {
+    return rc;
+  } else {
+    workspace_bytes = need;
+  }
+  for (int n0 = 0; n0 < ncols; n0 += 16) {
+    const int n = std::min(16, ncols - n0);
+    if (int rc = gemv_tc(tiles, M, K, x + (int64_t)n0 * ldx, ldx, y + (int64_t)n0 * ldy, ldy, n,
+                         workspace, workspace_bytes, st))
+      return rc;
   }
   return OK;
 }

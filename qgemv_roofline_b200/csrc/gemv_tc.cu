@@ -1,0 +1,729 @@
+// Small-batch q8_0 GEMV on the 5th-generation tensor cores (tcgen05, sm_100a).
+//
+// Y[n][r] = sum_b d[r][b] * sum_j q[r][32b + j] * X[n][32b + j] for up to 16
+// columns n per launch, the weights streamed once.  One ggml block is one
+// MMA: tcgen05.mma kind::i8 with K = 32 multiplies the block's int8 quants
+// (the A operand, read by the tensor core straight from shared memory: no
+// conversion instruction) by the block's activations in exact integer form,
+// and leaves the integer block dots in tensor memory (TMEM), where the CUDA
+// cores scale them once per block:
+//
+//  * x (prep kernel, one CTA per column): each column is normalised by an
+//    exact power of two 2^sh (max |x'| in [2^14, 2^15)); each 32-element
+//    block of it is rounded to block fixed point X_j = rint(x'_j 2^(22-e)),
+//    |x'| < 2^e on the block, |X_j| <= 2^22, and split into three signed
+//    byte digits X = p0 + 2^8 p1 + 2^16 p2 (p0, p1 in [-128, 127], p2 in
+//    [-64, 64]).  The digits are the B operand, row plane * NC + column, so
+//    one MMA (M = 128 rows, N = 32 or 48, K = 32) computes the three plane
+//    sums S_p of every column for 128 rows and one block, exactly
+//    (|S_p| < 2^19).
+//  * epilogue (8 warps; TMEM lane = row): lo = S0 + 2^8 S1 (exact in int32),
+//    F = 2^16 S2 + lo in fp32, acc[n] += F * (d * 2^(e-22)); y = acc 2^-sh.
+//    The rounding of x to the 2^(e-22) grid moves a row's dot by at most
+//    2^-23 sqrt(32) ||w|| ||x|| (Cauchy-Schwarz over each block), the fp32
+//    steps by a few ulps of the block terms: well inside 1e-5 ||w|| ||x||.
+//    A column holding a NaN or an infinity gives NaN in every row.
+//
+// Weights are "tc tiles" (qgemv_q8_0_tc_tile, a one-time re-layout): per
+// 128 rows x 256 columns one contiguous tile, the quants in the canonical
+// 128-byte-swizzled K-major layout the tensor core reads (2 boxes of
+// [128 rows][128 bytes]; 16-byte chunk c of row r at chunk position
+// c ^ (r % 8) of its 128-byte row; rows in groups of 8 at 1024 bytes), then
+// the [128 rows][8 blocks] fp16 scales; rows beyond M and columns beyond K
+// hold zero weights.  The tiles of one 128-row tile are consecutive in K.
+//
+// The (row tile, K tile) units are split evenly over one CTA per SM (a unit
+// is 34 KB of weights: the imbalance is at most one unit).  A row tile that
+// two or more CTAs share is finished by the CTA that completes its part
+// last (a counter per row tile): it adds the CTAs' partial sums in CTA order,
+// so results do not depend on timing.
+//
+// Per CTA (10 warps): warp 0 streams (weight tile, x tile) pairs into a
+// 4-stage shared-memory ring (bulk copies); one thread of warp 1 issues the
+// 8 MMAs of a stage, each half tile (4 blocks) into one slot of a TMEM ring
+// (4 slots of 4 x 32 columns, or 2 of 4 x 48), and commits each half to an
+// mbarrier; warps 2..9 (two groups of four, one warp per TMEM lane quarter,
+// group g taking half g of every tile) read a whole slot back with one wait
+// (tcgen05.ld), release it and accumulate: the TMEM read latency is paid
+// once per half tile, not once per block.  Every wait is bounded (the
+// library's wait limit): on timeout the error word records
+// QGEMV_ERR_TIMEOUT, the producer stops and waits for its copies, the MMA
+// thread stops issuing, the epilogue runs out its loop without waiting, and
+// the CTA frees its TMEM before it returns.
+#include "qgemv_common.cuh"
+#include "qgemv_internal.h"
+
+#include <algorithm>
+
+namespace qg {
+
+__device__ int g_tc_error = 0;
+__device__ long long g_tc_spin_limit = kDefaultSpinLimit;
+
+namespace {
+
+constexpr int TC_M = 128;                       // rows per tile (MMA M)
+constexpr int TC_KT = 256;                      // K per tile
+constexpr int TC_BLK = TC_KT / QK;              // blocks per tile (8)
+constexpr int TC_ABYTES = TC_M * TC_KT;         // quants of a tile
+constexpr int TC_BOX = TC_M * 128;              // one 128-byte-wide box of quants
+constexpr int TC_DBYTES = TC_M * TC_BLK * 2;    // fp16 scales of a tile
+constexpr int TC_TILE = TC_ABYTES + TC_DBYTES;  // 34816 bytes, a multiple of 1024
+constexpr int TC_BPS = TC_BLK / 2;              // blocks per TMEM slot (half a tile)
+constexpr int TC_TMEM_COLS = 512;
+constexpr int TC_GROUPS = 2;                    // epilogue warp groups (one per tile half)
+constexpr int TC_EPI = 4 * TC_GROUPS;           // epilogue warps
+constexpr int TC_THREADS = 32 * (2 + TC_EPI);
+constexpr int TC_STAGES = 4;
+constexpr int TC_HDR = 128;                     // workspace header: sh[16], nonfinite[16]
+
+template <int NC>
+struct TcCfg {
+  static constexpr int NB = NC == 16 ? 48 : 32;       // MMA N = B rows (3 * NC used)
+  static constexpr int BBOX = NB * 128;               // one box of x digits
+  static constexpr int XB = 2 * BBOX;                 // x digits of a K tile
+  static constexpr int XSB = TC_BLK * NC * 4;         // block scales [block][column] fp32
+  static constexpr int XT = XB + XSB;                 // x tile bytes (multiple of 16)
+  static constexpr int STAGE = (TC_TILE + XT + 1023) / 1024 * 1024;
+  static constexpr int RED = TC_GROUPS * NC * TC_M * 4;  // group reduction scratch
+  static constexpr int SLOTS = TC_TMEM_COLS / (TC_BPS * NB);  // TMEM slots: 4 (NB 32), 2 (NB 48)
+  static constexpr int ROUNDS = NC == 16 ? 2 : 1;     // TMEM reads per slot (registers)
+  static constexpr size_t SMEM = (size_t)TC_STAGES * STAGE + RED + 1024;
+  // kind::i8: s32 accumulators (bits 4-5 = 2), A and B signed (bits 7-9,
+  // 10-12 = 1), both K-major (bits 15, 16 = 0), N >> 3 at bit 17, M >> 4 at 24
+  static constexpr uint32_t IDESC = (2u << 4) | (1u << 7) | (1u << 10) |
+                                    ((uint32_t)(NB >> 3) << 17) | ((uint32_t)(TC_M >> 4) << 24);
+};
+static_assert(TcCfg<16>::SMEM <= 227 * 1024, "ring too large");
+static_assert(TcCfg<16>::SLOTS >= 2 && TcCfg<8>::SLOTS >= 2, "TMEM slots");
+static_assert(TC_TILE % 1024 == 0, "B operand must stay 1024-byte aligned");
+
+__device__ __forceinline__ long long tc_spin_limit() {
+  return *(volatile long long*)&g_tc_spin_limit;
+}
+__device__ __forceinline__ uint32_t saddr(const void* p) {
+  return (uint32_t)__cvta_generic_to_shared(p);
+}
+__device__ __forceinline__ bool mbar_try(uint32_t bar, uint32_t parity) {
+  uint32_t done;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
+      " selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(done)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return done != 0;
+}
+// Bounded wait; gives up at once when another thread raised the abort flag.
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort_flag) {
+  if (mbar_try(bar, parity)) return true;
+  const long long t0 = clock64(), lim = tc_spin_limit();
+  while (!mbar_try(bar, parity)) {
+    if (*abort_flag) return false;
+    if (clock64() - t0 > lim) {
+      atomicExch(&g_tc_error, (int)ERR_TIMEOUT);
+      __threadfence();
+      *abort_flag = 1;
+      return false;
+    }
+  }
+  return true;
+}
+// Wait for copies and MMAs in flight (they complete on their own) before the
+// CTA exits: ignores the abort flag, bounded by the default limit even when
+// the configured one is shorter.
+__device__ __forceinline__ void mbar_wait_drain(uint32_t bar, uint32_t parity) {
+  const long long t0 = clock64(), lim = max(tc_spin_limit(), kDefaultSpinLimit);
+  while (!mbar_try(bar, parity) && clock64() - t0 < lim) {
+  }
+}
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count));
+}
+__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes)
+               : "memory");
+}
+__device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::
+          "r"(dst),
+      "l"(src), "r"(bytes), "r"(bar)
+      : "memory");
+}
+__device__ __forceinline__ void epi_sync() {
+  asm volatile("bar.sync 1, %0;" ::"n"(TC_EPI * 32) : "memory");
+}
+
+// Shared-memory matrix descriptor of a K-major operand in the canonical
+// 128-byte-swizzled layout: start address >> 4 (bits 0-13), leading byte
+// offset 16 >> 4 (bits 16-29; not used by swizzled K-major operands), stride
+// byte offset 1024 >> 4 between 8-row groups (bits 32-45), descriptor version
+// 1 (bits 46-47), base offset 0 (atoms 1024-byte aligned), layout type 2 =
+// SWIZZLE_128B (bits 61-63).  Block b of a box starts 32 * b bytes into the
+// atom row: the hardware applies the swizzle to the computed addresses.
+__device__ __forceinline__ uint64_t sw128_desc(uint32_t addr) {
+  return (uint64_t)((addr >> 4) & 0x3FFFu) | ((uint64_t)1u << 16) | ((uint64_t)(1024u >> 4) << 32) |
+         ((uint64_t)1u << 46) | ((uint64_t)2u << 61);
+}
+
+__device__ __forceinline__ void tc_fence_before() {
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_after() {
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_commit(uint32_t bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                   bar)
+               : "memory");
+}
+
+// 32 lanes x NC consecutive 32-bit TMEM columns.
+template <int NC>
+__device__ __forceinline__ void tmem_ld(uint32_t ta, uint32_t (&v)[NC]) {
+  if constexpr (NC == 2) {
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x2.b32 {%0, %1}, [%2];"
+                 : "=r"(v[0]), "=r"(v[1])
+                 : "r"(ta));
+  } else if constexpr (NC == 4) {
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x4.b32 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3])
+                 : "r"(ta));
+  } else if constexpr (NC == 8) {
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
+                 : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]),
+                   "=r"(v[6]), "=r"(v[7])
+                 : "r"(ta));
+  } else {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, "
+        "%11, %12, %13, %14, %15}, [%16];"
+        : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]),
+          "=r"(v[7]), "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]),
+          "=r"(v[14]), "=r"(v[15])
+        : "r"(ta));
+  }
+}
+
+struct TcArgs {
+  const uint8_t* tiles;  // tc tiles [row tile][K tile]
+  uint8_t* ws;           // header, counters, partial sums, x tiles
+  float* y;
+  int64_t ldy;
+  int M, N, nkt, ntiles;
+  int cnt_off, part_off, xt_off;  // workspace offsets (bytes)
+};
+
+// The CTA that owns unit u when U units are split over G CTAs as
+// [U c / G, U (c + 1) / G).
+__device__ __forceinline__ int cta_of(int64_t u, int64_t U, int G) {
+  return (int)(((u + 1) * G + U - 1) / U) - 1;
+}
+
+__device__ __forceinline__ float finish(float tot, const int* hdr, int c) {
+  return hdr[16 + c] ? __int_as_float(0x7FC00000) : ldexpf(tot, -hdr[c]);
+}
+
+template <int NC>
+__global__ void __launch_bounds__(TC_THREADS, 1) k_gemv_tc(const __grid_constant__ TcArgs p) {
+  using C = TcCfg<NC>;
+  extern __shared__ uint8_t tc_smem_raw[];
+  __shared__ __align__(8) unsigned long long full[TC_STAGES];
+  __shared__ __align__(8) unsigned long long empty[TC_STAGES];
+  __shared__ __align__(8) unsigned long long tfull[4];
+  __shared__ __align__(8) unsigned long long tempty[4];
+  __shared__ __align__(8) unsigned long long mma_done;
+  __shared__ uint32_t tmem_base;
+  __shared__ int abort_flag;
+  __shared__ int last_flag;
+
+  // 1024-byte-aligned ring (the swizzle works on address bits)
+  uint8_t* ring = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(tc_smem_raw) + 1023) & ~(uintptr_t)1023);
+  float* red = reinterpret_cast<float*>(ring + (size_t)TC_STAGES * C::STAGE);
+  const uint32_t ring_s = saddr(ring);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t U = (int64_t)p.ntiles * p.nkt;
+  const int64_t u0 = U * blockIdx.x / gridDim.x, u1 = U * (blockIdx.x + 1) / gridDim.x;
+  const int nunits = (int)(u1 - u0);
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < TC_STAGES; ++s) {
+      mbar_init(saddr(&full[s]), 1);
+      mbar_init(saddr(&empty[s]), 1 + TC_EPI);  // the MMA commit + every epilogue warp
+    }
+    for (int s = 0; s < C::SLOTS; ++s) {
+      mbar_init(saddr(&tfull[s]), 1);
+      mbar_init(saddr(&tempty[s]), 4);  // the four lane-quarter warps of one group
+    }
+    mbar_init(saddr(&mma_done), 1);
+    abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 1) {  // all of TMEM: one CTA per SM (shared memory)
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     saddr(&tmem_base)),
+                 "r"(TC_TMEM_COLS)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = tmem_base;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      // weights do not depend on the previous kernel: prefetch them first
+      const int pre = min(TC_STAGES, nunits);
+      for (int i = 0; i < pre; ++i) {
+        const uint32_t bar = saddr(&full[i]);
+        mbar_expect_tx(bar, (uint32_t)(TC_TILE + C::XT));
+        bulk_g2s(ring_s + (uint32_t)(i * C::STAGE), p.tiles + (u0 + i) * TC_TILE, TC_TILE, bar);
+      }
+      asm volatile("griddepcontrol.wait;" ::: "memory");  // x tiles are written by the prep kernel
+      for (int i = 0; i < pre; ++i) {
+        const int kt = (int)((u0 + i) % p.nkt);
+        bulk_g2s(ring_s + (uint32_t)(i * C::STAGE + TC_TILE), p.ws + p.xt_off + (int64_t)kt * C::XT,
+                 C::XT, saddr(&full[i]));
+      }
+      int issued = pre;
+      for (int i = pre; i < nunits; ++i) {
+        const int s = i % TC_STAGES;
+        if (!mbar_wait(saddr(&empty[s]), (uint32_t)(((i / TC_STAGES) - 1) & 1), &abort_flag)) break;
+        const int64_t u = u0 + i;
+        const int kt = (int)(u % p.nkt);
+        const uint32_t bar = saddr(&full[s]);
+        const uint32_t dst = ring_s + (uint32_t)(s * C::STAGE);
+        mbar_expect_tx(bar, (uint32_t)(TC_TILE + C::XT));
+        bulk_g2s(dst, p.tiles + u * TC_TILE, TC_TILE, bar);
+        bulk_g2s(dst + TC_TILE, p.ws + p.xt_off + (int64_t)kt * C::XT, C::XT, bar);
+        issued = i + 1;
+      }
+      if (issued < nunits)  // aborted: wait (bounded) for the copies still in flight
+        for (int i = max(0, issued - TC_STAGES); i < issued; ++i)
+          mbar_wait_drain(saddr(&full[i % TC_STAGES]), (uint32_t)((i / TC_STAGES) & 1));
+    }
+  } else if (warp == 1) {
+    // ---------------------------------------------------------- MMA issuer
+    if (lane == 0) {
+      bool ok = true;
+      for (int i = 0; i < nunits && ok; ++i) {
+        const int s = i % TC_STAGES;
+        ok = mbar_wait(saddr(&full[s]), (uint32_t)((i / TC_STAGES) & 1), &abort_flag);
+        if (!ok) break;
+        tc_fence_after();
+        const uint32_t a0 = ring_s + (uint32_t)(s * C::STAGE);
+        const uint32_t b0 = a0 + TC_TILE;
+        // tile half h (blocks 4h .. 4h + 3) into slot hh % SLOTS, hh = 2i + h
+        for (int h = 0; h < 2 && ok; ++h) {
+          const uint32_t hh = 2u * i + h, slot = hh % C::SLOTS;
+          if (hh >= (uint32_t)C::SLOTS) {
+            ok = mbar_wait(saddr(&tempty[slot]), ((hh / C::SLOTS) - 1) & 1u, &abort_flag);
+            if (!ok) break;
+            tc_fence_after();
+          }
+          for (int bb = 0; bb < TC_BPS; ++bb) {
+            // block b: box b / 4, 32-byte K step b % 4 inside its 128-byte rows
+            const int b = h * TC_BPS + bb;
+            const uint64_t da = sw128_desc(a0 + (uint32_t)((b >> 2) * TC_BOX + (b & 3) * 32));
+            const uint64_t db = sw128_desc(b0 + (uint32_t)((b >> 2) * C::BBOX + (b & 3) * 32));
+            asm volatile(
+                "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+                " tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n}\n" ::"r"(
+                    tmem + (slot * TC_BPS + bb) * C::NB),
+                "l"(da), "l"(db), "r"(C::IDESC), "r"(0)
+                : "memory");
+          }
+          tc_commit(saddr(&tfull[slot]));
+        }
+        if (!ok) break;
+        tc_commit(saddr(&empty[s]));  // the stage is free once these MMAs have read it
+      }
+      // every MMA issued completes before the accumulators are freed
+      tc_commit(saddr(&mma_done));
+      mbar_wait_drain(saddr(&mma_done), 0u);
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue
+    asm volatile("griddepcontrol.wait;" ::: "memory");  // header and counters
+    const int e = warp - 2;
+    const int quarter = warp & 3;  // TMEM lanes 32 * quarter ... (this warp's rows)
+    const int g = e >> 2;          // tile half: blocks 4g .. 4g + 3
+    const int row = quarter * 32 + lane;
+    const int* hdr = reinterpret_cast<const int*>(p.ws);
+    unsigned* cnt = reinterpret_cast<unsigned*>(p.ws + p.cnt_off);
+    float* part = reinterpret_cast<float*>(p.ws + p.part_off);
+    float acc[NC];
+#pragma unroll
+    for (int c = 0; c < NC; ++c) acc[c] = 0.0f;
+    for (int i = 0; i < nunits; ++i) {
+      const int s = i % TC_STAGES;
+      const int64_t u = u0 + i;
+      const int rt = (int)(u / p.nkt), kt = (int)(u % p.nkt);
+      // the stage's scales are read from shared memory: wait for its copy too
+      mbar_wait(saddr(&full[s]), (uint32_t)((i / TC_STAGES) & 1), &abort_flag);
+      const uint8_t* stg = ring + (size_t)s * C::STAGE;
+      // the row's scales of this half: 4 fp16 (2 words)
+      const uint2 d4 = *reinterpret_cast<const uint2*>(stg + TC_ABYTES + row * 16 + g * 8);
+      const float* xs = reinterpret_cast<const float*>(stg + TC_TILE + C::XB);
+      // this group's half of the tile: blocks 4g .. 4g + 3, slot hh % SLOTS
+      const uint32_t hh = 2u * i + g, slot = hh % C::SLOTS;
+      mbar_wait(saddr(&tfull[slot]), (hh / C::SLOTS) & 1u, &abort_flag);
+      __syncwarp();
+      tc_fence_after();
+      const uint32_t ta = tmem + ((uint32_t)(quarter * 32) << 16) + slot * TC_BPS * C::NB;
+      constexpr int BR = TC_BPS / C::ROUNDS;  // blocks per TMEM read
+#pragma unroll
+      for (int rd = 0; rd < C::ROUNDS; ++rd) {
+        uint32_t v[BR][3][NC];
+#pragma unroll
+        for (int bb = 0; bb < BR; ++bb)
+#pragma unroll
+          for (int pl = 0; pl < 3; ++pl)
+            tmem_ld<NC>(ta + (uint32_t)((rd * BR + bb) * C::NB + pl * NC), v[bb][pl]);
+        asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+        if (rd == C::ROUNDS - 1) {
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(saddr(&tempty[slot]));
+        }
+#pragma unroll
+        for (int bb = 0; bb < BR; ++bb) {
+          const int bh = rd * BR + bb, b = g * TC_BPS + bh;  // bh: block within the half
+          const uint32_t dword = bh < 2 ? d4.x : d4.y;
+          const uint32_t dh = (bh & 1) ? (dword >> 16) : (dword & 0xFFFFu);
+          const float dv = __half2float(__ushort_as_half((unsigned short)dh));
+#pragma unroll
+          for (int c = 0; c < NC; ++c) {
+            const int lo = (int)(v[bb][0][c] + (v[bb][1][c] << 8));  // exact: |lo| < 2^28
+            const float f = fmaf((float)(int)v[bb][2][c], 65536.0f, (float)lo);
+            acc[c] = fmaf(f, dv * xs[b * NC + c], acc[c]);
+          }
+        }
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(saddr(&empty[s]));
+      if (kt != p.nkt - 1 && i != nunits - 1) continue;
+      // ---- end of this CTA's part of row tile rt: add the two groups
+#pragma unroll
+      for (int c = 0; c < NC; ++c) {
+        red[(g * NC + c) * TC_M + row] = acc[c];
+        acc[c] = 0.0f;
+      }
+      epi_sync();
+      const int64_t t0 = (int64_t)rt * p.nkt;
+      const bool complete = u0 <= t0 && kt == p.nkt - 1;  // the whole row tile is this CTA's
+      const int r = rt * TC_M + row;
+      const int my_side = (u0 / p.nkt == rt) ? 0 : 1;  // partial of the CTA's first or last tile
+      for (int c = g; c < NC; c += TC_GROUPS) {
+        float tot = 0.0f;
+#pragma unroll
+        for (int gg = 0; gg < TC_GROUPS; ++gg) tot += red[(gg * NC + c) * TC_M + row];
+        if (complete) {
+          if (r < p.M && c < p.N) p.y[(int64_t)c * p.ldy + r] = finish(tot, hdr, c);
+        } else {
+          part[(((int64_t)blockIdx.x * 2 + my_side) * NC + c) * TC_M + row] = tot;
+        }
+      }
+      if (!complete) {
+        // a row tile shared with other CTAs: the last one to finish adds the
+        // parts in CTA order
+        __threadfence();
+        epi_sync();
+        const int c0 = cta_of(t0, U, gridDim.x), c1 = cta_of(t0 + p.nkt - 1, U, gridDim.x);
+        if (e == 0 && lane == 0) last_flag = atomicAdd(&cnt[rt], 1u) == (unsigned)(c1 - c0);
+        epi_sync();
+        if (last_flag) {
+          __threadfence();
+          for (int c = g; c < NC; c += TC_GROUPS) {
+            float tot = 0.0f;
+            for (int cc = c0; cc <= c1; ++cc) {
+              const int side = (U * cc / gridDim.x) / p.nkt == rt ? 0 : 1;
+              tot += __ldcg(&part[(((int64_t)cc * 2 + side) * NC + c) * TC_M + row]);
+            }
+            if (r < p.M && c < p.N) p.y[(int64_t)c * p.ldy + r] = finish(tot, hdr, c);
+          }
+        }
+      }
+      epi_sync();  // red and last_flag are reused by the next row tile
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1) {
+    __syncwarp();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
+                 "r"(TC_TMEM_COLS)
+                 : "memory");
+  }
+}
+
+// ------------------------------------------------------------- x prep
+// One CTA per column (NC CTAs; columns >= N get zeros): the column's
+// power-of-two normalisation, then per 32-element block the exponent, the
+// fixed-point digits (written where the B operand reads them) and the block
+// scale.  CTA 0 also clears the row-tile counters.
+constexpr int XT_THREADS = 256;
+
+template <int NC>
+__global__ void __launch_bounds__(XT_THREADS) k_xprep_tc(const float* __restrict__ x, int64_t ldx,
+                                                         int K, int N, TcArgs p) {
+  using C = TcCfg<NC>;
+  // the GEMV may launch now and prefetch weights; it reads the workspace only
+  // after its griddepcontrol.wait, i.e. after this grid has completed
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  __shared__ uint32_t red[XT_THREADS / 32];
+  __shared__ int nonfinite;
+  const int col = blockIdx.x, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const float* xc = x + (int64_t)col * ldx;
+  const bool live = col < N;
+  if (threadIdx.x == 0) nonfinite = 0;
+  if (col == 0) {
+    unsigned* cnt = reinterpret_cast<unsigned*>(p.ws + p.cnt_off);
+    for (int t = threadIdx.x; t < p.ntiles; t += XT_THREADS) cnt[t] = 0u;
+  }
+  __syncthreads();
+  // max |x| over the finite elements, as bits
+  uint32_t m = 0u;
+  bool bad = false;
+  if (live)
+    for (int i = threadIdx.x; i < K; i += XT_THREADS) {
+      const uint32_t a = __float_as_uint(xc[i]) & 0x7FFFFFFFu;
+      if (a >= 0x7F800000u) bad = true;
+      else m = max(m, a);
+    }
+  if (bad) nonfinite = 1;
+  for (int o = 16; o; o >>= 1) m = max(m, __shfl_xor_sync(0xffffffffu, m, o));
+  if (lane == 0) red[warp] = m;
+  __syncthreads();
+  m = 0u;
+  for (int w = 0; w < XT_THREADS / 32; ++w) m = max(m, red[w]);
+  // x' = x 2^sh with max |x'| in [2^14, 2^15) (exact); y = acc 2^-sh
+  int sh = 0;
+  if (m != 0u) {
+    int ee;
+    frexpf(__uint_as_float(m), &ee);  // max = f 2^ee, f in [0.5, 1)
+    sh = 15 - ee;
+  }
+  const bool nf = nonfinite != 0;
+  int* hdr = reinterpret_cast<int*>(p.ws);
+  if (threadIdx.x == 0) {
+    hdr[col] = sh;
+    hdr[16 + col] = nf ? 1 : 0;
+  }
+  // blocks: warp w takes blocks w, w + 8, ...; lane = element of the block
+  const int nblk = p.nkt * TC_BLK;
+  for (int gb = warp; gb < nblk; gb += XT_THREADS / 32) {
+    const int kt = gb / TC_BLK, b = gb % TC_BLK;
+    const int k = gb * QK + lane;
+    const float v = live && !nf && k < K ? ldexpf(xc[k], sh) : 0.0f;
+    uint32_t a = __float_as_uint(v) & 0x7FFFFFFFu;
+    for (int o = 16; o; o >>= 1) a = max(a, __shfl_xor_sync(0xffffffffu, a, o));
+    int e = 0;  // |x'| < 2^e on the block
+    if (a != 0u) frexpf(__uint_as_float(a), &e);
+    // X = rint(x' 2^(22 - e)), |X| <= 2^22 (ldexpf scales exactly here)
+    const int X = a == 0u ? 0 : __float2int_rn(ldexpf(v, 22 - e));
+    const int p0 = (int)(signed char)(X & 0xFF);
+    const int X1 = (X - p0) >> 8;
+    const int p1 = (int)(signed char)(X1 & 0xFF);
+    const int p2 = (X1 - p1) >> 8;
+    uint8_t* xt = p.ws + p.xt_off + (size_t)kt * C::XT;
+    const int kb = b * QK + lane;  // element inside the K tile
+    const int box = kb >> 7, within = kb & 127, chunk = within >> 4;
+    const int pv[3] = {p0, p1, p2};
+#pragma unroll
+    for (int pl = 0; pl < 3; ++pl) {
+      const int nrow = pl * NC + col;  // B row
+      xt[box * C::BBOX + (nrow >> 3) * 1024 + (nrow & 7) * 128 + ((chunk ^ (nrow & 7)) << 4) +
+         (within & 15)] = (uint8_t)(signed char)pv[pl];
+    }
+    if (lane == 0) {
+      // 2^(e - 22), zero where that underflows: such a block lies below
+      // 2^-104 of the column maximum, far under the error bound
+      reinterpret_cast<float*>(xt + C::XB)[b * NC + col] = a == 0u ? 0.0f : ldexpf(1.0f, e - 22);
+    }
+  }
+}
+
+// ------------------------------------------------------------ tc tiles
+// One CTA per tile: quants (q8_0 from SoA planes or ggml blocks) in 16-byte
+// chunks, then the scales.
+__global__ void __launch_bounds__(256) k_tile_tc(const uint8_t* __restrict__ q,
+                                                 const unsigned short* __restrict__ d, bool aos,
+                                                 int M, int K, int nkt, uint8_t* __restrict__ out) {
+  const int kt = blockIdx.x, rt = blockIdx.y;
+  uint8_t* t = out + ((int64_t)rt * nkt + kt) * TC_TILE;
+  const int nb = K / QK;
+  constexpr int CH = TC_KT / 16;  // 16-byte chunks per tile row
+  for (int i = threadIdx.x; i < TC_M * CH; i += blockDim.x) {
+    const int r = i / CH, ch = i % CH;
+    const int row = rt * TC_M + r, k0 = kt * TC_KT + ch * 16;
+    uint4 v = make_uint4(0u, 0u, 0u, 0u);
+    if (row < M && k0 < K) {  // K % 32 == 0: a chunk is wholly inside K or beyond it
+      if (!aos) {
+        v = *reinterpret_cast<const uint4*>(q + (int64_t)row * K + k0);
+      } else {
+        const uint8_t* src = q + ((int64_t)row * nb + k0 / QK) * Q8_BLOCK + 2 + (k0 % QK);
+        uint32_t w[4];
+        for (int j = 0; j < 4; ++j)
+          w[j] = (uint32_t)src[4 * j] | ((uint32_t)src[4 * j + 1] << 8) |
+                 ((uint32_t)src[4 * j + 2] << 16) | ((uint32_t)src[4 * j + 3] << 24);
+        v = make_uint4(w[0], w[1], w[2], w[3]);
+      }
+    }
+    const int box = ch >> 3, c = ch & 7;
+    *reinterpret_cast<uint4*>(t + box * TC_BOX + (r >> 3) * 1024 + (r & 7) * 128 +
+                              ((c ^ (r & 7)) << 4)) = v;
+  }
+  unsigned short* ts = reinterpret_cast<unsigned short*>(t + TC_ABYTES);
+  for (int i = threadIdx.x; i < TC_M * TC_BLK; i += blockDim.x) {
+    const int r = i / TC_BLK, b = i % TC_BLK;
+    const int row = rt * TC_M + r, blk = kt * TC_BLK + b;
+    unsigned short h = 0;
+    if (row < M && blk < nb) {
+      if (!aos) {
+        h = d[(int64_t)row * nb + blk];
+      } else {
+        const uint8_t* src = q + ((int64_t)row * nb + blk) * Q8_BLOCK;
+        h = (unsigned short)(src[0] | (src[1] << 8));
+      }
+    }
+    ts[i] = h;
+  }
+}
+
+struct WsLayout {
+  int cnt_off, part_off, xt_off;
+  size_t bytes;
+};
+
+template <int NC>
+WsLayout ws_layout(int64_t M, int64_t K, int grid) {
+  const int64_t nkt = (K + TC_KT - 1) / TC_KT, ntiles = (M + TC_M - 1) / TC_M;
+  WsLayout w;
+  w.cnt_off = TC_HDR;
+  w.part_off = w.cnt_off + (int)((ntiles * 4 + 15) / 16 * 16);
+  w.xt_off = w.part_off + grid * 2 * NC * TC_M * 4;
+  w.bytes = (size_t)w.xt_off + (size_t)nkt * TcCfg<NC>::XT;
+  return w;
+}
+
+int tc_grid(int64_t M, int64_t K, int sms) {
+  const int64_t U = ((K + TC_KT - 1) / TC_KT) * ((M + TC_M - 1) / TC_M);
+  return (int)std::max<int64_t>(1, std::min<int64_t>(sms, U));
+}
+
+template <int NC>
+int launch_tc(const void* tiles, int64_t M, int64_t K, const float* x, int64_t ldx, float* y,
+              int64_t ldy, int N, void* ws, size_t ws_bytes, const DeviceInfo& dev,
+              cudaStream_t st) {
+  using C = TcCfg<NC>;
+  const int grid = tc_grid(M, K, dev.sms);
+  const WsLayout w = ws_layout<NC>(M, K, grid);
+  if (ws_bytes < w.bytes)
+    return set_error(ERR_ARG, "this call needs a workspace of %zu bytes, got %zu", w.bytes, ws_bytes);
+  static bool attr_done[64] = {};
+  if (dev.device >= 0 && dev.device < 64 && !attr_done[dev.device]) {
+    const cudaError_t e =
+        cudaFuncSetAttribute(k_gemv_tc<NC>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)C::SMEM);
+    if (e != cudaSuccess)
+      return set_error(ERR_CUDA, "k_gemv_tc shared memory: %s", cudaGetErrorString(e));
+    attr_done[dev.device] = true;
+  }
+  TcArgs a;
+  a.tiles = static_cast<const uint8_t*>(tiles);
+  a.ws = static_cast<uint8_t*>(ws);
+  a.y = y;
+  a.ldy = ldy;
+  a.M = (int)M;
+  a.N = N;
+  a.nkt = (int)((K + TC_KT - 1) / TC_KT);
+  a.ntiles = (int)((M + TC_M - 1) / TC_M);
+  a.cnt_off = w.cnt_off;
+  a.part_off = w.part_off;
+  a.xt_off = w.xt_off;
+
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchConfig_t cfg = {};
+  cfg.stream = st;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cfg.gridDim = dim3(NC);
+  cfg.blockDim = dim3(XT_THREADS);
+  cudaError_t e = cudaLaunchKernelEx(&cfg, k_xprep_tc<NC>, x, ldx, (int)K, N, a);
+  if (e != cudaSuccess) return set_error(ERR_CUDA, "k_xprep_tc launch: %s", cudaGetErrorString(e));
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(TC_THREADS);
+  cfg.dynamicSmemBytes = C::SMEM;
+  e = cudaLaunchKernelEx(&cfg, k_gemv_tc<NC>, a);
+  if (e != cudaSuccess) return set_error(ERR_CUDA, "k_gemv_tc launch: %s", cudaGetErrorString(e));
+  return check_launch("k_gemv_tc");
+}
+
+}  // namespace
+
+size_t tc_tiles_bytes(int64_t M, int64_t K) {
+  const int64_t nkt = (K + TC_KT - 1) / TC_KT, ntiles = (M + TC_M - 1) / TC_M;
+  return (size_t)(nkt * ntiles) * TC_TILE;
+}
+
+size_t tc_workspace_bytes(int64_t M, int64_t K, int sms) {
+  return ws_layout<16>(M, K, tc_grid(M, K, sms)).bytes;
+}
+
+int tile_weights_tc(bool aos, const void* q, const void* d, int64_t M, int64_t K, void* out,
+                    cudaStream_t st) {
+  const int nkt = (int)((K + TC_KT - 1) / TC_KT), ntiles = (int)((M + TC_M - 1) / TC_M);
+  if (nkt == 0 || ntiles == 0) return OK;
+  k_tile_tc<<<dim3(nkt, ntiles), 256, 0, st>>>(static_cast<const uint8_t*>(q),
+                                                 static_cast<const unsigned short*>(d), aos, (int)M,
+                                                 (int)K, nkt, static_cast<uint8_t*>(out));
+  return check_launch("k_tile_tc");
+}
+
+int gemv_tc(const void* tiles, int64_t M, int64_t K, const float* x, int64_t ldx, float* y,
+            int64_t ldy, int N, void* ws, size_t ws_bytes, cudaStream_t st) {
+  if (M == 0 || N == 0) return OK;
+  DeviceInfo dev;
+  if (int rc = current_device_info(dev)) return rc;
+  if (N <= 2) return launch_tc<2>(tiles, M, K, x, ldx, y, ldy, N, ws, ws_bytes, dev, st);
+  if (N <= 4) return launch_tc<4>(tiles, M, K, x, ldx, y, ldy, N, ws, ws_bytes, dev, st);
+  if (N <= 8) return launch_tc<8>(tiles, M, K, x, ldx, y, ldy, N, ws, ws_bytes, dev, st);
+  return launch_tc<16>(tiles, M, K, x, ldx, y, ldy, N, ws, ws_bytes, dev, st);
+}
+
+int set_tc_spin_limit(long long cycles) {
+  const cudaError_t e = cudaMemcpyToSymbol(g_tc_spin_limit, &cycles, sizeof(cycles));
+  if (e == cudaSuccess) return OK;
+  return set_error(ERR_CUDA, "setting the wait limit: %s", cudaGetErrorString(e));
+}
+
+int read_tc_error(int clear, cudaStream_t st, int* out) {
+  int v = 0;
+  cudaError_t e = cudaMemcpyFromSymbolAsync(&v, g_tc_error, sizeof(int), 0, cudaMemcpyDeviceToHost, st);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+  if (e != cudaSuccess)
+    return set_error(ERR_CUDA, "reading the device error word: %s", cudaGetErrorString(e));
+  if (clear && v) {
+    const int zero = 0;
+    e = cudaMemcpyToSymbolAsync(g_tc_error, &zero, sizeof(int), 0, cudaMemcpyHostToDevice, st);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+    if (e != cudaSuccess)
+      return set_error(ERR_CUDA, "clearing the device error word: %s", cudaGetErrorString(e));
+  }
+  *out = v;
+  return OK;
+}
+
+}  // namespace qg

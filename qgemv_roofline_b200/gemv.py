@@ -184,13 +184,53 @@ def qgemv_tiled(fmt: str, tiled: torch.Tensor, M: int, K: int, x: torch.Tensor,
     return y
 
 
+def tile_weights_tc(q: torch.Tensor | None = None, d: torch.Tensor | None = None,
+                    blocks: torch.Tensor | None = None, stream: int | None = None) -> torch.Tensor:
+    """q8_0 tc tiles (uint8, 1-D) of a matrix given as SoA planes (q, d) or
+    ggml blocks [M, K/32, 34]: the layout the tcgen05 batch kernel streams,
+    one bulk copy per 128 rows x 256 columns.  Made once per matrix."""
+    if blocks is not None:
+        if not blocks.is_cuda or blocks.dim() != 3 or not blocks.is_contiguous() \
+                or blocks.shape[2] != BLOCK_BYTES["q8_0"]:
+            raise ValueError("blocks must be a contiguous CUDA tensor [M, K/32, 34]")
+        M, K, src, dsrc, layout, dev = blocks.shape[0], blocks.shape[1] * QK, blocks, None, 1, blocks.device
+    else:
+        if q is None or d is None or not q.is_cuda or not q.is_contiguous() or not d.is_contiguous():
+            raise ValueError("q and d must be contiguous CUDA tensors")
+        M, K, src, dsrc, layout, dev = q.shape[0], q.shape[1], q, d, 0, q.device
+    out = torch.empty(_lib.lib().qgemv_q8_0_tc_bytes(M, K), dtype=torch.uint8, device=dev)
+    st = torch.cuda.current_stream(dev).cuda_stream if stream is None else stream
+    _lib.call("qgemv_q8_0_tc_tile", layout, src.data_ptr(),
+              None if dsrc is None else dsrc.data_ptr(), M, K, out.data_ptr(), st)
+    return out
+
+
+def qgemv_tc(tiles: torch.Tensor, M: int, K: int, x: torch.Tensor, y: torch.Tensor | None = None,
+             stream: int | None = None) -> torch.Tensor:
+    """q8_0 GEMV over tc tiles (tile_weights_tc) on the tcgen05 tensor cores;
+    x [K] or [N, K] for any N."""
+    if not tiles.is_cuda or tiles.dtype != torch.uint8:
+        raise ValueError("tiles must be a uint8 CUDA tensor")
+    if tiles.numel() != _lib.lib().qgemv_q8_0_tc_bytes(M, K):
+        raise ValueError(f"tiles hold {tiles.numel()} bytes, not those of a [{M}, {K}] q8_0 matrix")
+    X, Y, y, N, ldx, ldy = _xy(x, M, K, y, tiles.device)
+    st = torch.cuda.current_stream(tiles.device).cuda_stream if stream is None else stream
+    with torch.cuda.device(tiles.device):
+        nbytes = _lib.lib().qgemv_q8_0_tc_workspace_bytes(M, K)
+    ws = _workspace(tiles.device, nbytes, stream)
+    _lib.call("qgemv_q8_0_tc", tiles.data_ptr(), M, K, X.data_ptr(), Y.data_ptr(), N, ldx, ldy,
+              ws.data_ptr(), ws.numel(), st)
+    return y
+
+
 @dataclass
 class QuantizedMatrix:
     """A quantized [M, K] weight matrix resident on one GPU.
 
-    ``layout`` is "soa" (planes ``q``, ``d``), "aos" (ggml ``blocks``) or
+    ``layout`` is "soa" (planes ``q``, ``d``), "aos" (ggml ``blocks``),
     "tiled" (batch tiles, ``tiled``: the layout of the tensor-core batch
-    kernel, see ``to_tiled``).
+    kernel, see ``to_tiled``) or "tc" (q8_0 tc tiles, ``tiled``: the layout
+    of the tcgen05 batch kernel, see ``to_tc``).
     """
 
     fmt: str
@@ -218,7 +258,8 @@ class QuantizedMatrix:
 
     @property
     def device(self):
-        return {"soa": self.q, "aos": self.blocks, "tiled": self.tiled}[self.layout].device
+        return {"soa": self.q, "aos": self.blocks, "tiled": self.tiled,
+                "tc": self.tiled}[self.layout].device
 
     def to_tiled(self) -> "QuantizedMatrix":
         """The same matrix as batch tiles (for calls with several columns)."""
@@ -230,6 +271,20 @@ class QuantizedMatrix:
             t = tile_weights(self.fmt, blocks=self.blocks)
         return QuantizedMatrix(self.fmt, self.M, self.K, "tiled", tiled=t)
 
+    def to_tc(self) -> "QuantizedMatrix":
+        """The same q8_0 matrix as tc tiles (the tcgen05 batch kernel)."""
+        if self.fmt != "q8_0":
+            raise ValueError("tc tiles hold q8_0 weights only")
+        if self.layout == "tc":
+            return self
+        if self.layout == "soa":
+            t = tile_weights_tc(q=self.q, d=self.d)
+        elif self.layout == "aos":
+            t = tile_weights_tc(blocks=self.blocks)
+        else:
+            raise ValueError("make tc tiles from the SoA or ggml-block matrix")
+        return QuantizedMatrix(self.fmt, self.M, self.K, "tc", tiled=t)
+
     def matvec(self, x: torch.Tensor, y: torch.Tensor | None = None,
                stream: int | None = None, activations: str = "exact") -> torch.Tensor:
         """y = W x; ``activations="q8_1"`` selects the opt-in int8-activation
@@ -240,13 +295,17 @@ class QuantizedMatrix:
             if activations != "exact":
                 raise ValueError("batch tiles run the exact path only")
             return qgemv_tiled(self.fmt, self.tiled, self.M, self.K, x, y, stream)
+        if self.layout == "tc":
+            if activations != "exact":
+                raise ValueError("tc tiles run the exact path only")
+            return qgemv_tc(self.tiled, self.M, self.K, x, y, stream)
         return qgemv_aos(self.fmt, self.blocks, x, y, stream, activations)
 
     __call__ = matvec
 
     def rows(self, r0: int, r1: int) -> "QuantizedMatrix":
         """Row slice [r0, r1) as a new matrix (copies; used for row sharding)."""
-        if self.layout == "tiled":
+        if self.layout in ("tiled", "tc"):
             raise ValueError("slice the SoA or ggml-block matrix, then tile the slice")
         if self.layout == "soa":
             return QuantizedMatrix(self.fmt, r1 - r0, self.K, "soa",
@@ -255,8 +314,8 @@ class QuantizedMatrix:
                                blocks=self.blocks[r0:r1].contiguous())
 
     def to(self, device) -> "QuantizedMatrix":
-        if self.layout == "tiled":
-            return QuantizedMatrix(self.fmt, self.M, self.K, "tiled", tiled=self.tiled.to(device))
+        if self.layout in ("tiled", "tc"):
+            return QuantizedMatrix(self.fmt, self.M, self.K, self.layout, tiled=self.tiled.to(device))
         if self.layout == "soa":
             return QuantizedMatrix(self.fmt, self.M, self.K, "soa", q=self.q.to(device),
                                    d=self.d.to(device))
