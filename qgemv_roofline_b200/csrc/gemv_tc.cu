@@ -34,18 +34,20 @@
 //
 // The (row tile, K tile) units are split evenly over one CTA per SM (a unit
 // is 34 KB of weights: the imbalance is at most one unit).  A row tile that
-// two or more CTAs share is finished by the CTA that completes its part
-// last (a counter per row tile): it adds the CTAs' partial sums in CTA order,
-// so results do not depend on timing.
+// two or more CTAs share is finished by the epilogue warp that stores the
+// last part (a counter per row tile): it adds the CTAs' partial sums in CTA
+// order, so results do not depend on timing.
 //
 // Per CTA (10 warps): warp 0 streams (weight tile, x tile) pairs into a
 // 4-stage shared-memory ring (bulk copies); one thread of warp 1 issues the
-// 8 MMAs of a stage, each half tile (4 blocks) into one slot of a TMEM ring
-// (4 slots of 4 x 32 columns, or 2 of 4 x 48), and commits each half to an
-// mbarrier; warps 2..9 (two groups of four, one warp per TMEM lane quarter,
-// group g taking half g of every tile) read a whole slot back with one wait
-// (tcgen05.ld), release it and accumulate: the TMEM read latency is paid
-// once per half tile, not once per block.  Every wait is bounded (the
+// 8 MMAs of a stage, 4 (or, at 16 columns, 2) blocks into each slot of a TMEM
+// ring (4 slots of 4 x 32 columns, or 5 of 2 x 48), and commits each slot to
+// an mbarrier; warps 2..9 (two groups of four, one warp per TMEM lane
+// quarter, group g taking column half g) read their part of a whole slot back
+// with one wait (tcgen05.ld), release it and accumulate: the TMEM read
+// latency is paid once per slot, not once per block.  No barrier joins the
+// epilogue warps: each owns its rows and columns, and at the end of a row
+// tile stores y (or, for a row tile shared with other CTAs, its part).  Every wait is bounded (the
 // library's wait limit): on timeout the error word records
 // QGEMV_ERR_TIMEOUT, the producer stops and waits for its copies, the MMA
 // thread stops issuing, the epilogue runs out its loop without waiting, and
@@ -69,9 +71,8 @@ constexpr int TC_ABYTES = TC_M * TC_KT;         // quants of a tile
 constexpr int TC_BOX = TC_M * 128;              // one 128-byte-wide box of quants
 constexpr int TC_DBYTES = TC_M * TC_BLK * 2;    // fp16 scales of a tile
 constexpr int TC_TILE = TC_ABYTES + TC_DBYTES;  // 34816 bytes, a multiple of 1024
-constexpr int TC_BPS = TC_BLK / 2;              // blocks per TMEM slot (half a tile)
 constexpr int TC_TMEM_COLS = 512;
-constexpr int TC_GROUPS = 2;                    // epilogue warp groups (one per tile half)
+constexpr int TC_GROUPS = 2;                    // epilogue warp groups (one per column half)
 constexpr int TC_EPI = 4 * TC_GROUPS;           // epilogue warps
 constexpr int TC_THREADS = 32 * (2 + TC_EPI);
 constexpr int TC_STAGES = 4;
@@ -85,17 +86,17 @@ struct TcCfg {
   static constexpr int XSB = TC_BLK * NC * 4;         // block scales [block][column] fp32
   static constexpr int XT = XB + XSB;                 // x tile bytes (multiple of 16)
   static constexpr int STAGE = (TC_TILE + XT + 1023) / 1024 * 1024;
-  static constexpr int RED = TC_GROUPS * NC * TC_M * 4;  // group reduction scratch
-  static constexpr int SLOTS = TC_TMEM_COLS / (TC_BPS * NB);  // TMEM slots: 4 (NB 32), 2 (NB 48)
-  static constexpr int ROUNDS = NC == 16 ? 2 : 1;     // TMEM reads per slot (registers)
-  static constexpr size_t SMEM = (size_t)TC_STAGES * STAGE + RED + 1024;
+  static constexpr int BPS = NC == 16 ? 2 : 4;        // blocks per TMEM slot (one read)
+  static constexpr int HS = TC_BLK / 2 / BPS;         // slots per tile half
+  static constexpr int SLOTS = TC_TMEM_COLS / (BPS * NB);  // TMEM slots: 4 (NB 32), 5 (NB 48)
+  static constexpr size_t SMEM = (size_t)TC_STAGES * STAGE + 1024;
   // kind::i8: s32 accumulators (bits 4-5 = 2), A and B signed (bits 7-9,
   // 10-12 = 1), both K-major (bits 15, 16 = 0), N >> 3 at bit 17, M >> 4 at 24
   static constexpr uint32_t IDESC = (2u << 4) | (1u << 7) | (1u << 10) |
                                     ((uint32_t)(NB >> 3) << 17) | ((uint32_t)(TC_M >> 4) << 24);
 };
 static_assert(TcCfg<16>::SMEM <= 227 * 1024, "ring too large");
-static_assert(TcCfg<16>::SLOTS >= 2 && TcCfg<8>::SLOTS >= 2, "TMEM slots");
+static_assert(TcCfg<16>::SLOTS == 5 && TcCfg<8>::SLOTS == 4, "TMEM slots");
 static_assert(TC_TILE % 1024 == 0, "B operand must stay 1024-byte aligned");
 
 __device__ __forceinline__ long long tc_spin_limit() {
@@ -154,9 +155,6 @@ __device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t
       "l"(src), "r"(bytes), "r"(bar)
       : "memory");
 }
-__device__ __forceinline__ void epi_sync() {
-  asm volatile("bar.sync 1, %0;" ::"n"(TC_EPI * 32) : "memory");
-}
 
 // Shared-memory matrix descriptor of a K-major operand in the canonical
 // 128-byte-swizzled layout: start address >> 4 (bits 0-13), leading byte
@@ -185,7 +183,9 @@ __device__ __forceinline__ void tc_commit(uint32_t bar) {
 // 32 lanes x NC consecutive 32-bit TMEM columns.
 template <int NC>
 __device__ __forceinline__ void tmem_ld(uint32_t ta, uint32_t (&v)[NC]) {
-  if constexpr (NC == 2) {
+  if constexpr (NC == 1) {
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x1.b32 {%0}, [%1];" : "=r"(v[0]) : "r"(ta));
+  } else if constexpr (NC == 2) {
     asm volatile("tcgen05.ld.sync.aligned.32x32b.x2.b32 {%0, %1}, [%2];"
                  : "=r"(v[0]), "=r"(v[1])
                  : "r"(ta));
@@ -234,17 +234,15 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_gemv_tc(const __grid_constant
   extern __shared__ uint8_t tc_smem_raw[];
   __shared__ __align__(8) unsigned long long full[TC_STAGES];
   __shared__ __align__(8) unsigned long long empty[TC_STAGES];
-  __shared__ __align__(8) unsigned long long tfull[4];
-  __shared__ __align__(8) unsigned long long tempty[4];
+  __shared__ __align__(8) unsigned long long tfull[5];
+  __shared__ __align__(8) unsigned long long tempty[5];
   __shared__ __align__(8) unsigned long long mma_done;
   __shared__ uint32_t tmem_base;
   __shared__ int abort_flag;
-  __shared__ int last_flag;
 
   // 1024-byte-aligned ring (the swizzle works on address bits)
   uint8_t* ring = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(tc_smem_raw) + 1023) & ~(uintptr_t)1023);
-  float* red = reinterpret_cast<float*>(ring + (size_t)TC_STAGES * C::STAGE);
   const uint32_t ring_s = saddr(ring);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t U = (int64_t)p.ntiles * p.nkt;
@@ -258,7 +256,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_gemv_tc(const __grid_constant
     }
     for (int s = 0; s < C::SLOTS; ++s) {
       mbar_init(saddr(&tfull[s]), 1);
-      mbar_init(saddr(&tempty[s]), 4);  // the four lane-quarter warps of one group
+      mbar_init(saddr(&tempty[s]), TC_EPI);  // every epilogue warp reads every slot
     }
     mbar_init(saddr(&mma_done), 1);
     abort_flag = 0;
@@ -320,23 +318,24 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_gemv_tc(const __grid_constant
         tc_fence_after();
         const uint32_t a0 = ring_s + (uint32_t)(s * C::STAGE);
         const uint32_t b0 = a0 + TC_TILE;
-        // tile half h (blocks 4h .. 4h + 3) into slot hh % SLOTS, hh = 2i + h
-        for (int h = 0; h < 2 && ok; ++h) {
-          const uint32_t hh = 2u * i + h, slot = hh % C::SLOTS;
+        // slot sl of the tile (blocks sl * BPS ...) into TMEM slot hh % SLOTS,
+        // hh = 2 HS i + sl
+        for (int sl = 0; sl < 2 * C::HS && ok; ++sl) {
+          const uint32_t hh = 2u * C::HS * i + sl, slot = hh % C::SLOTS;
           if (hh >= (uint32_t)C::SLOTS) {
             ok = mbar_wait(saddr(&tempty[slot]), ((hh / C::SLOTS) - 1) & 1u, &abort_flag);
             if (!ok) break;
             tc_fence_after();
           }
-          for (int bb = 0; bb < TC_BPS; ++bb) {
+          for (int bb = 0; bb < C::BPS; ++bb) {
             // block b: box b / 4, 32-byte K step b % 4 inside its 128-byte rows
-            const int b = h * TC_BPS + bb;
+            const int b = sl * C::BPS + bb;
             const uint64_t da = sw128_desc(a0 + (uint32_t)((b >> 2) * TC_BOX + (b & 3) * 32));
             const uint64_t db = sw128_desc(b0 + (uint32_t)((b >> 2) * C::BBOX + (b & 3) * 32));
             asm volatile(
                 "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
                 " tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n}\n" ::"r"(
-                    tmem + (slot * TC_BPS + bb) * C::NB),
+                    tmem + (slot * C::BPS + bb) * C::NB),
                 "l"(da), "l"(db), "r"(C::IDESC), "r"(0)
                 : "memory");
           }
@@ -352,16 +351,17 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_gemv_tc(const __grid_constant
   } else {
     // ------------------------------------------------------------ epilogue
     asm volatile("griddepcontrol.wait;" ::: "memory");  // header and counters
+    constexpr int NCH = NC / 2;    // columns per warp
     const int e = warp - 2;
     const int quarter = warp & 3;  // TMEM lanes 32 * quarter ... (this warp's rows)
-    const int g = e >> 2;          // tile half: blocks 4g .. 4g + 3
+    const int g = e >> 2;          // this warp's columns: g * NCH ... (g + 1) * NCH - 1
     const int row = quarter * 32 + lane;
     const int* hdr = reinterpret_cast<const int*>(p.ws);
     unsigned* cnt = reinterpret_cast<unsigned*>(p.ws + p.cnt_off);
     float* part = reinterpret_cast<float*>(p.ws + p.part_off);
-    float acc[NC];
+    float acc[NCH];
 #pragma unroll
-    for (int c = 0; c < NC; ++c) acc[c] = 0.0f;
+    for (int c = 0; c < NCH; ++c) acc[c] = 0.0f;
     for (int i = 0; i < nunits; ++i) {
       const int s = i % TC_STAGES;
       const int64_t u = u0 + i;
@@ -369,38 +369,34 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_gemv_tc(const __grid_constant
       // the stage's scales are read from shared memory: wait for its copy too
       mbar_wait(saddr(&full[s]), (uint32_t)((i / TC_STAGES) & 1), &abort_flag);
       const uint8_t* stg = ring + (size_t)s * C::STAGE;
-      // the row's scales of this half: 4 fp16 (2 words)
-      const uint2 d4 = *reinterpret_cast<const uint2*>(stg + TC_ABYTES + row * 16 + g * 8);
-      const float* xs = reinterpret_cast<const float*>(stg + TC_TILE + C::XB);
-      // this group's half of the tile: blocks 4g .. 4g + 3, slot hh % SLOTS
-      const uint32_t hh = 2u * i + g, slot = hh % C::SLOTS;
-      mbar_wait(saddr(&tfull[slot]), (hh / C::SLOTS) & 1u, &abort_flag);
-      __syncwarp();
-      tc_fence_after();
-      const uint32_t ta = tmem + ((uint32_t)(quarter * 32) << 16) + slot * TC_BPS * C::NB;
-      constexpr int BR = TC_BPS / C::ROUNDS;  // blocks per TMEM read
+      const uint4 d8 = *reinterpret_cast<const uint4*>(stg + TC_ABYTES + row * 16);  // 8 fp16
+      const float* xs = reinterpret_cast<const float*>(stg + TC_TILE + C::XB) + g * NCH;
 #pragma unroll
-      for (int rd = 0; rd < C::ROUNDS; ++rd) {
-        uint32_t v[BR][3][NC];
+      for (int sl = 0; sl < 2 * C::HS; ++sl) {
+        const uint32_t hh = 2u * C::HS * i + sl, slot = hh % C::SLOTS;
+        mbar_wait(saddr(&tfull[slot]), (hh / C::SLOTS) & 1u, &abort_flag);
+        __syncwarp();
+        tc_fence_after();
+        const uint32_t ta =
+            tmem + ((uint32_t)(quarter * 32) << 16) + slot * C::BPS * C::NB + g * NCH;
+        uint32_t v[C::BPS][3][NCH];
 #pragma unroll
-        for (int bb = 0; bb < BR; ++bb)
+        for (int bb = 0; bb < C::BPS; ++bb)
 #pragma unroll
           for (int pl = 0; pl < 3; ++pl)
-            tmem_ld<NC>(ta + (uint32_t)((rd * BR + bb) * C::NB + pl * NC), v[bb][pl]);
+            tmem_ld<NCH>(ta + (uint32_t)(bb * C::NB + pl * NC), v[bb][pl]);
         asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-        if (rd == C::ROUNDS - 1) {
-          tc_fence_before();
-          __syncwarp();
-          if (lane == 0) mbar_arrive(saddr(&tempty[slot]));
-        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(saddr(&tempty[slot]));
 #pragma unroll
-        for (int bb = 0; bb < BR; ++bb) {
-          const int bh = rd * BR + bb, b = g * TC_BPS + bh;  // bh: block within the half
-          const uint32_t dword = bh < 2 ? d4.x : d4.y;
-          const uint32_t dh = (bh & 1) ? (dword >> 16) : (dword & 0xFFFFu);
+        for (int bb = 0; bb < C::BPS; ++bb) {
+          const int b = sl * C::BPS + bb;
+          const uint32_t dword = (b >> 1) == 0 ? d8.x : (b >> 1) == 1 ? d8.y : (b >> 1) == 2 ? d8.z : d8.w;
+          const uint32_t dh = (b & 1) ? (dword >> 16) : (dword & 0xFFFFu);
           const float dv = __half2float(__ushort_as_half((unsigned short)dh));
 #pragma unroll
-          for (int c = 0; c < NC; ++c) {
+          for (int c = 0; c < NCH; ++c) {
             const int lo = (int)(v[bb][0][c] + (v[bb][1][c] << 8));  // exact: |lo| < 2^28
             const float f = fmaf((float)(int)v[bb][2][c], 65536.0f, (float)lo);
             acc[c] = fmaf(f, dv * xs[b * NC + c], acc[c]);
@@ -410,48 +406,49 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_gemv_tc(const __grid_constant
       __syncwarp();
       if (lane == 0) mbar_arrive(saddr(&empty[s]));
       if (kt != p.nkt - 1 && i != nunits - 1) continue;
-      // ---- end of this CTA's part of row tile rt: add the two groups
+      // ---- end of this CTA's part of row tile rt
+      const int64_t t0 = (int64_t)rt * p.nkt;
+      const int r = rt * TC_M + row;
+      if (u0 <= t0 && kt == p.nkt - 1) {  // the whole row tile is this CTA's
 #pragma unroll
-      for (int c = 0; c < NC; ++c) {
-        red[(g * NC + c) * TC_M + row] = acc[c];
+        for (int c = 0; c < NCH; ++c) {
+          const int n = g * NCH + c;
+          if (r < p.M && n < p.N) p.y[(int64_t)n * p.ldy + r] = finish(acc[c], hdr, n);
+          acc[c] = 0.0f;
+        }
+        continue;
+      }
+      // a row tile shared with other CTAs: every warp stores its part (its
+      // rows and columns) and counts it in the tile's counter for its warp
+      // slot; the warp that stores the last such part adds them, in CTA order
+      const int my_side = (u0 / p.nkt == rt) ? 0 : 1;  // the CTA's first or last row tile
+#pragma unroll
+      for (int c = 0; c < NCH; ++c) {
+        part[(((int64_t)blockIdx.x * 2 + my_side) * NC + g * NCH + c) * TC_M + row] = acc[c];
         acc[c] = 0.0f;
       }
-      epi_sync();
-      const int64_t t0 = (int64_t)rt * p.nkt;
-      const bool complete = u0 <= t0 && kt == p.nkt - 1;  // the whole row tile is this CTA's
-      const int r = rt * TC_M + row;
-      const int my_side = (u0 / p.nkt == rt) ? 0 : 1;  // partial of the CTA's first or last tile
-      for (int c = g; c < NC; c += TC_GROUPS) {
-        float tot = 0.0f;
-#pragma unroll
-        for (int gg = 0; gg < TC_GROUPS; ++gg) tot += red[(gg * NC + c) * TC_M + row];
-        if (complete) {
-          if (r < p.M && c < p.N) p.y[(int64_t)c * p.ldy + r] = finish(tot, hdr, c);
-        } else {
-          part[(((int64_t)blockIdx.x * 2 + my_side) * NC + c) * TC_M + row] = tot;
-        }
-      }
-      if (!complete) {
-        // a row tile shared with other CTAs: the last one to finish adds the
-        // parts in CTA order
+      __threadfence();
+      __syncwarp();
+      const int c0 = cta_of(t0, U, gridDim.x), c1 = cta_of(t0 + p.nkt - 1, U, gridDim.x);
+      unsigned last = 0;
+      if (lane == 0) last = atomicAdd(&cnt[rt * TC_EPI + e], 1u) == (unsigned)(c1 - c0);
+      if (__shfl_sync(0xffffffffu, last, 0)) {
         __threadfence();
-        epi_sync();
-        const int c0 = cta_of(t0, U, gridDim.x), c1 = cta_of(t0 + p.nkt - 1, U, gridDim.x);
-        if (e == 0 && lane == 0) last_flag = atomicAdd(&cnt[rt], 1u) == (unsigned)(c1 - c0);
-        epi_sync();
-        if (last_flag) {
-          __threadfence();
-          for (int c = g; c < NC; c += TC_GROUPS) {
-            float tot = 0.0f;
-            for (int cc = c0; cc <= c1; ++cc) {
-              const int side = (U * cc / gridDim.x) / p.nkt == rt ? 0 : 1;
-              tot += __ldcg(&part[(((int64_t)cc * 2 + side) * NC + c) * TC_M + row]);
-            }
-            if (r < p.M && c < p.N) p.y[(int64_t)c * p.ldy + r] = finish(tot, hdr, c);
-          }
+        float tot[NCH];
+#pragma unroll
+        for (int c = 0; c < NCH; ++c) tot[c] = 0.0f;
+        for (int cc = c0; cc <= c1; ++cc) {
+          const int side = (U * cc / gridDim.x) / p.nkt == rt ? 0 : 1;
+          const float* src = part + (((int64_t)cc * 2 + side) * NC + g * NCH) * TC_M + row;
+#pragma unroll
+          for (int c = 0; c < NCH; ++c) tot[c] += __ldcg(src + c * TC_M);
+        }
+#pragma unroll
+        for (int c = 0; c < NCH; ++c) {
+          const int n = g * NCH + c;
+          if (r < p.M && n < p.N) p.y[(int64_t)n * p.ldy + r] = finish(tot[c], hdr, n);
         }
       }
-      epi_sync();  // red and last_flag are reused by the next row tile
     }
   }
 
@@ -467,41 +464,64 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_gemv_tc(const __grid_constant
 }
 
 // ------------------------------------------------------------- x prep
-// One CTA per column (NC CTAs; columns >= N get zeros): the column's
-// power-of-two normalisation, then per 32-element block the exponent, the
+// Grid (chunks, NC): CTA (c, col) handles blocks [c * chunk, (c + 1) * chunk)
+// of column col (columns >= N get zeros).  Every CTA of a column first finds
+// the column's maximum itself (the column is read once per CTA, from L2
+// after the first), then for each of its 32-element blocks the exponent, the
 // fixed-point digits (written where the B operand reads them) and the block
-// scale.  CTA 0 also clears the row-tile counters.
+// scale.  CTA (0, 0) also clears the counters of the shared row tiles.
 constexpr int XT_THREADS = 256;
+constexpr int XT_CHUNK_MIN = 32;             // blocks per CTA, at least
+constexpr int64_t XT_REREAD = (int64_t)1 << 18;  // column elements re-read per column, at most
+
+int xprep_chunk(int64_t K) {
+  const int64_t nblk = (K + TC_KT - 1) / TC_KT * TC_BLK;
+  const int64_t ctas = std::max<int64_t>(1, std::min<int64_t>((nblk + XT_CHUNK_MIN - 1) / XT_CHUNK_MIN,
+                                                              XT_REREAD / std::max<int64_t>(K, 1)));
+  return (int)((nblk + ctas - 1) / ctas);
+}
+
+__device__ __forceinline__ uint32_t finite_abs_bits(float v, bool& bad) {
+  const uint32_t a = __float_as_uint(v) & 0x7FFFFFFFu;
+  if (a >= 0x7F800000u) {
+    bad = true;
+    return 0u;
+  }
+  return a;
+}
 
 template <int NC>
 __global__ void __launch_bounds__(XT_THREADS) k_xprep_tc(const float* __restrict__ x, int64_t ldx,
-                                                         int K, int N, TcArgs p) {
+                                                         int K, int N, int chunk, TcArgs p) {
   using C = TcCfg<NC>;
   // the GEMV may launch now and prefetch weights; it reads the workspace only
   // after its griddepcontrol.wait, i.e. after this grid has completed
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   asm volatile("griddepcontrol.wait;" ::: "memory");
   __shared__ uint32_t red[XT_THREADS / 32];
-  __shared__ int nonfinite;
-  const int col = blockIdx.x, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int col = blockIdx.y, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const float* xc = x + (int64_t)col * ldx;
   const bool live = col < N;
-  if (threadIdx.x == 0) nonfinite = 0;
-  if (col == 0) {
+  if (blockIdx.x == 0 && col == 0) {
     unsigned* cnt = reinterpret_cast<unsigned*>(p.ws + p.cnt_off);
-    for (int t = threadIdx.x; t < p.ntiles; t += XT_THREADS) cnt[t] = 0u;
+    for (int t = threadIdx.x; t < p.ntiles * TC_EPI; t += XT_THREADS) cnt[t] = 0u;
   }
-  __syncthreads();
-  // max |x| over the finite elements, as bits
+  // max |x| over the finite elements, as bits (K % 32 == 0)
   uint32_t m = 0u;
   bool bad = false;
-  if (live)
-    for (int i = threadIdx.x; i < K; i += XT_THREADS) {
-      const uint32_t a = __float_as_uint(xc[i]) & 0x7FFFFFFFu;
-      if (a >= 0x7F800000u) bad = true;
-      else m = max(m, a);
+  if (live) {
+    if ((reinterpret_cast<uintptr_t>(xc) & 15) == 0) {
+      const float4* x4 = reinterpret_cast<const float4*>(xc);
+      for (int i = threadIdx.x; i < K / 4; i += XT_THREADS) {
+        const float4 v = x4[i];
+        m = max(max(m, finite_abs_bits(v.x, bad)), finite_abs_bits(v.y, bad));
+        m = max(max(m, finite_abs_bits(v.z, bad)), finite_abs_bits(v.w, bad));
+      }
+    } else {
+      for (int i = threadIdx.x; i < K; i += XT_THREADS) m = max(m, finite_abs_bits(xc[i], bad));
     }
-  if (bad) nonfinite = 1;
+  }
+  const bool nf = __syncthreads_or(bad) != 0;
   for (int o = 16; o; o >>= 1) m = max(m, __shfl_xor_sync(0xffffffffu, m, o));
   if (lane == 0) red[warp] = m;
   __syncthreads();
@@ -514,15 +534,16 @@ __global__ void __launch_bounds__(XT_THREADS) k_xprep_tc(const float* __restrict
     frexpf(__uint_as_float(m), &ee);  // max = f 2^ee, f in [0.5, 1)
     sh = 15 - ee;
   }
-  const bool nf = nonfinite != 0;
-  int* hdr = reinterpret_cast<int*>(p.ws);
-  if (threadIdx.x == 0) {
+  if (blockIdx.x == 0 && threadIdx.x == 0) {
+    int* hdr = reinterpret_cast<int*>(p.ws);
     hdr[col] = sh;
     hdr[16 + col] = nf ? 1 : 0;
   }
-  // blocks: warp w takes blocks w, w + 8, ...; lane = element of the block
+  // this CTA's blocks: warp w takes blocks b0 + w, b0 + w + 8, ...; lane =
+  // element of the block
   const int nblk = p.nkt * TC_BLK;
-  for (int gb = warp; gb < nblk; gb += XT_THREADS / 32) {
+  const int b0 = blockIdx.x * chunk, b1 = min(nblk, b0 + chunk);
+  for (int gb = b0 + warp; gb < b1; gb += XT_THREADS / 32) {
     const int kt = gb / TC_BLK, b = gb % TC_BLK;
     const int k = gb * QK + lane;
     const float v = live && !nf && k < K ? ldexpf(xc[k], sh) : 0.0f;
@@ -538,12 +559,12 @@ __global__ void __launch_bounds__(XT_THREADS) k_xprep_tc(const float* __restrict
     const int p2 = (X1 - p1) >> 8;
     uint8_t* xt = p.ws + p.xt_off + (size_t)kt * C::XT;
     const int kb = b * QK + lane;  // element inside the K tile
-    const int box = kb >> 7, within = kb & 127, chunk = within >> 4;
+    const int box = kb >> 7, within = kb & 127, chk = within >> 4;
     const int pv[3] = {p0, p1, p2};
 #pragma unroll
     for (int pl = 0; pl < 3; ++pl) {
       const int nrow = pl * NC + col;  // B row
-      xt[box * C::BBOX + (nrow >> 3) * 1024 + (nrow & 7) * 128 + ((chunk ^ (nrow & 7)) << 4) +
+      xt[box * C::BBOX + (nrow >> 3) * 1024 + (nrow & 7) * 128 + ((chk ^ (nrow & 7)) << 4) +
          (within & 15)] = (uint8_t)(signed char)pv[pl];
     }
     if (lane == 0) {
@@ -611,7 +632,7 @@ WsLayout ws_layout(int64_t M, int64_t K, int grid) {
   const int64_t nkt = (K + TC_KT - 1) / TC_KT, ntiles = (M + TC_M - 1) / TC_M;
   WsLayout w;
   w.cnt_off = TC_HDR;
-  w.part_off = w.cnt_off + (int)((ntiles * 4 + 15) / 16 * 16);
+  w.part_off = w.cnt_off + (int)((ntiles * TC_EPI * 4 + 15) / 16 * 16);
   w.xt_off = w.part_off + grid * 2 * NC * TC_M * 4;
   w.bytes = (size_t)w.xt_off + (size_t)nkt * TcCfg<NC>::XT;
   return w;
@@ -659,9 +680,10 @@ int launch_tc(const void* tiles, int64_t M, int64_t K, const float* x, int64_t l
   cfg.stream = st;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  cfg.gridDim = dim3(NC);
+  const int chunk = xprep_chunk(K);
+  cfg.gridDim = dim3((a.nkt * TC_BLK + chunk - 1) / chunk, NC);
   cfg.blockDim = dim3(XT_THREADS);
-  cudaError_t e = cudaLaunchKernelEx(&cfg, k_xprep_tc<NC>, x, ldx, (int)K, N, a);
+  cudaError_t e = cudaLaunchKernelEx(&cfg, k_xprep_tc<NC>, x, ldx, (int)K, N, chunk, a);
   if (e != cudaSuccess) return set_error(ERR_CUDA, "k_xprep_tc launch: %s", cudaGetErrorString(e));
   cfg.gridDim = dim3(grid);
   cfg.blockDim = dim3(TC_THREADS);
