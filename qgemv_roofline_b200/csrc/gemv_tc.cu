@@ -8,17 +8,18 @@
 // and leaves the integer block dots in tensor memory (TMEM), where the CUDA
 // cores scale them once per block:
 //
-//  * x (prep kernel, one CTA per column): each column is normalised by an
-//    exact power of two 2^sh (max |x'| in [2^14, 2^15)); each 32-element
-//    block of it is rounded to block fixed point X_j = rint(x'_j 2^(22-e)),
-//    |x'| < 2^e on the block, |X_j| <= 2^22, and split into three signed
-//    byte digits X = p0 + 2^8 p1 + 2^16 p2 (p0, p1 in [-128, 127], p2 in
-//    [-64, 64]).  The digits are the B operand, row plane * NC + column, so
-//    one MMA (M = 128 rows, N = 32 or 48, K = 32) computes the three plane
-//    sums S_p of every column for 128 rows and one block, exactly
-//    (|S_p| < 2^19).
+//  * x (prep kernel, many CTAs): each 32-element block of a column is
+//    rounded to block fixed point X_j = rint(x_j 2^(22-e)), |x| < 2^e on the
+//    block, |X_j| <= 2^22, and split into three signed byte digits
+//    X = p0 + 2^8 p1 + 2^16 p2 (p0, p1 in [-128, 127], p2 in [-64, 64]).  The
+//    digits are the B operand, row plane * NC + column, so one MMA (M = 128
+//    rows, N = 8 to 48, K = 32) computes the three plane sums S_p of every
+//    column for 128 rows and one block, exactly (|S_p| < 2^19).  The block
+//    scale is 2^(e + sh - 22), where 2^sh normalises the column (max |x 2^sh|
+//    in [2^14, 2^15), so no scale leaves the float range); the GEMV derives
+//    sh from the prep CTAs' maxima.
 //  * epilogue (8 warps; TMEM lane = row): lo = S0 + 2^8 S1 (exact in int32),
-//    F = 2^16 S2 + lo in fp32, acc[n] += F * (d * 2^(e-22)); y = acc 2^-sh.
+//    F = 2^16 S2 + lo in fp32, acc[n] += F * (d * 2^(e+sh-22)); y = acc 2^-sh.
 //    The rounding of x to the 2^(e-22) grid moves a row's dot by at most
 //    2^-23 sqrt(32) ||w|| ||x|| (Cauchy-Schwarz over each block), the fp32
 //    steps by a few ulps of the block terms: well inside 1e-5 ||w|| ||x||.
@@ -38,20 +39,24 @@
 // last part (a counter per row tile): it adds the CTAs' partial sums in CTA
 // order, so results do not depend on timing.
 //
-// Per CTA (10 warps): warp 0 streams (weight tile, x tile) pairs into a
-// 4-stage shared-memory ring (bulk copies); one thread of warp 1 issues the
-// 8 MMAs of a stage, 4 (or, at 16 columns, 2) blocks into each slot of a TMEM
-// ring (4 slots of 4 x 32 columns, or 5 of 2 x 48), and commits each slot to
-// an mbarrier; warps 2..9 (two groups of four, one warp per TMEM lane
-// quarter, group g taking column half g) read their part of a whole slot back
-// with one wait (tcgen05.ld), release it and accumulate: the TMEM read
+// Per CTA (10 warps): warp 0 streams each unit with bulk copies into two
+// shared-memory rings: the quants and the x digits (what the MMAs read) into
+// a ring of 4-6 weight stages, freed by the MMAs' commit alone, and the
+// tile's fp16 scales with the x block scales into an 8-slot scale ring, freed
+// by the epilogue; so the weight stream never waits for the epilogue's
+// arithmetic.  One thread of warp 1 issues the 8 MMAs of a stage, 4 (or, at
+// 16 columns, 2) blocks into each slot of a TMEM ring (8 x 4 x 8, 8 x 4 x 16,
+// 4 x 4 x 32 or 5 x 2 x 48 columns at 2, 4, 8, 16 columns of x), and commits
+// each slot to an mbarrier; warps 2..9 (two groups of four, one warp per TMEM
+// lane quarter, group g taking column half g) read their part of a whole slot
+// back with one wait (tcgen05.ld), release it and accumulate: the TMEM read
 // latency is paid once per slot, not once per block.  No barrier joins the
 // epilogue warps: each owns its rows and columns, and at the end of a row
-// tile stores y (or, for a row tile shared with other CTAs, its part).  Every wait is bounded (the
-// library's wait limit): on timeout the error word records
-// QGEMV_ERR_TIMEOUT, the producer stops and waits for its copies, the MMA
-// thread stops issuing, the epilogue runs out its loop without waiting, and
-// the CTA frees its TMEM before it returns.
+// tile stores y (or, for a row tile shared with other CTAs, its part).
+// Every wait is bounded (the library's wait limit): on timeout the error word
+// records QGEMV_ERR_TIMEOUT, the producer stops and waits for its copies, the
+// MMA thread stops issuing, the epilogue runs out its loop without waiting,
+// and the CTA frees its TMEM before it returns.
 #include "qgemv_common.cuh"
 #include "qgemv_internal.h"
 
@@ -75,29 +80,45 @@ constexpr int TC_TMEM_COLS = 512;
 constexpr int TC_GROUPS = 2;                    // epilogue warp groups (one per column half)
 constexpr int TC_EPI = 4 * TC_GROUPS;           // epilogue warps
 constexpr int TC_THREADS = 32 * (2 + TC_EPI);
-constexpr int TC_STAGES = 4;
-constexpr int TC_HDR = 128;                     // workspace header: sh[16], nonfinite[16]
+constexpr int TC_PMAX = 64;                     // x prep chunks per column, at most
+// workspace header: per column and prep chunk, the chunk's max |x| as bits
+// (0xFFFFFFFF when the chunk holds a NaN or an infinity)
+constexpr int TC_HDR = 16 * TC_PMAX * 4;
+constexpr int TC_EMPTY = -100000;               // block exponent of an all-zero block
+constexpr int TC_SMEM_MAX = 227 * 1024 - 512;   // dynamic shared memory we use at most
+constexpr int TC_SS = 8;                        // scale ring slots
+constexpr int TC_MAXSLOTS = 8;                  // TMEM slots, at most
 
 template <int NC>
 struct TcCfg {
-  static constexpr int NB = NC == 16 ? 48 : 32;       // MMA N = B rows (3 * NC used)
+  // MMA N = B rows, of which 3 * NC hold digits (N = 8, 16, 32 or 48)
+  static constexpr int NB = NC == 16 ? 48 : NC == 8 ? 32 : NC == 4 ? 16 : 8;
   static constexpr int BBOX = NB * 128;               // one box of x digits
   static constexpr int XB = 2 * BBOX;                 // x digits of a K tile
   static constexpr int XSB = TC_BLK * NC * 4;         // block scales [block][column] fp32
   static constexpr int XT = XB + XSB;                 // x tile bytes (multiple of 16)
-  static constexpr int STAGE = (TC_TILE + XT + 1023) / 1024 * 1024;
+  // weight stage: quants + x digits (what the MMAs read; freed by their commit)
+  static constexpr int WSTAGE = TC_ABYTES + XB;       // a multiple of 1024
+  // scale slot: the tile's fp16 scales + x block scales (read by the epilogue)
+  static constexpr int SSLOT = (TC_DBYTES + XSB + 127) / 128 * 128;
+  static constexpr int SW = (TC_SMEM_MAX - 1024 - TC_SS * SSLOT) / WSTAGE > 6
+                                ? 6
+                                : (TC_SMEM_MAX - 1024 - TC_SS * SSLOT) / WSTAGE;
   static constexpr int BPS = NC == 16 ? 2 : 4;        // blocks per TMEM slot (one read)
   static constexpr int HS = TC_BLK / 2 / BPS;         // slots per tile half
-  static constexpr int SLOTS = TC_TMEM_COLS / (BPS * NB);  // TMEM slots: 4 (NB 32), 5 (NB 48)
-  static constexpr size_t SMEM = (size_t)TC_STAGES * STAGE + 1024;
+  static constexpr int SLOTS = TC_TMEM_COLS / (BPS * NB) > TC_MAXSLOTS ? TC_MAXSLOTS
+                                                                       : TC_TMEM_COLS / (BPS * NB);
+  static constexpr size_t SMEM = (size_t)SW * WSTAGE + (size_t)TC_SS * SSLOT + 1024;
   // kind::i8: s32 accumulators (bits 4-5 = 2), A and B signed (bits 7-9,
   // 10-12 = 1), both K-major (bits 15, 16 = 0), N >> 3 at bit 17, M >> 4 at 24
   static constexpr uint32_t IDESC = (2u << 4) | (1u << 7) | (1u << 10) |
                                     ((uint32_t)(NB >> 3) << 17) | ((uint32_t)(TC_M >> 4) << 24);
 };
-static_assert(TcCfg<16>::SMEM <= 227 * 1024, "ring too large");
-static_assert(TcCfg<16>::SLOTS == 5 && TcCfg<8>::SLOTS == 4, "TMEM slots");
-static_assert(TC_TILE % 1024 == 0, "B operand must stay 1024-byte aligned");
+static_assert(TcCfg<16>::SMEM <= TC_SMEM_MAX && TcCfg<2>::SMEM <= TC_SMEM_MAX, "ring too large");
+static_assert(TcCfg<16>::SW >= 4 && TcCfg<8>::SW >= 5 && TcCfg<2>::SW <= TC_SS, "ring depth");
+static_assert(TcCfg<16>::SLOTS == 5 && TcCfg<8>::SLOTS == 4 && TcCfg<2>::SLOTS == 8, "TMEM slots");
+static_assert(TC_ABYTES % 1024 == 0 && TcCfg<2>::WSTAGE % 1024 == 0, "operands stay 1024-byte aligned");
+
 
 __device__ __forceinline__ long long tc_spin_limit() {
   return *(volatile long long*)&g_tc_spin_limit;
@@ -215,6 +236,7 @@ struct TcArgs {
   float* y;
   int64_t ldy;
   int M, N, nkt, ntiles;
+  int nchunk;                     // x prep chunks per column
   int cnt_off, part_off, xt_off;  // workspace offsets (bytes)
 };
 
@@ -224,35 +246,52 @@ __device__ __forceinline__ int cta_of(int64_t u, int64_t U, int G) {
   return (int)(((u + 1) * G + U - 1) / U) - 1;
 }
 
-__device__ __forceinline__ float finish(float tot, const int* hdr, int c) {
-  return hdr[16 + c] ? __int_as_float(0x7FC00000) : ldexpf(tot, -hdr[c]);
+// y from the accumulated sum: NaN for a column holding a NaN or an infinity,
+// else the sum scaled back by 2^-sh.
+__device__ __forceinline__ float finish(float tot, int sh, bool nonfinite) {
+  return nonfinite ? __int_as_float(0x7FC00000) : ldexpf(tot, -sh);
+}
+
+// 2^k as a float, 0 below the normal range (k <= 15 here).
+__device__ __forceinline__ float exp2i(int k) {
+  return k >= -126 ? __int_as_float((k + 127) << 23) : 0.0f;
 }
 
 template <int NC>
 __global__ void __launch_bounds__(TC_THREADS, 1) k_gemv_tc(const __grid_constant__ TcArgs p) {
   using C = TcCfg<NC>;
+  constexpr int SW = C::SW;
   extern __shared__ uint8_t tc_smem_raw[];
-  __shared__ __align__(8) unsigned long long full[TC_STAGES];
-  __shared__ __align__(8) unsigned long long empty[TC_STAGES];
-  __shared__ __align__(8) unsigned long long tfull[5];
-  __shared__ __align__(8) unsigned long long tempty[5];
+  __shared__ __align__(8) unsigned long long full[SW];       // weight stage landed
+  __shared__ __align__(8) unsigned long long empty[SW];      // its MMAs have read it
+  __shared__ __align__(8) unsigned long long sfull[TC_SS];   // scale slot landed
+  __shared__ __align__(8) unsigned long long sempty[TC_SS];  // the epilogue is done with it
+  __shared__ __align__(8) unsigned long long tfull[TC_MAXSLOTS];
+  __shared__ __align__(8) unsigned long long tempty[TC_MAXSLOTS];
   __shared__ __align__(8) unsigned long long mma_done;
   __shared__ uint32_t tmem_base;
   __shared__ int abort_flag;
+  __shared__ float xscr[TC_EPI][8 * NC];  // per epilogue warp: block scales of a unit
 
-  // 1024-byte-aligned ring (the swizzle works on address bits)
+  // 1024-byte-aligned weight ring (the swizzle works on address bits), then
+  // the scale ring
   uint8_t* ring = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(tc_smem_raw) + 1023) & ~(uintptr_t)1023);
-  const uint32_t ring_s = saddr(ring);
+  uint8_t* sring = ring + (size_t)SW * C::WSTAGE;
+  const uint32_t ring_s = saddr(ring), sring_s = saddr(sring);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t U = (int64_t)p.ntiles * p.nkt;
   const int64_t u0 = U * blockIdx.x / gridDim.x, u1 = U * (blockIdx.x + 1) / gridDim.x;
   const int nunits = (int)(u1 - u0);
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < TC_STAGES; ++s) {
+    for (int s = 0; s < SW; ++s) {
       mbar_init(saddr(&full[s]), 1);
-      mbar_init(saddr(&empty[s]), 1 + TC_EPI);  // the MMA commit + every epilogue warp
+      mbar_init(saddr(&empty[s]), 1);  // the MMA commit
+    }
+    for (int s = 0; s < TC_SS; ++s) {
+      mbar_init(saddr(&sfull[s]), 1);
+      mbar_init(saddr(&sempty[s]), TC_EPI);  // every epilogue warp
     }
     for (int s = 0; s < C::SLOTS; ++s) {
       mbar_init(saddr(&tfull[s]), 1);
@@ -276,48 +315,61 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_gemv_tc(const __grid_constant
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
+    // unit i: quants -> weight stage i % SW, x digits behind them; the tile's
+    // scales and the x block scales -> scale slot i % TC_SS
     if (lane == 0) {
+      const uint8_t* xt = p.ws + p.xt_off;
       // weights do not depend on the previous kernel: prefetch them first
-      const int pre = min(TC_STAGES, nunits);
+      const int pre = min(SW, nunits);
       for (int i = 0; i < pre; ++i) {
-        const uint32_t bar = saddr(&full[i]);
-        mbar_expect_tx(bar, (uint32_t)(TC_TILE + C::XT));
-        bulk_g2s(ring_s + (uint32_t)(i * C::STAGE), p.tiles + (u0 + i) * TC_TILE, TC_TILE, bar);
+        const uint8_t* t = p.tiles + (u0 + i) * TC_TILE;
+        mbar_expect_tx(saddr(&full[i]), (uint32_t)(TC_ABYTES + C::XB));
+        mbar_expect_tx(saddr(&sfull[i]), (uint32_t)(TC_DBYTES + C::XSB));
+        bulk_g2s(ring_s + (uint32_t)(i * C::WSTAGE), t, TC_ABYTES, saddr(&full[i]));
+        bulk_g2s(sring_s + (uint32_t)(i * C::SSLOT), t + TC_ABYTES, TC_DBYTES, saddr(&sfull[i]));
       }
       asm volatile("griddepcontrol.wait;" ::: "memory");  // x tiles are written by the prep kernel
       for (int i = 0; i < pre; ++i) {
-        const int kt = (int)((u0 + i) % p.nkt);
-        bulk_g2s(ring_s + (uint32_t)(i * C::STAGE + TC_TILE), p.ws + p.xt_off + (int64_t)kt * C::XT,
-                 C::XT, saddr(&full[i]));
+        const uint8_t* x = xt + (int64_t)((u0 + i) % p.nkt) * C::XT;
+        bulk_g2s(ring_s + (uint32_t)(i * C::WSTAGE + TC_ABYTES), x, C::XB, saddr(&full[i]));
+        bulk_g2s(sring_s + (uint32_t)(i * C::SSLOT + TC_DBYTES), x + C::XB, C::XSB, saddr(&sfull[i]));
       }
       int issued = pre;
       for (int i = pre; i < nunits; ++i) {
-        const int s = i % TC_STAGES;
-        if (!mbar_wait(saddr(&empty[s]), (uint32_t)(((i / TC_STAGES) - 1) & 1), &abort_flag)) break;
+        const int s = i % SW, j = i % TC_SS;
+        if (!mbar_wait(saddr(&empty[s]), (uint32_t)(((i / SW) - 1) & 1), &abort_flag)) break;
+        if (i >= TC_SS &&
+            !mbar_wait(saddr(&sempty[j]), (uint32_t)(((i / TC_SS) - 1) & 1), &abort_flag))
+          break;
         const int64_t u = u0 + i;
-        const int kt = (int)(u % p.nkt);
-        const uint32_t bar = saddr(&full[s]);
-        const uint32_t dst = ring_s + (uint32_t)(s * C::STAGE);
-        mbar_expect_tx(bar, (uint32_t)(TC_TILE + C::XT));
-        bulk_g2s(dst, p.tiles + u * TC_TILE, TC_TILE, bar);
-        bulk_g2s(dst + TC_TILE, p.ws + p.xt_off + (int64_t)kt * C::XT, C::XT, bar);
+        const uint8_t* t = p.tiles + u * TC_TILE;
+        const uint8_t* x = xt + (int64_t)(u % p.nkt) * C::XT;
+        mbar_expect_tx(saddr(&full[s]), (uint32_t)(TC_ABYTES + C::XB));
+        mbar_expect_tx(saddr(&sfull[j]), (uint32_t)(TC_DBYTES + C::XSB));
+        bulk_g2s(ring_s + (uint32_t)(s * C::WSTAGE), t, TC_ABYTES, saddr(&full[s]));
+        bulk_g2s(ring_s + (uint32_t)(s * C::WSTAGE + TC_ABYTES), x, C::XB, saddr(&full[s]));
+        bulk_g2s(sring_s + (uint32_t)(j * C::SSLOT), t + TC_ABYTES, TC_DBYTES, saddr(&sfull[j]));
+        bulk_g2s(sring_s + (uint32_t)(j * C::SSLOT + TC_DBYTES), x + C::XB, C::XSB, saddr(&sfull[j]));
         issued = i + 1;
       }
-      if (issued < nunits)  // aborted: wait (bounded) for the copies still in flight
-        for (int i = max(0, issued - TC_STAGES); i < issued; ++i)
-          mbar_wait_drain(saddr(&full[i % TC_STAGES]), (uint32_t)((i / TC_STAGES) & 1));
+      if (issued < nunits) {  // aborted: wait (bounded) for the copies still in flight
+        for (int i = max(0, issued - SW); i < issued; ++i)
+          mbar_wait_drain(saddr(&full[i % SW]), (uint32_t)((i / SW) & 1));
+        for (int i = max(0, issued - TC_SS); i < issued; ++i)
+          mbar_wait_drain(saddr(&sfull[i % TC_SS]), (uint32_t)((i / TC_SS) & 1));
+      }
     }
   } else if (warp == 1) {
     // ---------------------------------------------------------- MMA issuer
     if (lane == 0) {
       bool ok = true;
       for (int i = 0; i < nunits && ok; ++i) {
-        const int s = i % TC_STAGES;
-        ok = mbar_wait(saddr(&full[s]), (uint32_t)((i / TC_STAGES) & 1), &abort_flag);
+        const int s = i % SW;
+        ok = mbar_wait(saddr(&full[s]), (uint32_t)((i / SW) & 1), &abort_flag);
         if (!ok) break;
         tc_fence_after();
-        const uint32_t a0 = ring_s + (uint32_t)(s * C::STAGE);
-        const uint32_t b0 = a0 + TC_TILE;
+        const uint32_t a0 = ring_s + (uint32_t)(s * C::WSTAGE);
+        const uint32_t b0 = a0 + TC_ABYTES;
         // slot sl of the tile (blocks sl * BPS ...) into TMEM slot hh % SLOTS,
         // hh = 2 HS i + sl
         for (int sl = 0; sl < 2 * C::HS && ok; ++sl) {
@@ -356,21 +408,59 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_gemv_tc(const __grid_constant
     const int quarter = warp & 3;  // TMEM lanes 32 * quarter ... (this warp's rows)
     const int g = e >> 2;          // this warp's columns: g * NCH ... (g + 1) * NCH - 1
     const int row = quarter * 32 + lane;
-    const int* hdr = reinterpret_cast<const int*>(p.ws);
+    // column n's normalisation 2^sh (max |x'| in [2^14, 2^15), exact) from
+    // the prep chunks' maxima; nonfinite: the column holds a NaN or an infinity
+    int shc[NCH];
+    bool nfc[NCH];
+#pragma unroll
+    for (int c = 0; c < NCH; ++c) {
+      const uint32_t* cm = reinterpret_cast<const uint32_t*>(p.ws) + (g * NCH + c) * TC_PMAX;
+      uint32_t m = 0u;
+      bool bad = false;
+      for (int k = lane; k < p.nchunk; k += 32) {
+        const uint32_t v = cm[k];
+        if (v == 0xFFFFFFFFu) bad = true;
+        else m = max(m, v);
+      }
+      for (int o = 16; o; o >>= 1) m = max(m, __shfl_xor_sync(0xffffffffu, m, o));
+      int sh = 0;
+      if (m != 0u) {
+        int ee;
+        frexpf(__uint_as_float(m), &ee);  // max = f 2^ee, f in [0.5, 1)
+        sh = 15 - ee;
+      }
+      shc[c] = sh;
+      nfc[c] = __any_sync(0xffffffffu, bad);
+    }
+    // lane l converts the block exponents of (block l / NCH, column l % NCH)
+    // (and of block (l + 32) / NCH when 8 NCH > 32) into block scales
+    int sh_l = 0;
+#pragma unroll
+    for (int c = 0; c < NCH; ++c)
+      if (c == lane % NCH) sh_l = shc[c];
     unsigned* cnt = reinterpret_cast<unsigned*>(p.ws + p.cnt_off);
     float* part = reinterpret_cast<float*>(p.ws + p.part_off);
     float acc[NCH];
 #pragma unroll
     for (int c = 0; c < NCH; ++c) acc[c] = 0.0f;
     for (int i = 0; i < nunits; ++i) {
-      const int s = i % TC_STAGES;
+      const int j = i % TC_SS;
       const int64_t u = u0 + i;
       const int rt = (int)(u / p.nkt), kt = (int)(u % p.nkt);
-      // the stage's scales are read from shared memory: wait for its copy too
-      mbar_wait(saddr(&full[s]), (uint32_t)((i / TC_STAGES) & 1), &abort_flag);
-      const uint8_t* stg = ring + (size_t)s * C::STAGE;
-      const uint4 d8 = *reinterpret_cast<const uint4*>(stg + TC_ABYTES + row * 16);  // 8 fp16
-      const float* xs = reinterpret_cast<const float*>(stg + TC_TILE + C::XB) + g * NCH;
+      // the unit's scales: scale slot j
+      mbar_wait(saddr(&sfull[j]), (uint32_t)((i / TC_SS) & 1), &abort_flag);
+      const uint8_t* sst = sring + (size_t)j * C::SSLOT;
+      const uint4 d8 = *reinterpret_cast<const uint4*>(sst + row * 16);  // 8 fp16
+      // block scales 2^(e + sh - 22) of this warp's columns, e = the block's
+      // exponent (|x| < 2^e on the block); zero for an all-zero block
+      // (converted lane-parallel into this warp's scratch, read back by
+      // broadcast)
+      const int* ei = reinterpret_cast<const int*>(sst + TC_DBYTES) + g * NCH + lane % NCH;
+      float* xs = xscr[e];
+      __syncwarp();  // the previous unit's reads of the scratch are done
+      if (lane < 8 * NCH) xs[lane] = exp2i(ei[(lane / NCH) * NC] + sh_l - 22);
+      if (8 * NCH > 32) xs[lane + 32] = exp2i(ei[((lane + 32) / NCH) * NC] + sh_l - 22);
+      __syncwarp();
 #pragma unroll
       for (int sl = 0; sl < 2 * C::HS; ++sl) {
         const uint32_t hh = 2u * C::HS * i + sl, slot = hh % C::SLOTS;
@@ -399,12 +489,12 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_gemv_tc(const __grid_constant
           for (int c = 0; c < NCH; ++c) {
             const int lo = (int)(v[bb][0][c] + (v[bb][1][c] << 8));  // exact: |lo| < 2^28
             const float f = fmaf((float)(int)v[bb][2][c], 65536.0f, (float)lo);
-            acc[c] = fmaf(f, dv * xs[b * NC + c], acc[c]);
+            acc[c] = fmaf(f, dv * xs[b * NCH + c], acc[c]);
           }
         }
       }
       __syncwarp();
-      if (lane == 0) mbar_arrive(saddr(&empty[s]));
+      if (lane == 0) mbar_arrive(saddr(&sempty[j]));
       if (kt != p.nkt - 1 && i != nunits - 1) continue;
       // ---- end of this CTA's part of row tile rt
       const int64_t t0 = (int64_t)rt * p.nkt;
@@ -413,7 +503,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_gemv_tc(const __grid_constant
 #pragma unroll
         for (int c = 0; c < NCH; ++c) {
           const int n = g * NCH + c;
-          if (r < p.M && n < p.N) p.y[(int64_t)n * p.ldy + r] = finish(acc[c], hdr, n);
+          if (r < p.M && n < p.N) p.y[(int64_t)n * p.ldy + r] = finish(acc[c], shc[c], nfc[c]);
           acc[c] = 0.0f;
         }
         continue;
@@ -446,7 +536,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_gemv_tc(const __grid_constant
 #pragma unroll
         for (int c = 0; c < NCH; ++c) {
           const int n = g * NCH + c;
-          if (r < p.M && n < p.N) p.y[(int64_t)n * p.ldy + r] = finish(tot[c], hdr, n);
+          if (r < p.M && n < p.N) p.y[(int64_t)n * p.ldy + r] = finish(tot[c], shc[c], nfc[c]);
         }
       }
     }
@@ -465,29 +555,21 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_gemv_tc(const __grid_constant
 
 // ------------------------------------------------------------- x prep
 // Grid (chunks, NC): CTA (c, col) handles blocks [c * chunk, (c + 1) * chunk)
-// of column col (columns >= N get zeros).  Every CTA of a column first finds
-// the column's maximum itself (the column is read once per CTA, from L2
-// after the first), then for each of its 32-element blocks the exponent, the
-// fixed-point digits (written where the B operand reads them) and the block
-// scale.  CTA (0, 0) also clears the counters of the shared row tiles.
+// of column col (columns >= N get zeros), one block per warp at a time: the
+// block's exponent e (|x| < 2^e on the block), the fixed-point digits of
+// rint(x 2^(22 - e)) (written where the B operand reads them; a power-of-two
+// normalisation of the column would not change them) and e itself.  The
+// CTA's maximum |x| goes to the header, from which the GEMV derives the
+// column's normalisation; no pass over the whole column.  CTA (0, 0) also
+// clears the counters of the shared row tiles.
 constexpr int XT_THREADS = 256;
-constexpr int XT_CHUNK_MIN = 32;             // blocks per CTA, at least
-constexpr int64_t XT_REREAD = (int64_t)1 << 18;  // column elements re-read per column, at most
 
+// Blocks per prep CTA: one per warp while that keeps to TC_PMAX CTAs a column.
 int xprep_chunk(int64_t K) {
   const int64_t nblk = (K + TC_KT - 1) / TC_KT * TC_BLK;
-  const int64_t ctas = std::max<int64_t>(1, std::min<int64_t>((nblk + XT_CHUNK_MIN - 1) / XT_CHUNK_MIN,
-                                                              XT_REREAD / std::max<int64_t>(K, 1)));
+  const int64_t per = XT_THREADS / 32;
+  const int64_t ctas = std::max<int64_t>(1, std::min<int64_t>(TC_PMAX, (nblk + per - 1) / per));
   return (int)((nblk + ctas - 1) / ctas);
-}
-
-__device__ __forceinline__ uint32_t finite_abs_bits(float v, bool& bad) {
-  const uint32_t a = __float_as_uint(v) & 0x7FFFFFFFu;
-  if (a >= 0x7F800000u) {
-    bad = true;
-    return 0u;
-  }
-  return a;
 }
 
 template <int NC>
@@ -506,52 +588,24 @@ __global__ void __launch_bounds__(XT_THREADS) k_xprep_tc(const float* __restrict
     unsigned* cnt = reinterpret_cast<unsigned*>(p.ws + p.cnt_off);
     for (int t = threadIdx.x; t < p.ntiles * TC_EPI; t += XT_THREADS) cnt[t] = 0u;
   }
-  // max |x| over the finite elements, as bits (K % 32 == 0)
-  uint32_t m = 0u;
-  bool bad = false;
-  if (live) {
-    if ((reinterpret_cast<uintptr_t>(xc) & 15) == 0) {
-      const float4* x4 = reinterpret_cast<const float4*>(xc);
-      for (int i = threadIdx.x; i < K / 4; i += XT_THREADS) {
-        const float4 v = x4[i];
-        m = max(max(m, finite_abs_bits(v.x, bad)), finite_abs_bits(v.y, bad));
-        m = max(max(m, finite_abs_bits(v.z, bad)), finite_abs_bits(v.w, bad));
-      }
-    } else {
-      for (int i = threadIdx.x; i < K; i += XT_THREADS) m = max(m, finite_abs_bits(xc[i], bad));
-    }
-  }
-  const bool nf = __syncthreads_or(bad) != 0;
-  for (int o = 16; o; o >>= 1) m = max(m, __shfl_xor_sync(0xffffffffu, m, o));
-  if (lane == 0) red[warp] = m;
-  __syncthreads();
-  m = 0u;
-  for (int w = 0; w < XT_THREADS / 32; ++w) m = max(m, red[w]);
-  // x' = x 2^sh with max |x'| in [2^14, 2^15) (exact); y = acc 2^-sh
-  int sh = 0;
-  if (m != 0u) {
-    int ee;
-    frexpf(__uint_as_float(m), &ee);  // max = f 2^ee, f in [0.5, 1)
-    sh = 15 - ee;
-  }
-  if (blockIdx.x == 0 && threadIdx.x == 0) {
-    int* hdr = reinterpret_cast<int*>(p.ws);
-    hdr[col] = sh;
-    hdr[16 + col] = nf ? 1 : 0;
-  }
-  // this CTA's blocks: warp w takes blocks b0 + w, b0 + w + 8, ...; lane =
-  // element of the block
   const int nblk = p.nkt * TC_BLK;
   const int b0 = blockIdx.x * chunk, b1 = min(nblk, b0 + chunk);
+  uint32_t cmax = 0u;  // max |x| of this warp's blocks, as bits (warp-uniform)
+  bool bad = false;    // a NaN or an infinity among them
   for (int gb = b0 + warp; gb < b1; gb += XT_THREADS / 32) {
     const int kt = gb / TC_BLK, b = gb % TC_BLK;
     const int k = gb * QK + lane;
-    const float v = live && !nf && k < K ? ldexpf(xc[k], sh) : 0.0f;
-    uint32_t a = __float_as_uint(v) & 0x7FFFFFFFu;
+    const float xv = live && k < K ? xc[k] : 0.0f;
+    uint32_t a = __float_as_uint(xv) & 0x7FFFFFFFu;
+    const bool nonfinite = __any_sync(0xffffffffu, a >= 0x7F800000u);
+    bad |= nonfinite;
+    const float v = nonfinite ? 0.0f : xv;  // such a column's y is NaN anyway
+    a = nonfinite ? 0u : a;
     for (int o = 16; o; o >>= 1) a = max(a, __shfl_xor_sync(0xffffffffu, a, o));
-    int e = 0;  // |x'| < 2^e on the block
-    if (a != 0u) frexpf(__uint_as_float(a), &e);
-    // X = rint(x' 2^(22 - e)), |X| <= 2^22 (ldexpf scales exactly here)
+    cmax = max(cmax, a);
+    int e = TC_EMPTY;
+    if (a != 0u) frexpf(__uint_as_float(a), &e);  // block max = f 2^e, f in [0.5, 1)
+    // X = rint(x 2^(22 - e)), |X| <= 2^22 (ldexpf scales exactly here)
     const int X = a == 0u ? 0 : __float2int_rn(ldexpf(v, 22 - e));
     const int p0 = (int)(signed char)(X & 0xFF);
     const int X1 = (X - p0) >> 8;
@@ -567,11 +621,15 @@ __global__ void __launch_bounds__(XT_THREADS) k_xprep_tc(const float* __restrict
       xt[box * C::BBOX + (nrow >> 3) * 1024 + (nrow & 7) * 128 + ((chk ^ (nrow & 7)) << 4) +
          (within & 15)] = (uint8_t)(signed char)pv[pl];
     }
-    if (lane == 0) {
-      // 2^(e - 22), zero where that underflows: such a block lies below
-      // 2^-104 of the column maximum, far under the error bound
-      reinterpret_cast<float*>(xt + C::XB)[b * NC + col] = a == 0u ? 0.0f : ldexpf(1.0f, e - 22);
-    }
+    if (lane == 0) reinterpret_cast<int*>(xt + C::XB)[b * NC + col] = e;
+  }
+  if (lane == 0) red[warp] = bad ? 0xFFFFFFFFu : cmax;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    uint32_t m = 0u;
+    for (int w = 0; w < XT_THREADS / 32; ++w)
+      m = (m == 0xFFFFFFFFu || red[w] == 0xFFFFFFFFu) ? 0xFFFFFFFFu : max(m, red[w]);
+    reinterpret_cast<uint32_t*>(p.ws)[col * TC_PMAX + blockIdx.x] = m;
   }
 }
 
@@ -681,7 +739,8 @@ int launch_tc(const void* tiles, int64_t M, int64_t K, const float* x, int64_t l
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   const int chunk = xprep_chunk(K);
-  cfg.gridDim = dim3((a.nkt * TC_BLK + chunk - 1) / chunk, NC);
+  a.nchunk = (a.nkt * TC_BLK + chunk - 1) / chunk;
+  cfg.gridDim = dim3(a.nchunk, NC);
   cfg.blockDim = dim3(XT_THREADS);
   cudaError_t e = cudaLaunchKernelEx(&cfg, k_xprep_tc<NC>, x, ldx, (int)K, N, chunk, a);
   if (e != cudaSuccess) return set_error(ERR_CUDA, "k_xprep_tc launch: %s", cudaGetErrorString(e));
