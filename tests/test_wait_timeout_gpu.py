@@ -118,3 +118,41 @@ def test_wait_limit_argument_and_default():
     assert lib.qgemv_set_wait_limit(1 << 50) == 7  # QGEMV_ERR_ARG: absurd limit
     assert lib.qgemv_set_wait_limit(-1) == OK      # default
     assert lib.qgemv_set_wait_limit(0) == OK
+
+
+def test_tc_kernel_waits_time_out_and_recover(short_wait_limit):
+    """The tcgen05 batch kernel under a 1 us wait limit: its ring waits run out
+    (the producer waiting for a free stage, the MMA thread for data, the
+    epilogue for accumulators), the CTAs stop, wait for their copies and MMAs
+    in flight, free their tensor memory and return; the error word reads
+    QGEMV_ERR_TIMEOUT, and the next call at the default limit is exact."""
+    lib = short_wait_limit
+    assert lib.qgemv_set_wait_limit(0) == OK
+    M, K, N = 28672, 8192, 4
+    q, d, _ = make("q8_0", M, K, seed=43)
+    qt, dt = planes(q, d)
+    tiles = qg.tile_weights_tc(q=qt, d=dt)
+    X = torch.randn(N, K, device=DEV, generator=torch.Generator(device=DEV).manual_seed(5))
+    y_good = qg.qgemv_tc(tiles, M, K, X).clone()
+    torch.cuda.synchronize()
+    assert lib.qgemv_check_device_error(0, None) == OK
+
+    assert lib.qgemv_set_wait_limit(1) == OK  # 1 us: shorter than a DRAM round trip under load
+    seen = False
+    for _ in range(3):
+        t0 = time.perf_counter()
+        y = qg.qgemv_tc(tiles, M, K, X)
+        torch.cuda.synchronize()
+        assert time.perf_counter() - t0 < 20.0  # returned
+        if lib.qgemv_check_device_error(1, None) == ERR_TIMEOUT:
+            seen = True
+            break
+    assert seen, "no wait of the tc kernel ran out under a 1 us limit"
+    assert lib.qgemv_check_device_error(0, None) == OK
+
+    assert lib.qgemv_set_wait_limit(0) == OK
+    for _ in range(2):
+        y2 = qg.qgemv_tc(tiles, M, K, X)
+        torch.cuda.synchronize()
+        assert torch.equal(y2, y_good)
+    assert lib.qgemv_check_device_error(0, None) == OK
