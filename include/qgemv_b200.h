@@ -294,29 +294,43 @@ QGEMV_API int qgemv_tiled_gemv(int format, const void* tiled, int64_t M, int64_t
                                const float* x, float* y, int32_t ncols, int64_t ldx, int64_t ldy,
                                void* workspace, size_t workspace_bytes, void* stream);
 
-/* q8_0 tc tiles: the weights re-laid for the tcgen05 (5th-generation tensor
- * core) batch kernel, one contiguous tile per 128 rows x 256 columns: the
- * int8 quants in the 128-byte-swizzled K-major layout the tensor core reads
- * from shared memory (2 boxes of [128 rows][128 bytes]; 16-byte chunk c of
- * row r at chunk position c ^ (r % 8); rows in groups of 8 at 1024 bytes),
- * then the [128 rows][8 blocks] fp16 scales; rows beyond M and columns
- * beyond K hold zero weights; tile (row tile t, K tile k) at
- * (t * ceil(K / 256) + k) * 34816 bytes.  Made once per weight matrix from
- * SoA planes (layout 0: q, d) or ggml blocks (layout 1: q = blocks).  No
- * reference counterpart: the reference had no batched kernel. */
+/* tc tiles: the weights re-laid for the tcgen05 (5th-generation tensor core)
+ * batch kernel, one contiguous tile per 128 rows x 256 columns; tile (row
+ * tile t, K tile k) at (t * ceil(K / 256) + k) * tile bytes.
+ *   q8_0 (34816 bytes): the int8 quants in the 128-byte-swizzled K-major
+ *     layout the tensor core reads from shared memory (2 boxes of
+ *     [128 rows][128 bytes]; 16-byte chunk c of row r at chunk position
+ *     c ^ (r % 8); rows in groups of 8 at 1024 bytes), then the
+ *     [128 rows][8 blocks] fp16 scales;
+ *   q4_0 (18432 bytes): the blocks' 16 nibble bytes as [8 blocks][128 rows]
+ *     (widened to int8 in shared memory by the kernel), then the scales.
+ * Rows beyond M and columns beyond K hold zero quants and zero scales.  Made
+ * once per weight matrix from SoA planes (layout 0: q, d) or ggml blocks
+ * (layout 1: q = blocks).  No reference counterpart: the reference had no
+ * batched kernel. */
+QGEMV_API size_t qgemv_tc_bytes(int format, int64_t M, int64_t K);
+QGEMV_API int qgemv_tc_tile(int format, int layout, const void* q, const void* d, int64_t M,
+                            int64_t K, void* tiles, void* stream);
+
+/* Y = X W^T from tc tiles on the tcgen05 tensor cores, any ncols >= 0 (16 per
+ * launch), K % 32 == 0, K <= 2^20.  Each 32-weight block is one integer MMA
+ * (kind::i8) against x in 22-bit block fixed point (three signed byte
+ * digits); rows are within 1e-5 ||w_row|| ||x|| of the exact dot, a column
+ * holding a NaN or an infinity gives NaN in every row.  workspace:
+ * qgemv_tc_workspace_bytes(M, K) bytes on the current device (both formats,
+ * any ncols), 16-byte aligned, or NULL for the per-stream workspace.  Calls
+ * that share a workspace must not overlap in time.  The kernel's waits are
+ * bounded by qgemv_set_wait_limit; a timeout is reported by
+ * qgemv_check_device_error. */
+QGEMV_API size_t qgemv_tc_workspace_bytes(int64_t M, int64_t K);
+QGEMV_API int qgemv_tc_gemv(int format, const void* tiles, int64_t M, int64_t K, const float* x,
+                            float* y, int32_t ncols, int64_t ldx, int64_t ldy, void* workspace,
+                            size_t workspace_bytes, void* stream);
+
+/* The same for q8_0 (format QGEMV_Q8_0 implied). */
 QGEMV_API size_t qgemv_q8_0_tc_bytes(int64_t M, int64_t K);
 QGEMV_API int qgemv_q8_0_tc_tile(int layout, const void* q, const void* d, int64_t M, int64_t K,
                                  void* tiles, void* stream);
-
-/* Y = X W^T from q8_0 tc tiles on the tcgen05 tensor cores, any ncols >= 0
- * (16 per launch), K % 32 == 0, K <= 2^20.  Each 32-weight block is one
- * integer MMA against x in 22-bit block fixed point (three signed byte
- * digits); rows are within 1e-5 ||w_row|| ||x|| of the exact dot, a column
- * holding a NaN or an infinity gives NaN in every row.  workspace:
- * qgemv_q8_0_tc_workspace_bytes(M, K) bytes on the current device, 16-byte
- * aligned, or NULL for the per-stream workspace.  Calls that share a
- * workspace must not overlap in time.  The kernel's waits are bounded by
- * qgemv_set_wait_limit; a timeout is reported by qgemv_check_device_error. */
 QGEMV_API size_t qgemv_q8_0_tc_workspace_bytes(int64_t M, int64_t K);
 QGEMV_API int qgemv_q8_0_tc(const void* tiles, int64_t M, int64_t K, const float* x, float* y,
                             int32_t ncols, int64_t ldx, int64_t ldy, void* workspace,

@@ -7,7 +7,7 @@ Public API (torch tensors as buffers; compute in libqgemv_b200.so):
   ``dequant_q4_0``, plus ``to_aos`` / ``from_aos`` and ``quantize_*_aos``;
 * GEMV: ``qgemv(fmt, q, d, x)``, ``qgemv_aos(fmt, blocks, x)``,
   ``qgemv_tiled(fmt, tile_weights(fmt, q, d), M, K, X)`` (batch tiles),
-  ``qgemv_tc(tile_weights_tc(q, d), M, K, X)`` (q8_0 on the tcgen05 tensor cores),
+  ``qgemv_tc(tile_weights_tc(q, d, fmt=fmt), M, K, X, fmt=fmt)`` (the tcgen05 tensor cores),
   ``QuantizedMatrix``;
 * GGUF files: ``gguf.GGUFReader`` (load q8_0 / q4_0 tensors onto a GPU), ``gguf.write_gguf``;
 * roof probes: ``roof.measure``, ``roof.cublas_fp16_mv``;

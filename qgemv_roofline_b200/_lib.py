@@ -130,6 +130,11 @@ SIGNATURES = {
     "qgemv_tiled_workspace_bytes": ([_i64, _i32], ctypes.c_size_t),
     "qgemv_tiled_gemv": ([ctypes.c_int, _vp, _i64, _i64, _vp, _vp, _i32, _i64, _i64, _vp,
                           ctypes.c_size_t, _vp], ctypes.c_int),
+    "qgemv_tc_bytes": ([ctypes.c_int, _i64, _i64], ctypes.c_size_t),
+    "qgemv_tc_tile": ([ctypes.c_int, ctypes.c_int, _vp, _vp, _i64, _i64, _vp, _vp], ctypes.c_int),
+    "qgemv_tc_workspace_bytes": ([_i64, _i64], ctypes.c_size_t),
+    "qgemv_tc_gemv": ([ctypes.c_int, _vp, _i64, _i64, _vp, _vp, _i32, _i64, _i64, _vp,
+                       ctypes.c_size_t, _vp], ctypes.c_int),
     "qgemv_q8_0_tc_bytes": ([_i64, _i64], ctypes.c_size_t),
     "qgemv_q8_0_tc_tile": ([ctypes.c_int, _vp, _vp, _i64, _i64, _vp, _vp], ctypes.c_int),
     "qgemv_q8_0_tc_workspace_bytes": ([_i64, _i64], ctypes.c_size_t),

@@ -656,13 +656,14 @@ QGEMV_API int qgemv_tiled_gemv(int format, const void* tiled, int64_t M, int64_t
   return OK;
 }
 
-QGEMV_API size_t qgemv_q8_0_tc_bytes(int64_t M, int64_t K) {
-  if (check_mk(M, K)) return 0;
-  return tc_tiles_bytes(M, K);
+QGEMV_API size_t qgemv_tc_bytes(int format, int64_t M, int64_t K) {
+  if (check_fmt(format) || check_mk(M, K)) return 0;
+  return tc_tiles_bytes(format, M, K);
 }
 
-QGEMV_API int qgemv_q8_0_tc_tile(int layout, const void* q, const void* d, int64_t M, int64_t K,
-                                 void* tiles, void* stream) {
+QGEMV_API int qgemv_tc_tile(int format, int layout, const void* q, const void* d, int64_t M,
+                            int64_t K, void* tiles, void* stream) {
+  if (int rc = check_fmt(format)) return rc;
   if (int rc = check_mk(M, K)) return rc;
   if (layout != 0 && layout != 1)
     return set_error(ERR_ARG, "layout must be 0 (SoA planes) or 1 (ggml blocks), got %d", layout);
@@ -672,19 +673,20 @@ QGEMV_API int qgemv_q8_0_tc_tile(int layout, const void* q, const void* d, int64
   if (misaligned(tiles, 16)) return set_error(ERR_ALIGN, "tiles must be 16-byte aligned");
   if (layout == 0 && (misaligned(q, 16) || misaligned(d, 2)))
     return set_error(ERR_ALIGN, "q must be 16-byte and d 2-byte aligned");
-  return tile_weights_tc(layout == 1, q, d, M, K, tiles, static_cast<cudaStream_t>(stream));
+  return tile_weights_tc(format, layout == 1, q, d, M, K, tiles, static_cast<cudaStream_t>(stream));
 }
 
-QGEMV_API size_t qgemv_q8_0_tc_workspace_bytes(int64_t M, int64_t K) {
+QGEMV_API size_t qgemv_tc_workspace_bytes(int64_t M, int64_t K) {
   if (check_mk(M, K)) return 0;
   DeviceInfo dev;
   if (current_device_info(dev)) return 0;
   return tc_workspace_bytes(M, K, dev.sms);
 }
 
-QGEMV_API int qgemv_q8_0_tc(const void* tiles, int64_t M, int64_t K, const float* x, float* y,
-                            int32_t ncols, int64_t ldx, int64_t ldy, void* workspace,
+QGEMV_API int qgemv_tc_gemv(int format, const void* tiles, int64_t M, int64_t K, const float* x,
+                            float* y, int32_t ncols, int64_t ldx, int64_t ldy, void* workspace,
                             size_t workspace_bytes, void* stream) {
+  if (int rc = check_fmt(format)) return rc;
   if (int rc = check_mk(M, K)) return rc;
   if (K > ((int64_t)1 << 20))
     return set_error(ERR_UNSUPPORTED, "K=%lld above 2^20 for tc tiles", (long long)K);
@@ -716,11 +718,28 @@ QGEMV_API int qgemv_q8_0_tc(const void* tiles, int64_t M, int64_t K, const float
   }
   for (int n0 = 0; n0 < ncols; n0 += 16) {
     const int n = std::min(16, ncols - n0);
-    if (int rc = gemv_tc(tiles, M, K, x + (int64_t)n0 * ldx, ldx, y + (int64_t)n0 * ldy, ldy, n,
-                         workspace, workspace_bytes, st))
+    if (int rc = gemv_tc(format, tiles, M, K, x + (int64_t)n0 * ldx, ldx, y + (int64_t)n0 * ldy,
+                         ldy, n, workspace, workspace_bytes, st))
       return rc;
   }
   return OK;
+}
+
+QGEMV_API size_t qgemv_q8_0_tc_bytes(int64_t M, int64_t K) { return qgemv_tc_bytes(8, M, K); }
+
+QGEMV_API int qgemv_q8_0_tc_tile(int layout, const void* q, const void* d, int64_t M, int64_t K,
+                                 void* tiles, void* stream) {
+  return qgemv_tc_tile(8, layout, q, d, M, K, tiles, stream);
+}
+
+QGEMV_API size_t qgemv_q8_0_tc_workspace_bytes(int64_t M, int64_t K) {
+  return qgemv_tc_workspace_bytes(M, K);
+}
+
+QGEMV_API int qgemv_q8_0_tc(const void* tiles, int64_t M, int64_t K, const float* x, float* y,
+                            int32_t ncols, int64_t ldx, int64_t ldy, void* workspace,
+                            size_t workspace_bytes, void* stream) {
+  return qgemv_tc_gemv(8, tiles, M, K, x, y, ncols, ldx, ldy, workspace, workspace_bytes, stream);
 }
 
 QGEMV_API int qgemv_q8_0_aos(const void* blocks, const float* x, float* y, int64_t M, int64_t K,

@@ -39,23 +39,26 @@
 // last part (a counter per row tile): it adds the CTAs' partial sums in CTA
 // order, so results do not depend on timing.
 //
-// Per CTA (10 warps): warp 0 streams each unit with bulk copies into two
-// shared-memory rings: the quants and the x digits (what the MMAs read) into
-// a ring of 4-6 weight stages, freed by the MMAs' commit alone, and the
-// tile's fp16 scales with the x block scales into an 8-slot scale ring, freed
-// by the epilogue; so the weight stream never waits for the epilogue's
-// arithmetic.  One thread of warp 1 issues the 8 MMAs of a stage, 4 (or, at
-// 16 columns, 2) blocks into each slot of a TMEM ring (8 x 4 x 8, 8 x 4 x 16,
-// 4 x 4 x 32 or 5 x 2 x 48 columns at 2, 4, 8, 16 columns of x), and commits
-// each slot to an mbarrier; warps 2..9 (two groups of four, one warp per TMEM
-// lane quarter, group g taking column half g) read their part of a whole slot
-// back with one wait (tcgen05.ld), release it and accumulate: the TMEM read
-// latency is paid once per slot, not once per block.  No barrier joins the
-// epilogue warps: each owns its rows and columns, and at the end of a row
-// tile stores y (or, for a row tile shared with other CTAs, its part).
+// Per CTA (11 warps; 19 for q4_0): warp 0 streams each unit with bulk copies
+// into two shared-memory rings: the quants and the x digits (what the MMAs
+// read) into a ring of 3-6 weight stages, freed by the MMAs' commit (and, for
+// q4_0, by the converter warps), and the tile's fp16 scales with the x block
+// exponents into an 8-slot scale ring, freed by the epilogue; so the weight
+// stream never waits for the epilogue's arithmetic.  One thread each of warps
+// 1 and 2 (alternate units: a tcgen05.mma costs ~80-90 cycles to issue)
+// issues the 8 MMAs of a unit, 4 (or, at 16 columns, 2) blocks into each slot
+// of a TMEM ring (8 x 4 x 8, 8 x 4 x 16, 4 x 4 x 32 or 5 x 2 x 48 columns at
+// 2, 4, 8, 16 columns of x), and commits each slot to an mbarrier; warps
+// 3..10 (two groups of four, one warp per TMEM lane quarter, group g taking
+// column half g) read their part of a whole slot back with one wait
+// (tcgen05.ld), release it and accumulate: the TMEM read latency is paid once
+// per slot, not once per block.  No barrier joins the epilogue warps: each
+// owns its rows and columns, and at the end of a row tile stores y (or, for a
+// row tile shared with other CTAs, its part).  For q4_0, warps 11..18 widen
+// each unit's nibbles into a 3-slot A ring first.
 // Every wait is bounded (the library's wait limit): on timeout the error word
 // records QGEMV_ERR_TIMEOUT, the producer stops and waits for its copies, the
-// MMA thread stops issuing, the epilogue runs out its loop without waiting,
+// MMA threads stop issuing, the epilogue runs out its loop without waiting,
 // and the CTA frees its TMEM before it returns.
 #include "qgemv_common.cuh"
 #include "qgemv_internal.h"
@@ -75,50 +78,80 @@ constexpr int TC_BLK = TC_KT / QK;              // blocks per tile (8)
 constexpr int TC_ABYTES = TC_M * TC_KT;         // quants of a tile
 constexpr int TC_BOX = TC_M * 128;              // one 128-byte-wide box of quants
 constexpr int TC_DBYTES = TC_M * TC_BLK * 2;    // fp16 scales of a tile
-constexpr int TC_TILE = TC_ABYTES + TC_DBYTES;  // 34816 bytes, a multiple of 1024
 constexpr int TC_TMEM_COLS = 512;
 constexpr int TC_GROUPS = 2;                    // epilogue warp groups (one per column half)
 constexpr int TC_EPI = 4 * TC_GROUPS;           // epilogue warps
-constexpr int TC_THREADS = 32 * (2 + TC_EPI);
+constexpr int TC_MMAW = 2;                      // MMA-issuing warps (each its own TMEM half)
+constexpr int TC_W0E = 1 + TC_MMAW;             // first epilogue warp
 constexpr int TC_PMAX = 64;                     // x prep chunks per column, at most
 // workspace header: per column and prep chunk, the chunk's max |x| as bits
 // (0xFFFFFFFF when the chunk holds a NaN or an infinity)
 constexpr int TC_HDR = 16 * TC_PMAX * 4;
 constexpr int TC_EMPTY = -100000;               // block exponent of an all-zero block
-constexpr int TC_SMEM_MAX = 227 * 1024 - 512;   // dynamic shared memory we use at most
+constexpr int TC_SMEM_MAX = 227 * 1024 - 1024;  // shared memory we use at most (dynamic + scratch)
 constexpr int TC_SS = 8;                        // scale ring slots
 constexpr int TC_MAXSLOTS = 8;                  // TMEM slots, at most
 
+// What depends on the column count only (the x side, shared with the prep).
 template <int NC>
 struct TcCfg {
   // MMA N = B rows, of which 3 * NC hold digits (N = 8, 16, 32 or 48)
   static constexpr int NB = NC == 16 ? 48 : NC == 8 ? 32 : NC == 4 ? 16 : 8;
   static constexpr int BBOX = NB * 128;               // one box of x digits
   static constexpr int XB = 2 * BBOX;                 // x digits of a K tile
-  static constexpr int XSB = TC_BLK * NC * 4;         // block scales [block][column] fp32
+  static constexpr int XSB = TC_BLK * NC * 4;         // block exponents [block][column] int32
   static constexpr int XT = XB + XSB;                 // x tile bytes (multiple of 16)
-  // weight stage: quants + x digits (what the MMAs read; freed by their commit)
-  static constexpr int WSTAGE = TC_ABYTES + XB;       // a multiple of 1024
-  // scale slot: the tile's fp16 scales + x block scales (read by the epilogue)
+  // scale slot: the tile's fp16 scales + x block exponents (read by the epilogue)
   static constexpr int SSLOT = (TC_DBYTES + XSB + 127) / 128 * 128;
-  static constexpr int SW = (TC_SMEM_MAX - 1024 - TC_SS * SSLOT) / WSTAGE > 6
-                                ? 6
-                                : (TC_SMEM_MAX - 1024 - TC_SS * SSLOT) / WSTAGE;
   static constexpr int BPS = NC == 16 ? 2 : 4;        // blocks per TMEM slot (one read)
-  static constexpr int HS = TC_BLK / 2 / BPS;         // slots per tile half
-  static constexpr int SLOTS = TC_TMEM_COLS / (BPS * NB) > TC_MAXSLOTS ? TC_MAXSLOTS
-                                                                       : TC_TMEM_COLS / (BPS * NB);
-  static constexpr size_t SMEM = (size_t)SW * WSTAGE + (size_t)TC_SS * SSLOT + 1024;
+  static constexpr int NSL = TC_BLK / BPS;            // TMEM slots per tile
+  static constexpr int SPW = NSL / TC_MMAW;           // of which each MMA warp issues
+  static constexpr int REG = TC_TMEM_COLS / TC_MMAW;  // TMEM columns of one MMA warp
+  // slots in each MMA warp's own ring
+  static constexpr int SLW = REG / (BPS * NB) > TC_MAXSLOTS ? TC_MAXSLOTS : REG / (BPS * NB);
   // kind::i8: s32 accumulators (bits 4-5 = 2), A and B signed (bits 7-9,
   // 10-12 = 1), both K-major (bits 15, 16 = 0), N >> 3 at bit 17, M >> 4 at 24
   static constexpr uint32_t IDESC = (2u << 4) | (1u << 7) | (1u << 10) |
                                     ((uint32_t)(NB >> 3) << 17) | ((uint32_t)(TC_M >> 4) << 24);
 };
-static_assert(TcCfg<16>::SMEM <= TC_SMEM_MAX && TcCfg<2>::SMEM <= TC_SMEM_MAX, "ring too large");
-static_assert(TcCfg<16>::SW >= 4 && TcCfg<8>::SW >= 5 && TcCfg<2>::SW <= TC_SS, "ring depth");
-static_assert(TcCfg<16>::SLOTS == 5 && TcCfg<8>::SLOTS == 4 && TcCfg<2>::SLOTS == 8, "TMEM slots");
-static_assert(TC_ABYTES % 1024 == 0 && TcCfg<2>::WSTAGE % 1024 == 0, "operands stay 1024-byte aligned");
 
+// q8_0 tiles hold the int8 quants in the MMA's A layout; q4_0 tiles hold the
+// nibbles packed as [8 blocks][128 rows][16 bytes], widened to int8 (n - 8)
+// in the A layout by 8 converter warps, into a 3-slot A ring.
+template <int FMT> __host__ __device__ constexpr int tc_qbytes() { return FMT == 8 ? TC_ABYTES : TC_ABYTES / 2; }
+template <int FMT> __host__ __device__ constexpr int tc_tile() { return tc_qbytes<FMT>() + TC_DBYTES; }
+
+template <int FMT, int NC>
+struct TcFmt : TcCfg<NC> {
+  static constexpr int QB = tc_qbytes<FMT>();         // quant bytes per tile
+  static constexpr int TILE = tc_tile<FMT>();         // 34816 (q8_0), 18432 (q4_0)
+  static constexpr int CONV = FMT == 8 ? 0 : 8;       // converter warps
+  static constexpr int SA = FMT == 8 ? 0 : 3;         // A ring slots (q4_0)
+  static constexpr int THREADS = 32 * (TC_W0E + TC_EPI + CONV);
+  // weight stage: quants + x digits (what the MMAs, or the converters, read)
+  static constexpr int WSTAGE = QB + TcCfg<NC>::XB;   // a multiple of 1024
+  // left for weight stages: the budget minus alignment slack, the scale and A
+  // rings and the epilogue warps' static scratch (8 x 8 NC floats)
+  static constexpr int FREE =
+      TC_SMEM_MAX - 1024 - TC_SS * TcCfg<NC>::SSLOT - SA * TC_ABYTES - TC_EPI * 8 * NC * 4;
+  static constexpr int SW = FREE / WSTAGE > 8 ? 8 : FREE / WSTAGE;
+  static constexpr size_t SMEM =
+      (size_t)SW * WSTAGE + (size_t)SA * TC_ABYTES + (size_t)TC_SS * TcCfg<NC>::SSLOT + 1024;
+};
+static_assert(TcFmt<8, 16>::SMEM + TC_EPI * 8 * 16 * 4 <= TC_SMEM_MAX &&
+                  TcFmt<4, 16>::SMEM + TC_EPI * 8 * 16 * 4 <= TC_SMEM_MAX &&
+                  TcFmt<8, 2>::SMEM <= TC_SMEM_MAX && TcFmt<4, 2>::SMEM <= TC_SMEM_MAX,
+              "ring too large");
+static_assert(TcFmt<8, 16>::SW >= 4 && TcFmt<8, 8>::SW >= 5 && TcFmt<4, 16>::SW >= 3 &&
+                  TcFmt<4, 2>::SW <= TC_SS,
+              "ring depth");
+static_assert(TcCfg<16>::SLW == 2 && TcCfg<8>::SLW == 2 && TcCfg<4>::SLW == 4 &&
+                  TcCfg<2>::SLW == 8 && TcCfg<16>::SPW >= 1 && TcCfg<2>::SPW >= 1 &&
+                  TcCfg<16>::SLW >= TcCfg<16>::SPW && TcCfg<8>::SLW >= TcCfg<8>::SPW,
+              "TMEM rings");
+static_assert(TC_ABYTES % 1024 == 0 && TcFmt<4, 2>::WSTAGE % 1024 == 0 &&
+                  TcFmt<8, 2>::WSTAGE % 1024 == 0,
+              "operands stay 1024-byte aligned");
 
 __device__ __forceinline__ long long tc_spin_limit() {
   return *(volatile long long*)&g_tc_spin_limit;
@@ -240,6 +273,17 @@ struct TcArgs {
   int cnt_off, part_off, xt_off;  // workspace offsets (bytes)
 };
 
+// q4_0 nibbles to int8: the 4 bytes of w hold weights j (low nibbles) and
+// j + 16 (high nibbles) of 4 consecutive j; n - 8 as a signed byte is the
+// nibble with bit 3 flipped (a 4-bit two's complement value), sign-extended:
+// m | 0xF0 where bit 3 of m is set, i.e. m + 0x1E * (bit 3 of m).
+__device__ __forceinline__ void widen_q4(uint32_t w, uint32_t& lo, uint32_t& hi) {
+  const uint32_t ml = (w & 0x0F0F0F0Fu) ^ 0x08080808u;
+  const uint32_t mh = ((w >> 4) & 0x0F0F0F0Fu) ^ 0x08080808u;
+  lo = ml + (ml & 0x08080808u) * 0x1Eu;  // 0x08 * 0x1E = 0xF0: no carry between bytes
+  hi = mh + (mh & 0x08080808u) * 0x1Eu;
+}
+
 // The CTA that owns unit u when U units are split over G CTAs as
 // [U c / G, U (c + 1) / G).
 __device__ __forceinline__ int cta_of(int64_t u, int64_t U, int G) {
@@ -257,28 +301,32 @@ __device__ __forceinline__ float exp2i(int k) {
   return k >= -126 ? __int_as_float((k + 127) << 23) : 0.0f;
 }
 
-template <int NC>
-__global__ void __launch_bounds__(TC_THREADS, 1) k_gemv_tc(const __grid_constant__ TcArgs p) {
-  using C = TcCfg<NC>;
+template <int FMT, int NC>
+__global__ void __launch_bounds__(TcFmt<FMT, NC>::THREADS, 1)
+    k_gemv_tc(const __grid_constant__ TcArgs p) {
+  using C = TcFmt<FMT, NC>;
   constexpr int SW = C::SW;
   extern __shared__ uint8_t tc_smem_raw[];
   __shared__ __align__(8) unsigned long long full[SW];       // weight stage landed
-  __shared__ __align__(8) unsigned long long empty[SW];      // its MMAs have read it
+  __shared__ __align__(8) unsigned long long empty[SW];      // its MMAs (and converters) read it
+  __shared__ __align__(8) unsigned long long afull[4];       // q4_0: A slot widened
+  __shared__ __align__(8) unsigned long long aempty[4];      // q4_0: its MMAs have read it
   __shared__ __align__(8) unsigned long long sfull[TC_SS];   // scale slot landed
   __shared__ __align__(8) unsigned long long sempty[TC_SS];  // the epilogue is done with it
-  __shared__ __align__(8) unsigned long long tfull[TC_MAXSLOTS];
-  __shared__ __align__(8) unsigned long long tempty[TC_MAXSLOTS];
+  __shared__ __align__(8) unsigned long long tfull[TC_MMAW][TC_MAXSLOTS];   // MMAs of a slot done
+  __shared__ __align__(8) unsigned long long tempty[TC_MMAW][TC_MAXSLOTS];  // the epilogue read it
   __shared__ __align__(8) unsigned long long mma_done;
   __shared__ uint32_t tmem_base;
   __shared__ int abort_flag;
   __shared__ float xscr[TC_EPI][8 * NC];  // per epilogue warp: block scales of a unit
 
-  // 1024-byte-aligned weight ring (the swizzle works on address bits), then
-  // the scale ring
+  // 1024-byte-aligned weight ring (the swizzle works on address bits), the A
+  // ring (q4_0), then the scale ring
   uint8_t* ring = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(tc_smem_raw) + 1023) & ~(uintptr_t)1023);
-  uint8_t* sring = ring + (size_t)SW * C::WSTAGE;
-  const uint32_t ring_s = saddr(ring), sring_s = saddr(sring);
+  uint8_t* aring = ring + (size_t)SW * C::WSTAGE;
+  uint8_t* sring = aring + (size_t)C::SA * TC_ABYTES;
+  const uint32_t ring_s = saddr(ring), aring_s = saddr(aring), sring_s = saddr(sring);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t U = (int64_t)p.ntiles * p.nkt;
   const int64_t u0 = U * blockIdx.x / gridDim.x, u1 = U * (blockIdx.x + 1) / gridDim.x;
@@ -287,17 +335,22 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_gemv_tc(const __grid_constant
   if (threadIdx.x == 0) {
     for (int s = 0; s < SW; ++s) {
       mbar_init(saddr(&full[s]), 1);
-      mbar_init(saddr(&empty[s]), 1);  // the MMA commit
+      mbar_init(saddr(&empty[s]), TC_MMAW + C::CONV);  // each MMA warp's commit (+ converter warps)
+    }
+    for (int s = 0; s < C::SA; ++s) {
+      mbar_init(saddr(&afull[s]), C::CONV);  // every converter warp
+      mbar_init(saddr(&aempty[s]), TC_MMAW);  // each MMA warp's commit
     }
     for (int s = 0; s < TC_SS; ++s) {
       mbar_init(saddr(&sfull[s]), 1);
       mbar_init(saddr(&sempty[s]), TC_EPI);  // every epilogue warp
     }
-    for (int s = 0; s < C::SLOTS; ++s) {
-      mbar_init(saddr(&tfull[s]), 1);
-      mbar_init(saddr(&tempty[s]), TC_EPI);  // every epilogue warp reads every slot
-    }
-    mbar_init(saddr(&mma_done), 1);
+    for (int w = 0; w < TC_MMAW; ++w)
+      for (int s = 0; s < C::SLW; ++s) {
+        mbar_init(saddr(&tfull[w][s]), 1);
+        mbar_init(saddr(&tempty[w][s]), TC_EPI);  // every epilogue warp reads every slot
+      }
+    mbar_init(saddr(&mma_done), TC_MMAW);  // one commit per MMA warp
     abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
@@ -322,16 +375,16 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_gemv_tc(const __grid_constant
       // weights do not depend on the previous kernel: prefetch them first
       const int pre = min(SW, nunits);
       for (int i = 0; i < pre; ++i) {
-        const uint8_t* t = p.tiles + (u0 + i) * TC_TILE;
-        mbar_expect_tx(saddr(&full[i]), (uint32_t)(TC_ABYTES + C::XB));
+        const uint8_t* t = p.tiles + (u0 + i) * C::TILE;
+        mbar_expect_tx(saddr(&full[i]), (uint32_t)(C::QB + C::XB));
         mbar_expect_tx(saddr(&sfull[i]), (uint32_t)(TC_DBYTES + C::XSB));
-        bulk_g2s(ring_s + (uint32_t)(i * C::WSTAGE), t, TC_ABYTES, saddr(&full[i]));
-        bulk_g2s(sring_s + (uint32_t)(i * C::SSLOT), t + TC_ABYTES, TC_DBYTES, saddr(&sfull[i]));
+        bulk_g2s(ring_s + (uint32_t)(i * C::WSTAGE), t, C::QB, saddr(&full[i]));
+        bulk_g2s(sring_s + (uint32_t)(i * C::SSLOT), t + C::QB, TC_DBYTES, saddr(&sfull[i]));
       }
       asm volatile("griddepcontrol.wait;" ::: "memory");  // x tiles are written by the prep kernel
       for (int i = 0; i < pre; ++i) {
         const uint8_t* x = xt + (int64_t)((u0 + i) % p.nkt) * C::XT;
-        bulk_g2s(ring_s + (uint32_t)(i * C::WSTAGE + TC_ABYTES), x, C::XB, saddr(&full[i]));
+        bulk_g2s(ring_s + (uint32_t)(i * C::WSTAGE + C::QB), x, C::XB, saddr(&full[i]));
         bulk_g2s(sring_s + (uint32_t)(i * C::SSLOT + TC_DBYTES), x + C::XB, C::XSB, saddr(&sfull[i]));
       }
       int issued = pre;
@@ -342,13 +395,13 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_gemv_tc(const __grid_constant
             !mbar_wait(saddr(&sempty[j]), (uint32_t)(((i / TC_SS) - 1) & 1), &abort_flag))
           break;
         const int64_t u = u0 + i;
-        const uint8_t* t = p.tiles + u * TC_TILE;
+        const uint8_t* t = p.tiles + u * C::TILE;
         const uint8_t* x = xt + (int64_t)(u % p.nkt) * C::XT;
-        mbar_expect_tx(saddr(&full[s]), (uint32_t)(TC_ABYTES + C::XB));
+        mbar_expect_tx(saddr(&full[s]), (uint32_t)(C::QB + C::XB));
         mbar_expect_tx(saddr(&sfull[j]), (uint32_t)(TC_DBYTES + C::XSB));
-        bulk_g2s(ring_s + (uint32_t)(s * C::WSTAGE), t, TC_ABYTES, saddr(&full[s]));
-        bulk_g2s(ring_s + (uint32_t)(s * C::WSTAGE + TC_ABYTES), x, C::XB, saddr(&full[s]));
-        bulk_g2s(sring_s + (uint32_t)(j * C::SSLOT), t + TC_ABYTES, TC_DBYTES, saddr(&sfull[j]));
+        bulk_g2s(ring_s + (uint32_t)(s * C::WSTAGE), t, C::QB, saddr(&full[s]));
+        bulk_g2s(ring_s + (uint32_t)(s * C::WSTAGE + C::QB), x, C::XB, saddr(&full[s]));
+        bulk_g2s(sring_s + (uint32_t)(j * C::SSLOT), t + C::QB, TC_DBYTES, saddr(&sfull[j]));
         bulk_g2s(sring_s + (uint32_t)(j * C::SSLOT + TC_DBYTES), x + C::XB, C::XSB, saddr(&sfull[j]));
         issued = i + 1;
       }
@@ -359,52 +412,111 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_gemv_tc(const __grid_constant
           mbar_wait_drain(saddr(&sfull[i % TC_SS]), (uint32_t)((i / TC_SS) & 1));
       }
     }
-  } else if (warp == 1) {
-    // ---------------------------------------------------------- MMA issuer
+  } else if (warp <= TC_MMAW) {
+    // --------------------------------------------------------- MMA issuers
+    // one thread per MMA warp; warp w (= mw + 1) issues slots mw * SPW ...
+    // (mw + 1) * SPW - 1 of every unit (a tcgen05.mma costs ~80-90 cycles to
+    // issue from one thread), into its own ring of SLW TMEM slots in columns
+    // mw * REG ...: each ring has one issuer, in order, so a slot's previous
+    // use is always issued before the wait for its release
     if (lane == 0) {
+      const int mw = warp - 1;
       bool ok = true;
       for (int i = 0; i < nunits && ok; ++i) {
         const int s = i % SW;
         ok = mbar_wait(saddr(&full[s]), (uint32_t)((i / SW) & 1), &abort_flag);
+        // q4_0: the widened quants of unit i are in A slot i % SA
+        if (ok && FMT == 4)
+          ok = mbar_wait(saddr(&afull[i % C::SA]), (uint32_t)((i / C::SA) & 1), &abort_flag);
         if (!ok) break;
         tc_fence_after();
-        const uint32_t a0 = ring_s + (uint32_t)(s * C::WSTAGE);
-        const uint32_t b0 = a0 + TC_ABYTES;
-        // slot sl of the tile (blocks sl * BPS ...) into TMEM slot hh % SLOTS,
-        // hh = 2 HS i + sl
-        for (int sl = 0; sl < 2 * C::HS && ok; ++sl) {
-          const uint32_t hh = 2u * C::HS * i + sl, slot = hh % C::SLOTS;
-          if (hh >= (uint32_t)C::SLOTS) {
-            ok = mbar_wait(saddr(&tempty[slot]), ((hh / C::SLOTS) - 1) & 1u, &abort_flag);
+        const uint32_t b0 = ring_s + (uint32_t)(s * C::WSTAGE + C::QB);
+        const uint32_t a0 = FMT == 8 ? ring_s + (uint32_t)(s * C::WSTAGE)
+                                     : aring_s + (uint32_t)((i % C::SA) * TC_ABYTES);
+        // descriptors of block 0; block b adds its byte offset >> 4 (the start
+        // address field, bits 0-13, cannot carry: shared addresses < 256 KB)
+        const uint64_t da0 = sw128_desc(a0), db0 = sw128_desc(b0);
+        // slot sl = mw SPW + r of the tile (blocks sl * BPS ...) into ring
+        // slot hl % SLW, hl = SPW i + r
+#pragma unroll
+        for (int r = 0; r < C::SPW && ok; ++r) {
+          const int sl = mw * C::SPW + r;
+          const uint32_t hl = (uint32_t)C::SPW * i + r, slot = hl % C::SLW;
+          if (hl >= (uint32_t)C::SLW) {
+            ok = mbar_wait(saddr(&tempty[mw][slot]), ((hl / C::SLW) - 1) & 1u, &abort_flag);
             if (!ok) break;
             tc_fence_after();
           }
+#pragma unroll
           for (int bb = 0; bb < C::BPS; ++bb) {
             // block b: box b / 4, 32-byte K step b % 4 inside its 128-byte rows
             const int b = sl * C::BPS + bb;
-            const uint64_t da = sw128_desc(a0 + (uint32_t)((b >> 2) * TC_BOX + (b & 3) * 32));
-            const uint64_t db = sw128_desc(b0 + (uint32_t)((b >> 2) * C::BBOX + (b & 3) * 32));
+            const uint64_t da = da0 + (uint64_t)((((b >> 2) * TC_BOX + (b & 3) * 32)) >> 4);
+            const uint64_t db = db0 + (uint64_t)((((b >> 2) * C::BBOX + (b & 3) * 32)) >> 4);
             asm volatile(
                 "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
                 " tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n}\n" ::"r"(
-                    tmem + (slot * C::BPS + bb) * C::NB),
+                    tmem + mw * C::REG + (slot * C::BPS + bb) * C::NB),
                 "l"(da), "l"(db), "r"(C::IDESC), "r"(0)
                 : "memory");
           }
-          tc_commit(saddr(&tfull[slot]));
+          tc_commit(saddr(&tfull[mw][slot]));
         }
         if (!ok) break;
         tc_commit(saddr(&empty[s]));  // the stage is free once these MMAs have read it
+        if (FMT == 4) tc_commit(saddr(&aempty[i % C::SA]));  // and so is the A slot
       }
       // every MMA issued completes before the accumulators are freed
       tc_commit(saddr(&mma_done));
       mbar_wait_drain(saddr(&mma_done), 0u);
     }
+  } else if (FMT == 4 && warp >= TC_W0E + TC_EPI) {
+    // ---------------------------------------------------------- converters
+    // q4_0: thread (r, h) (one per row of the tile and half of its blocks)
+    // widens blocks 4h .. 4h + 3 of row r (16 bytes of nibbles each: weight j
+    // low nibble, j + 16 high) into int8 n - 8 at the A layout's swizzled
+    // positions, unit after unit into A slot i % SA
+    const int ct = threadIdx.x - 32 * (TC_W0E + TC_EPI);  // 0..255
+    const int r = ct & (TC_M - 1), h = ct >> 7;
+    bool ok = true;
+    for (int i = 0; i < nunits && ok; ++i) {
+      const int s = i % SW;
+      ok = mbar_wait(saddr(&full[s]), (uint32_t)((i / SW) & 1), &abort_flag);
+      if (ok && i >= C::SA)
+        ok = mbar_wait(saddr(&aempty[i % C::SA]), (uint32_t)(((i / C::SA) - 1) & 1), &abort_flag);
+      if (!ok) break;
+      tc_fence_after();  // the A slot was last read by MMAs (async proxy)
+      const uint8_t* pk = ring + (size_t)s * C::WSTAGE;
+      uint8_t* arow = aring + (size_t)(i % C::SA) * TC_ABYTES + h * TC_BOX + (r >> 3) * 1024 +
+                      (r & 7) * 128;
+      uint4 w[4];
+#pragma unroll
+      for (int k = 0; k < 4; ++k) w[k] = *reinterpret_cast<const uint4*>(pk + ((4 * h + k) * TC_M + r) * 16);
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        uint4 lo, hi;
+        widen_q4(w[k].x, lo.x, hi.x);
+        widen_q4(w[k].y, lo.y, hi.y);
+        widen_q4(w[k].z, lo.z, hi.z);
+        widen_q4(w[k].w, lo.w, hi.w);
+        // block 4h + k: box h, 16-byte chunks 2k (weights 0-15) and 2k + 1
+        // (weights 16-31) of the row, swizzled
+        *reinterpret_cast<uint4*>(arow + (((2 * k) ^ (r & 7)) << 4)) = lo;
+        *reinterpret_cast<uint4*>(arow + (((2 * k + 1) ^ (r & 7)) << 4)) = hi;
+      }
+      // generic-proxy stores, read next by the tensor core (async proxy)
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      __syncwarp();
+      if (lane == 0) {
+        mbar_arrive(saddr(&afull[i % C::SA]));
+        mbar_arrive(saddr(&empty[s]));  // the packed quants are read
+      }
+    }
   } else {
     // ------------------------------------------------------------ epilogue
     asm volatile("griddepcontrol.wait;" ::: "memory");  // header and counters
     constexpr int NCH = NC / 2;    // columns per warp
-    const int e = warp - 2;
+    const int e = warp - TC_W0E;
     const int quarter = warp & 3;  // TMEM lanes 32 * quarter ... (this warp's rows)
     const int g = e >> 2;          // this warp's columns: g * NCH ... (g + 1) * NCH - 1
     const int row = quarter * 32 + lane;
@@ -462,13 +574,15 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_gemv_tc(const __grid_constant
       if (8 * NCH > 32) xs[lane + 32] = exp2i(ei[((lane + 32) / NCH) * NC] + sh_l - 22);
       __syncwarp();
 #pragma unroll
-      for (int sl = 0; sl < 2 * C::HS; ++sl) {
-        const uint32_t hh = 2u * C::HS * i + sl, slot = hh % C::SLOTS;
-        mbar_wait(saddr(&tfull[slot]), (hh / C::SLOTS) & 1u, &abort_flag);
+      for (int sl = 0; sl < C::NSL; ++sl) {
+        // slot sl of the tile: MMA warp mw's ring slot hl % SLW, hl = SPW i + r
+        const int mw = sl / C::SPW, r = sl % C::SPW;
+        const uint32_t hl = (uint32_t)C::SPW * i + r, slot = hl % C::SLW;
+        mbar_wait(saddr(&tfull[mw][slot]), (hl / C::SLW) & 1u, &abort_flag);
         __syncwarp();
         tc_fence_after();
         const uint32_t ta =
-            tmem + ((uint32_t)(quarter * 32) << 16) + slot * C::BPS * C::NB + g * NCH;
+            tmem + ((uint32_t)(quarter * 32) << 16) + mw * C::REG + slot * C::BPS * C::NB + g * NCH;
         uint32_t v[C::BPS][3][NCH];
 #pragma unroll
         for (int bb = 0; bb < C::BPS; ++bb)
@@ -478,7 +592,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_gemv_tc(const __grid_constant
         asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(saddr(&tempty[slot]));
+        if (lane == 0) mbar_arrive(saddr(&tempty[mw][slot]));
 #pragma unroll
         for (int bb = 0; bb < C::BPS; ++bb) {
           const int b = sl * C::BPS + bb;
@@ -634,24 +748,34 @@ __global__ void __launch_bounds__(XT_THREADS) k_xprep_tc(const float* __restrict
 }
 
 // ------------------------------------------------------------ tc tiles
-// One CTA per tile: quants (q8_0 from SoA planes or ggml blocks) in 16-byte
-// chunks, then the scales.
+// One CTA per tile, from SoA planes or ggml blocks: q8_0 quants in 16-byte
+// chunks at their swizzled A-layout positions, q4_0 blocks (16 bytes of
+// nibbles) packed as [block][row]; then the [row][block] fp16 scales.
+// Rows beyond M and blocks beyond K get zero quants and zero scales.
+template <int FMT>
 __global__ void __launch_bounds__(256) k_tile_tc(const uint8_t* __restrict__ q,
                                                  const unsigned short* __restrict__ d, bool aos,
                                                  int M, int K, int nkt, uint8_t* __restrict__ out) {
+  constexpr int BLOCK = FMT == 8 ? Q8_BLOCK : Q4_BLOCK;  // ggml block bytes
   const int kt = blockIdx.x, rt = blockIdx.y;
-  uint8_t* t = out + ((int64_t)rt * nkt + kt) * TC_TILE;
+  uint8_t* t = out + ((int64_t)rt * nkt + kt) * tc_tile<FMT>();
   const int nb = K / QK;
-  constexpr int CH = TC_KT / 16;  // 16-byte chunks per tile row
+  const int64_t qrow = FMT == 8 ? K : K / 2;  // SoA quant bytes per row
+  constexpr int CH = FMT == 8 ? TC_KT / 16 : TC_BLK;  // 16-byte chunks per tile row
   for (int i = threadIdx.x; i < TC_M * CH; i += blockDim.x) {
-    const int r = i / CH, ch = i % CH;
-    const int row = rt * TC_M + r, k0 = kt * TC_KT + ch * 16;
+    // q8_0: consecutive threads read consecutive chunks of a row; q4_0: the
+    // same block of consecutive rows (consecutive in the tile)
+    const int r = FMT == 8 ? i / CH : i % TC_M, ch = FMT == 8 ? i % CH : i / TC_M;
+    const int row = rt * TC_M + r;
+    // chunk ch: q8_0 elements kt * 256 + 16 ch ...; q4_0 block kt * 8 + ch
+    const int blk = FMT == 8 ? kt * TC_BLK + ch / 2 : kt * TC_BLK + ch;
+    const int off = FMT == 8 ? (ch & 1) * 16 : 0;  // byte offset inside the block's quants
     uint4 v = make_uint4(0u, 0u, 0u, 0u);
-    if (row < M && k0 < K) {  // K % 32 == 0: a chunk is wholly inside K or beyond it
+    if (row < M && blk < nb) {
       if (!aos) {
-        v = *reinterpret_cast<const uint4*>(q + (int64_t)row * K + k0);
+        v = *reinterpret_cast<const uint4*>(q + (int64_t)row * qrow + (int64_t)blk * (FMT == 8 ? 32 : 16) + off);
       } else {
-        const uint8_t* src = q + ((int64_t)row * nb + k0 / QK) * Q8_BLOCK + 2 + (k0 % QK);
+        const uint8_t* src = q + ((int64_t)row * nb + blk) * BLOCK + 2 + off;
         uint32_t w[4];
         for (int j = 0; j < 4; ++j)
           w[j] = (uint32_t)src[4 * j] | ((uint32_t)src[4 * j + 1] << 8) |
@@ -659,11 +783,15 @@ __global__ void __launch_bounds__(256) k_tile_tc(const uint8_t* __restrict__ q,
         v = make_uint4(w[0], w[1], w[2], w[3]);
       }
     }
-    const int box = ch >> 3, c = ch & 7;
-    *reinterpret_cast<uint4*>(t + box * TC_BOX + (r >> 3) * 1024 + (r & 7) * 128 +
-                              ((c ^ (r & 7)) << 4)) = v;
+    if (FMT == 8) {
+      const int box = ch >> 3, c = ch & 7;
+      *reinterpret_cast<uint4*>(t + box * TC_BOX + (r >> 3) * 1024 + (r & 7) * 128 +
+                                ((c ^ (r & 7)) << 4)) = v;
+    } else {
+      *reinterpret_cast<uint4*>(t + (ch * TC_M + r) * 16) = v;
+    }
   }
-  unsigned short* ts = reinterpret_cast<unsigned short*>(t + TC_ABYTES);
+  unsigned short* ts = reinterpret_cast<unsigned short*>(t + tc_qbytes<FMT>());
   for (int i = threadIdx.x; i < TC_M * TC_BLK; i += blockDim.x) {
     const int r = i / TC_BLK, b = i % TC_BLK;
     const int row = rt * TC_M + r, blk = kt * TC_BLK + b;
@@ -672,7 +800,7 @@ __global__ void __launch_bounds__(256) k_tile_tc(const uint8_t* __restrict__ q,
       if (!aos) {
         h = d[(int64_t)row * nb + blk];
       } else {
-        const uint8_t* src = q + ((int64_t)row * nb + blk) * Q8_BLOCK;
+        const uint8_t* src = q + ((int64_t)row * nb + blk) * BLOCK;
         h = (unsigned short)(src[0] | (src[1] << 8));
       }
     }
@@ -701,11 +829,11 @@ int tc_grid(int64_t M, int64_t K, int sms) {
   return (int)std::max<int64_t>(1, std::min<int64_t>(sms, U));
 }
 
-template <int NC>
+template <int FMT, int NC>
 int launch_tc(const void* tiles, int64_t M, int64_t K, const float* x, int64_t ldx, float* y,
               int64_t ldy, int N, void* ws, size_t ws_bytes, const DeviceInfo& dev,
               cudaStream_t st) {
-  using C = TcCfg<NC>;
+  using C = TcFmt<FMT, NC>;
   const int grid = tc_grid(M, K, dev.sms);
   const WsLayout w = ws_layout<NC>(M, K, grid);
   if (ws_bytes < w.bytes)
@@ -713,7 +841,7 @@ int launch_tc(const void* tiles, int64_t M, int64_t K, const float* x, int64_t l
   static bool attr_done[64] = {};
   if (dev.device >= 0 && dev.device < 64 && !attr_done[dev.device]) {
     const cudaError_t e =
-        cudaFuncSetAttribute(k_gemv_tc<NC>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)C::SMEM);
+        cudaFuncSetAttribute(k_gemv_tc<FMT, NC>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)C::SMEM);
     if (e != cudaSuccess)
       return set_error(ERR_CUDA, "k_gemv_tc shared memory: %s", cudaGetErrorString(e));
     attr_done[dev.device] = true;
@@ -745,43 +873,55 @@ int launch_tc(const void* tiles, int64_t M, int64_t K, const float* x, int64_t l
   cudaError_t e = cudaLaunchKernelEx(&cfg, k_xprep_tc<NC>, x, ldx, (int)K, N, chunk, a);
   if (e != cudaSuccess) return set_error(ERR_CUDA, "k_xprep_tc launch: %s", cudaGetErrorString(e));
   cfg.gridDim = dim3(grid);
-  cfg.blockDim = dim3(TC_THREADS);
+  cfg.blockDim = dim3(C::THREADS);
   cfg.dynamicSmemBytes = C::SMEM;
-  e = cudaLaunchKernelEx(&cfg, k_gemv_tc<NC>, a);
+  e = cudaLaunchKernelEx(&cfg, k_gemv_tc<FMT, NC>, a);
   if (e != cudaSuccess) return set_error(ERR_CUDA, "k_gemv_tc launch: %s", cudaGetErrorString(e));
   return check_launch("k_gemv_tc");
 }
 
 }  // namespace
 
-size_t tc_tiles_bytes(int64_t M, int64_t K) {
+size_t tc_tiles_bytes(int fmt, int64_t M, int64_t K) {
   const int64_t nkt = (K + TC_KT - 1) / TC_KT, ntiles = (M + TC_M - 1) / TC_M;
-  return (size_t)(nkt * ntiles) * TC_TILE;
+  return (size_t)(nkt * ntiles) * (fmt == 8 ? tc_tile<8>() : tc_tile<4>());
 }
 
 size_t tc_workspace_bytes(int64_t M, int64_t K, int sms) {
   return ws_layout<16>(M, K, tc_grid(M, K, sms)).bytes;
 }
 
-int tile_weights_tc(bool aos, const void* q, const void* d, int64_t M, int64_t K, void* out,
-                    cudaStream_t st) {
+int tile_weights_tc(int fmt, bool aos, const void* q, const void* d, int64_t M, int64_t K,
+                    void* out, cudaStream_t st) {
   const int nkt = (int)((K + TC_KT - 1) / TC_KT), ntiles = (int)((M + TC_M - 1) / TC_M);
   if (nkt == 0 || ntiles == 0) return OK;
-  k_tile_tc<<<dim3(nkt, ntiles), 256, 0, st>>>(static_cast<const uint8_t*>(q),
-                                                 static_cast<const unsigned short*>(d), aos, (int)M,
-                                                 (int)K, nkt, static_cast<uint8_t*>(out));
+  const uint8_t* qq = static_cast<const uint8_t*>(q);
+  const unsigned short* dd = static_cast<const unsigned short*>(d);
+  uint8_t* o = static_cast<uint8_t*>(out);
+  if (fmt == 8)
+    k_tile_tc<8><<<dim3(nkt, ntiles), 256, 0, st>>>(qq, dd, aos, (int)M, (int)K, nkt, o);
+  else
+    k_tile_tc<4><<<dim3(nkt, ntiles), 256, 0, st>>>(qq, dd, aos, (int)M, (int)K, nkt, o);
   return check_launch("k_tile_tc");
 }
 
-int gemv_tc(const void* tiles, int64_t M, int64_t K, const float* x, int64_t ldx, float* y,
-            int64_t ldy, int N, void* ws, size_t ws_bytes, cudaStream_t st) {
+template <int FMT>
+int gemv_tc_fmt(const void* tiles, int64_t M, int64_t K, const float* x, int64_t ldx, float* y,
+                int64_t ldy, int N, void* ws, size_t ws_bytes, const DeviceInfo& dev,
+                cudaStream_t st) {
+  if (N <= 2) return launch_tc<FMT, 2>(tiles, M, K, x, ldx, y, ldy, N, ws, ws_bytes, dev, st);
+  if (N <= 4) return launch_tc<FMT, 4>(tiles, M, K, x, ldx, y, ldy, N, ws, ws_bytes, dev, st);
+  if (N <= 8) return launch_tc<FMT, 8>(tiles, M, K, x, ldx, y, ldy, N, ws, ws_bytes, dev, st);
+  return launch_tc<FMT, 16>(tiles, M, K, x, ldx, y, ldy, N, ws, ws_bytes, dev, st);
+}
+
+int gemv_tc(int fmt, const void* tiles, int64_t M, int64_t K, const float* x, int64_t ldx,
+            float* y, int64_t ldy, int N, void* ws, size_t ws_bytes, cudaStream_t st) {
   if (M == 0 || N == 0) return OK;
   DeviceInfo dev;
   if (int rc = current_device_info(dev)) return rc;
-  if (N <= 2) return launch_tc<2>(tiles, M, K, x, ldx, y, ldy, N, ws, ws_bytes, dev, st);
-  if (N <= 4) return launch_tc<4>(tiles, M, K, x, ldx, y, ldy, N, ws, ws_bytes, dev, st);
-  if (N <= 8) return launch_tc<8>(tiles, M, K, x, ldx, y, ldy, N, ws, ws_bytes, dev, st);
-  return launch_tc<16>(tiles, M, K, x, ldx, y, ldy, N, ws, ws_bytes, dev, st);
+  if (fmt == 8) return gemv_tc_fmt<8>(tiles, M, K, x, ldx, y, ldy, N, ws, ws_bytes, dev, st);
+  return gemv_tc_fmt<4>(tiles, M, K, x, ldx, y, ldy, N, ws, ws_bytes, dev, st);
 }
 
 int set_tc_spin_limit(long long cycles) {

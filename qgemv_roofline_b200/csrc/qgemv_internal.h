@@ -113,15 +113,15 @@ size_t tiled_bytes(int fmt, int64_t M, int64_t K);
 int tile_weights(int fmt, bool aos, const void* q, const void* d, int64_t M, int64_t K,
                  void* out, cudaStream_t st);
 int gemv_tiled(int fmt, const GemvCall& c, cudaStream_t st);  // c.q = tiles, 1..16 columns
-// q8_0 tc tiles and the tcgen05 batch kernel (gemv_tc.cu): 1..16 columns per
-// call; the workspace bound holds for every column count on a device with
-// `sms` SMs.
-size_t tc_tiles_bytes(int64_t M, int64_t K);
+// tc tiles and the tcgen05 batch kernel (gemv_tc.cu), q8_0 (fmt 8) and q4_0
+// (fmt 4): 1..16 columns per call; the workspace bound holds for every column
+// count and both formats on a device with `sms` SMs.
+size_t tc_tiles_bytes(int fmt, int64_t M, int64_t K);
 size_t tc_workspace_bytes(int64_t M, int64_t K, int sms);
-int tile_weights_tc(bool aos, const void* q, const void* d, int64_t M, int64_t K, void* out,
-                    cudaStream_t st);
-int gemv_tc(const void* tiles, int64_t M, int64_t K, const float* x, int64_t ldx, float* y,
-            int64_t ldy, int N, void* ws, size_t ws_bytes, cudaStream_t st);
+int tile_weights_tc(int fmt, bool aos, const void* q, const void* d, int64_t M, int64_t K,
+                    void* out, cudaStream_t st);
+int gemv_tc(int fmt, const void* tiles, int64_t M, int64_t K, const float* x, int64_t ldx,
+            float* y, int64_t ldy, int N, void* ws, size_t ws_bytes, cudaStream_t st);
 int set_tc_spin_limit(long long cycles);
 int read_tc_error(int clear, cudaStream_t st, int* out);
 // Workspace cached per (device, stream) for callers that pass none; grows on

@@ -185,41 +185,48 @@ def qgemv_tiled(fmt: str, tiled: torch.Tensor, M: int, K: int, x: torch.Tensor,
 
 
 def tile_weights_tc(q: torch.Tensor | None = None, d: torch.Tensor | None = None,
-                    blocks: torch.Tensor | None = None, stream: int | None = None) -> torch.Tensor:
-    """q8_0 tc tiles (uint8, 1-D) of a matrix given as SoA planes (q, d) or
-    ggml blocks [M, K/32, 34]: the layout the tcgen05 batch kernel streams,
+                    blocks: torch.Tensor | None = None, stream: int | None = None,
+                    fmt: str = "q8_0") -> torch.Tensor:
+    """tc tiles (uint8, 1-D) of a ``fmt`` matrix given as SoA planes (q, d) or
+    ggml blocks [M, K/32, 34|18]: the layout the tcgen05 batch kernel streams,
     one bulk copy per 128 rows x 256 columns.  Made once per matrix."""
+    _check_fmt(fmt)
+    fid = _lib.FORMAT_CODE[fmt]
     if blocks is not None:
         if not blocks.is_cuda or blocks.dim() != 3 or not blocks.is_contiguous() \
-                or blocks.shape[2] != BLOCK_BYTES["q8_0"]:
-            raise ValueError("blocks must be a contiguous CUDA tensor [M, K/32, 34]")
+                or blocks.shape[2] != BLOCK_BYTES[fmt]:
+            raise ValueError(f"blocks must be a contiguous CUDA tensor [M, K/32, {BLOCK_BYTES[fmt]}]")
         M, K, src, dsrc, layout, dev = blocks.shape[0], blocks.shape[1] * QK, blocks, None, 1, blocks.device
     else:
         if q is None or d is None or not q.is_cuda or not q.is_contiguous() or not d.is_contiguous():
             raise ValueError("q and d must be contiguous CUDA tensors")
-        M, K, src, dsrc, layout, dev = q.shape[0], q.shape[1], q, d, 0, q.device
-    out = torch.empty(_lib.lib().qgemv_q8_0_tc_bytes(M, K), dtype=torch.uint8, device=dev)
+        M = q.shape[0]
+        K = q.shape[1] if fmt == "q8_0" else q.shape[1] * 2
+        src, dsrc, layout, dev = q, d, 0, q.device
+    out = torch.empty(_lib.lib().qgemv_tc_bytes(fid, M, K), dtype=torch.uint8, device=dev)
     st = torch.cuda.current_stream(dev).cuda_stream if stream is None else stream
-    _lib.call("qgemv_q8_0_tc_tile", layout, src.data_ptr(),
+    _lib.call("qgemv_tc_tile", fid, layout, src.data_ptr(),
               None if dsrc is None else dsrc.data_ptr(), M, K, out.data_ptr(), st)
     return out
 
 
 def qgemv_tc(tiles: torch.Tensor, M: int, K: int, x: torch.Tensor, y: torch.Tensor | None = None,
-             stream: int | None = None) -> torch.Tensor:
-    """q8_0 GEMV over tc tiles (tile_weights_tc) on the tcgen05 tensor cores;
+             stream: int | None = None, fmt: str = "q8_0") -> torch.Tensor:
+    """GEMV over tc tiles (tile_weights_tc) on the tcgen05 tensor cores;
     x [K] or [N, K] for any N."""
+    _check_fmt(fmt)
+    fid = _lib.FORMAT_CODE[fmt]
     if not tiles.is_cuda or tiles.dtype != torch.uint8:
         raise ValueError("tiles must be a uint8 CUDA tensor")
-    if tiles.numel() != _lib.lib().qgemv_q8_0_tc_bytes(M, K):
-        raise ValueError(f"tiles hold {tiles.numel()} bytes, not those of a [{M}, {K}] q8_0 matrix")
+    if tiles.numel() != _lib.lib().qgemv_tc_bytes(fid, M, K):
+        raise ValueError(f"tiles hold {tiles.numel()} bytes, not those of a [{M}, {K}] {fmt} matrix")
     X, Y, y, N, ldx, ldy = _xy(x, M, K, y, tiles.device)
     st = torch.cuda.current_stream(tiles.device).cuda_stream if stream is None else stream
     with torch.cuda.device(tiles.device):
-        nbytes = _lib.lib().qgemv_q8_0_tc_workspace_bytes(M, K)
+        nbytes = _lib.lib().qgemv_tc_workspace_bytes(M, K)
     ws = _workspace(tiles.device, nbytes, stream)
-    _lib.call("qgemv_q8_0_tc", tiles.data_ptr(), M, K, X.data_ptr(), Y.data_ptr(), N, ldx, ldy,
-              ws.data_ptr(), ws.numel(), st)
+    _lib.call("qgemv_tc_gemv", fid, tiles.data_ptr(), M, K, X.data_ptr(), Y.data_ptr(), N, ldx,
+              ldy, ws.data_ptr(), ws.numel(), st)
     return y
 
 
@@ -272,15 +279,13 @@ class QuantizedMatrix:
         return QuantizedMatrix(self.fmt, self.M, self.K, "tiled", tiled=t)
 
     def to_tc(self) -> "QuantizedMatrix":
-        """The same q8_0 matrix as tc tiles (the tcgen05 batch kernel)."""
-        if self.fmt != "q8_0":
-            raise ValueError("tc tiles hold q8_0 weights only")
+        """The same matrix as tc tiles (the tcgen05 batch kernel)."""
         if self.layout == "tc":
             return self
         if self.layout == "soa":
-            t = tile_weights_tc(q=self.q, d=self.d)
+            t = tile_weights_tc(q=self.q, d=self.d, fmt=self.fmt)
         elif self.layout == "aos":
-            t = tile_weights_tc(blocks=self.blocks)
+            t = tile_weights_tc(blocks=self.blocks, fmt=self.fmt)
         else:
             raise ValueError("make tc tiles from the SoA or ggml-block matrix")
         return QuantizedMatrix(self.fmt, self.M, self.K, "tc", tiled=t)
@@ -298,7 +303,7 @@ class QuantizedMatrix:
         if self.layout == "tc":
             if activations != "exact":
                 raise ValueError("tc tiles run the exact path only")
-            return qgemv_tc(self.tiled, self.M, self.K, x, y, stream)
+            return qgemv_tc(self.tiled, self.M, self.K, x, y, stream, fmt=self.fmt)
         return qgemv_aos(self.fmt, self.blocks, x, y, stream, activations)
 
     __call__ = matvec
