@@ -274,10 +274,10 @@ def _gpu_uuid(dev):
 
 
 def batch_records(args, rank, world, dev, steps, warmup):
-    """W [28672, 8192] (rows sharded) with X [N, 8192], N in 1..16: q8_0 from
-    tc tiles (the tcgen05 kernel), both formats from batch tiles and from SoA
-    planes; weights rotated over >= 4x L2.  Returns a list of records (us per
-    call, aggregate GB/s)."""
+    """W [28672, 8192] (rows sharded) with X [N, 8192], N in 1..16, both formats
+    from tc tiles (the tcgen05 kernel), from batch tiles and from SoA planes;
+    weights rotated over >= 4x L2.  Returns a list of records (us per call,
+    aggregate GB/s)."""
     import torch
     import torch.distributed as dist
 
@@ -297,10 +297,10 @@ def batch_records(args, rank, world, dev, steps, warmup):
         copies = max(2, math.ceil(4 * L2_BYTES / wbytes(fmt, rows, K)))
         soa = [(q, d)] + [(q.clone(), d.clone()) for _ in range(copies - 1)]
         tiles = [qg.tile_weights(fmt, q=a, d=b) for a, b in soa]
-        # q8_0 also as tc tiles (the tcgen05 kernel)
-        tcs = [qg.tile_weights_tc(q=a, d=b) for a, b in soa] if fmt == "q8_0" else []
-        nb_tc = max(lib.qgemv_q8_0_tc_workspace_bytes(rows, K), 16) if tcs else 0
-        ws_tc = torch.empty(nb_tc, dtype=torch.uint8, device=dev) if tcs else None
+        # also as tc tiles (the tcgen05 kernel)
+        tcs = [qg.tile_weights_tc(q=a, d=b, fmt=fmt) for a, b in soa]
+        nb_tc = max(lib.qgemv_tc_workspace_bytes(rows, K), 16)
+        ws_tc = torch.empty(nb_tc, dtype=torch.uint8, device=dev)
         fid = 8 if fmt == "q8_0" else 4
         for N in (1, 2, 4, 8, 16):
             X = torch.randn(N, K, device=dev)
@@ -325,11 +325,10 @@ def batch_records(args, rank, world, dev, steps, warmup):
             def tc_call():
                 t = tcs[it[0] % copies]
                 it[0] += 1
-                _lib.call("qgemv_q8_0_tc", t.data_ptr(), rows, K, X.data_ptr(), Y.data_ptr(), N,
-                          K, rows, ws_tc.data_ptr(), nb_tc, sp)
+                _lib.call("qgemv_tc_gemv", fid, t.data_ptr(), rows, K, X.data_ptr(), Y.data_ptr(),
+                          N, K, rows, ws_tc.data_ptr(), nb_tc, sp)
 
-            calls = (("tc", tc_call),) if tcs else ()
-            for layout, fn in calls + (("tiled", tiled_call), ("soa", soa_call)):
+            for layout, fn in (("tc", tc_call), ("tiled", tiled_call), ("soa", soa_call)):
                 ms = _timed(torch, dist, dev, world, fn, warmup, steps)
                 per = ms / steps
                 b = alg_bytes(fmt, rows, K, N)

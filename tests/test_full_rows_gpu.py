@@ -118,8 +118,8 @@ def test_xl_98304x4096_every_row(fmt):
 def test_small_batch_28672x8192_every_row(fmt):
     """W [28672, 8192] with 16 columns: the batch-tile kernel and the SoA-plane
     kernel, every row and column; then 5 columns (a partial column group) on
-    the batch tiles; for q8_0 also the tcgen05 kernel on tc tiles at 16, 8, 4,
-    2 and 1 columns (the paths the small-batch benchmark reports)."""
+    the batch tiles; and the tcgen05 kernel on tc tiles at 16, 8, 4, 2 and 1
+    columns (the paths the small-batch benchmark reports)."""
     M, K, N = 28672, 8192, 16
     g = torch.Generator(device=DEV).manual_seed(4 + (fmt == "q4_0"))
     W = torch.randn(M, K, generator=g, device=DEV) * 0.02
@@ -138,15 +138,14 @@ def test_small_batch_28672x8192_every_row(fmt):
     assert torch.equal(Y2, 2.0 * Yt)  # power-of-two scaling is exact end to end
     Y5 = qg.qgemv_tiled(fmt, tiles, M, K, X[3:8])
     assert_all_rows(Y5.cpu().numpy(), y_ref[3:8], wn, Xh[3:8], "batch tiles, 5 columns")
-    if fmt == "q8_0":
-        # the tcgen05 kernel on tc tiles: 16, 8, 4, 2 and 1 columns (every
-        # configuration of its TMEM ring), every row
-        del tiles
-        tc = qg.tile_weights_tc(q=q, d=d)
-        for n0, n1 in ((0, 16), (3, 11), (5, 9), (8, 10), (15, 16)):
-            Yc = qg.qgemv_tc(tc, M, K, X[n0:n1] if n1 - n0 > 1 else X[n0])
-            assert_all_rows(Yc.cpu().numpy(), y_ref[n0:n1], wn, Xh[n0:n1],
-                            f"tc tiles, {n1 - n0} columns")
+    # the tcgen05 kernel on tc tiles: 16, 8, 4, 2 and 1 columns (every
+    # configuration of its TMEM rings), every row
+    del tiles
+    tc = qg.tile_weights_tc(q=q, d=d, fmt=fmt)
+    for n0, n1 in ((0, 16), (3, 11), (5, 9), (8, 10), (15, 16)):
+        Yc = qg.qgemv_tc(tc, M, K, X[n0:n1] if n1 - n0 > 1 else X[n0], fmt=fmt)
+        assert_all_rows(Yc.cpu().numpy(), y_ref[n0:n1], wn, Xh[n0:n1],
+                        f"tc tiles, {n1 - n0} columns")
     qg._lib.call("qgemv_check_device_error", 0, None)
 
 
