@@ -39,23 +39,23 @@
 // last part (a counter per row tile): it adds the CTAs' partial sums in CTA
 // order, so results do not depend on timing.
 //
-// Per CTA (11 warps; 19 for q4_0): warp 0 streams each unit with bulk copies
-// into two shared-memory rings: the quants and the x digits (what the MMAs
-// read) into a ring of 3-6 weight stages, freed by the MMAs' commit (and, for
-// q4_0, by the converter warps), and the tile's fp16 scales with the x block
-// exponents into an 8-slot scale ring, freed by the epilogue; so the weight
-// stream never waits for the epilogue's arithmetic.  One thread each of warps
-// 1 and 2 (alternate units: a tcgen05.mma costs ~80-90 cycles to issue)
-// issues the 8 MMAs of a unit, 4 (or, at 16 columns, 2) blocks into each slot
-// of a TMEM ring (8 x 4 x 8, 8 x 4 x 16, 4 x 4 x 32 or 5 x 2 x 48 columns at
-// 2, 4, 8, 16 columns of x), and commits each slot to an mbarrier; warps
-// 3..10 (two groups of four, one warp per TMEM lane quarter, group g taking
-// column half g) read their part of a whole slot back with one wait
-// (tcgen05.ld), release it and accumulate: the TMEM read latency is paid once
-// per slot, not once per block.  No barrier joins the epilogue warps: each
-// owns its rows and columns, and at the end of a row tile stores y (or, for a
-// row tile shared with other CTAs, its part).  For q4_0, warps 11..18 widen
-// each unit's nibbles into a 3-slot A ring first.
+// Per CTA (11 warps; 19 for q4_0): warp 0
+// streams each unit with bulk copies into two shared-memory rings: the quants
+// and the x digits (what the MMAs read) into a ring of 3-6 weight stages,
+// freed by the MMAs' commits (and, for q4_0, by the converter warps), and the
+// tile's fp16 scales with the x block exponents into an 8-slot scale ring,
+// freed by the epilogue; so the weight stream never waits for the epilogue's
+// arithmetic.  One thread each of warps 1 and 2 (a tcgen05.mma costs ~80-90
+// cycles to issue) issues half of every unit's blocks, 4 (or, at 16 columns,
+// 2) blocks into each slot of its own TMEM ring, and commits each slot to an
+// mbarrier; the epilogue warps 3..10 (2 groups of four, one warp per TMEM
+// lane quarter, group g taking the g-th half of the columns) read
+// their part of a whole slot back with one wait (tcgen05.ld), release it and
+// accumulate: the TMEM read latency is paid once per slot, not once per
+// block.  No barrier joins the epilogue warps: each owns its rows and
+// columns, and at the end of a row tile stores y (or, for a row tile shared
+// with other CTAs, its part).  For q4_0, the 8 warps after the epilogue's
+// widen each unit's nibbles into a 3-slot A ring first.
 // Every wait is bounded (the library's wait limit): on timeout the error word
 // records QGEMV_ERR_TIMEOUT, the producer stops and waits for its copies, the
 // MMA threads stop issuing, the epilogue runs out its loop without waiting,
@@ -79,8 +79,7 @@ constexpr int TC_ABYTES = TC_M * TC_KT;         // quants of a tile
 constexpr int TC_BOX = TC_M * 128;              // one 128-byte-wide box of quants
 constexpr int TC_DBYTES = TC_M * TC_BLK * 2;    // fp16 scales of a tile
 constexpr int TC_TMEM_COLS = 512;
-constexpr int TC_GROUPS = 2;                    // epilogue warp groups (one per column half)
-constexpr int TC_EPI = 4 * TC_GROUPS;           // epilogue warps
+constexpr int TC_EPI_MAX = 16;                  // epilogue warps, at most (4 column groups)
 constexpr int TC_MMAW = 2;                      // MMA-issuing warps (each its own TMEM half)
 constexpr int TC_W0E = 1 + TC_MMAW;             // first epilogue warp
 constexpr int TC_PMAX = 64;                     // x prep chunks per column, at most
@@ -126,20 +125,25 @@ struct TcFmt : TcCfg<NC> {
   static constexpr int QB = tc_qbytes<FMT>();         // quant bytes per tile
   static constexpr int TILE = tc_tile<FMT>();         // 34816 (q8_0), 18432 (q4_0)
   static constexpr int CONV = FMT == 8 ? 0 : 8;       // converter warps
+  // epilogue: G column groups of 4 warps (one per TMEM lane quarter); 4 groups
+  // at 8 and 16 columns measured no faster (28672x8192 q8_0: 56.1 / 75.6 us
+  // against 53.9 / 75.6 us with 2), so 2 everywhere
+  static constexpr int G = 2;
+  static constexpr int EPI = 4 * G;
   static constexpr int SA = FMT == 8 ? 0 : 3;         // A ring slots (q4_0)
-  static constexpr int THREADS = 32 * (TC_W0E + TC_EPI + CONV);
+  static constexpr int THREADS = 32 * (TC_W0E + EPI + CONV);
   // weight stage: quants + x digits (what the MMAs, or the converters, read)
   static constexpr int WSTAGE = QB + TcCfg<NC>::XB;   // a multiple of 1024
   // left for weight stages: the budget minus alignment slack, the scale and A
   // rings and the epilogue warps' static scratch (8 x 8 NC floats)
   static constexpr int FREE =
-      TC_SMEM_MAX - 1024 - TC_SS * TcCfg<NC>::SSLOT - SA * TC_ABYTES - TC_EPI * 8 * NC * 4;
+      TC_SMEM_MAX - 1024 - TC_SS * TcCfg<NC>::SSLOT - SA * TC_ABYTES - 8 * NC * 4 * 4;
   static constexpr int SW = FREE / WSTAGE > 8 ? 8 : FREE / WSTAGE;
   static constexpr size_t SMEM =
       (size_t)SW * WSTAGE + (size_t)SA * TC_ABYTES + (size_t)TC_SS * TcCfg<NC>::SSLOT + 1024;
 };
-static_assert(TcFmt<8, 16>::SMEM + TC_EPI * 8 * 16 * 4 <= TC_SMEM_MAX &&
-                  TcFmt<4, 16>::SMEM + TC_EPI * 8 * 16 * 4 <= TC_SMEM_MAX &&
+static_assert(TcFmt<8, 16>::SMEM + 8 * 16 * 4 * 4 <= TC_SMEM_MAX &&
+                  TcFmt<4, 16>::SMEM + 8 * 16 * 4 * 4 <= TC_SMEM_MAX &&
                   TcFmt<8, 2>::SMEM <= TC_SMEM_MAX && TcFmt<4, 2>::SMEM <= TC_SMEM_MAX,
               "ring too large");
 static_assert(TcFmt<8, 16>::SW >= 4 && TcFmt<8, 8>::SW >= 5 && TcFmt<4, 16>::SW >= 3 &&
@@ -318,7 +322,7 @@ __global__ void __launch_bounds__(TcFmt<FMT, NC>::THREADS, 1)
   __shared__ __align__(8) unsigned long long mma_done;
   __shared__ uint32_t tmem_base;
   __shared__ int abort_flag;
-  __shared__ float xscr[TC_EPI][8 * NC];  // per epilogue warp: block scales of a unit
+  __shared__ float xscr[C::EPI][8 * NC / C::G];  // per epilogue warp: block scales of a unit
 
   // 1024-byte-aligned weight ring (the swizzle works on address bits), the A
   // ring (q4_0), then the scale ring
@@ -343,12 +347,12 @@ __global__ void __launch_bounds__(TcFmt<FMT, NC>::THREADS, 1)
     }
     for (int s = 0; s < TC_SS; ++s) {
       mbar_init(saddr(&sfull[s]), 1);
-      mbar_init(saddr(&sempty[s]), TC_EPI);  // every epilogue warp
+      mbar_init(saddr(&sempty[s]), C::EPI);  // every epilogue warp
     }
     for (int w = 0; w < TC_MMAW; ++w)
       for (int s = 0; s < C::SLW; ++s) {
         mbar_init(saddr(&tfull[w][s]), 1);
-        mbar_init(saddr(&tempty[w][s]), TC_EPI);  // every epilogue warp reads every slot
+        mbar_init(saddr(&tempty[w][s]), C::EPI);  // every epilogue warp reads every slot
       }
     mbar_init(saddr(&mma_done), TC_MMAW);  // one commit per MMA warp
     abort_flag = 0;
@@ -470,13 +474,13 @@ __global__ void __launch_bounds__(TcFmt<FMT, NC>::THREADS, 1)
       tc_commit(saddr(&mma_done));
       mbar_wait_drain(saddr(&mma_done), 0u);
     }
-  } else if (FMT == 4 && warp >= TC_W0E + TC_EPI) {
+  } else if (FMT == 4 && warp >= TC_W0E + C::EPI) {
     // ---------------------------------------------------------- converters
     // q4_0: thread (r, h) (one per row of the tile and half of its blocks)
     // widens blocks 4h .. 4h + 3 of row r (16 bytes of nibbles each: weight j
     // low nibble, j + 16 high) into int8 n - 8 at the A layout's swizzled
     // positions, unit after unit into A slot i % SA
-    const int ct = threadIdx.x - 32 * (TC_W0E + TC_EPI);  // 0..255
+    const int ct = threadIdx.x - 32 * (TC_W0E + C::EPI);  // 0..255
     const int r = ct & (TC_M - 1), h = ct >> 7;
     bool ok = true;
     for (int i = 0; i < nunits && ok; ++i) {
@@ -515,7 +519,7 @@ __global__ void __launch_bounds__(TcFmt<FMT, NC>::THREADS, 1)
   } else {
     // ------------------------------------------------------------ epilogue
     asm volatile("griddepcontrol.wait;" ::: "memory");  // header and counters
-    constexpr int NCH = NC / 2;    // columns per warp
+    constexpr int NCH = NC / C::G;  // columns per warp
     const int e = warp - TC_W0E;
     const int quarter = warp & 3;  // TMEM lanes 32 * quarter ... (this warp's rows)
     const int g = e >> 2;          // this warp's columns: g * NCH ... (g + 1) * NCH - 1
@@ -635,7 +639,7 @@ __global__ void __launch_bounds__(TcFmt<FMT, NC>::THREADS, 1)
       __syncwarp();
       const int c0 = cta_of(t0, U, gridDim.x), c1 = cta_of(t0 + p.nkt - 1, U, gridDim.x);
       unsigned last = 0;
-      if (lane == 0) last = atomicAdd(&cnt[rt * TC_EPI + e], 1u) == (unsigned)(c1 - c0);
+      if (lane == 0) last = atomicAdd(&cnt[rt * TC_EPI_MAX + e], 1u) == (unsigned)(c1 - c0);
       if (__shfl_sync(0xffffffffu, last, 0)) {
         __threadfence();
         float tot[NCH];
@@ -700,7 +704,7 @@ __global__ void __launch_bounds__(XT_THREADS) k_xprep_tc(const float* __restrict
   const bool live = col < N;
   if (blockIdx.x == 0 && col == 0) {
     unsigned* cnt = reinterpret_cast<unsigned*>(p.ws + p.cnt_off);
-    for (int t = threadIdx.x; t < p.ntiles * TC_EPI; t += XT_THREADS) cnt[t] = 0u;
+    for (int t = threadIdx.x; t < p.ntiles * TC_EPI_MAX; t += XT_THREADS) cnt[t] = 0u;
   }
   const int nblk = p.nkt * TC_BLK;
   const int b0 = blockIdx.x * chunk, b1 = min(nblk, b0 + chunk);
@@ -818,7 +822,7 @@ WsLayout ws_layout(int64_t M, int64_t K, int grid) {
   const int64_t nkt = (K + TC_KT - 1) / TC_KT, ntiles = (M + TC_M - 1) / TC_M;
   WsLayout w;
   w.cnt_off = TC_HDR;
-  w.part_off = w.cnt_off + (int)((ntiles * TC_EPI * 4 + 15) / 16 * 16);
+  w.part_off = w.cnt_off + (int)((ntiles * TC_EPI_MAX * 4 + 15) / 16 * 16);
   w.xt_off = w.part_off + grid * 2 * NC * TC_M * 4;
   w.bytes = (size_t)w.xt_off + (size_t)nkt * TcCfg<NC>::XT;
   return w;
