@@ -275,7 +275,9 @@ def _gpu_uuid(dev):
 
 def batch_records(args, rank, world, dev, steps, warmup):
     """W [28672, 8192] (rows sharded) with X [N, 8192], N in 1..16, both formats
-    from tc tiles (the tcgen05 kernel), from batch tiles and from SoA planes;
+    from tc tiles (the tcgen05 kernel), from batch tiles, from SoA planes (the
+    tcgen05 kernel through 2-D tensor copies) and from SoA planes through the
+    static-workspace entry (the mma.sync kernel);
     weights rotated over >= 4x L2.  Returns a list of records (us per call,
     aggregate GB/s)."""
     import torch
@@ -307,14 +309,24 @@ def batch_records(args, rank, world, dev, steps, warmup):
             Y = torch.empty(N, rows, device=dev)
             nb = max(lib.qgemv_tiled_workspace_bytes(K, N), 16)
             ws = torch.empty(nb, dtype=torch.uint8, device=dev)
+            nb_soa = max(lib.qgemv_soa_workspace_bytes(fid, rows, K, N), 16)
+            ws_soa = torch.empty(nb_soa, dtype=torch.uint8, device=dev)
             sp = torch.cuda.current_stream().cuda_stream
             it = [0]
 
             def soa_call():
+                # 2..16 columns: the tcgen05 kernel straight from the planes
                 a, b = soa[it[0] % copies]
                 it[0] += 1
                 _lib.call("qgemv_soa_ws", fid, a.data_ptr(), b.data_ptr(), X.data_ptr(),
-                          Y.data_ptr(), rows, K, N, K, rows, ws.data_ptr(), nb, sp)
+                          Y.data_ptr(), rows, K, N, K, rows, ws_soa.data_ptr(), nb_soa, sp)
+
+            def soa_static_call():
+                # the fixed in-library workspace: the mma.sync kernel on the planes
+                a, b = soa[it[0] % copies]
+                it[0] += 1
+                _lib.call("qgemv_soa_static_ws", fid, a.data_ptr(), b.data_ptr(), X.data_ptr(),
+                          Y.data_ptr(), rows, K, N, K, rows, sp)
 
             def tiled_call():
                 t = tiles[it[0] % copies]
@@ -328,7 +340,8 @@ def batch_records(args, rank, world, dev, steps, warmup):
                 _lib.call("qgemv_tc_gemv", fid, t.data_ptr(), rows, K, X.data_ptr(), Y.data_ptr(),
                           N, K, rows, ws_tc.data_ptr(), nb_tc, sp)
 
-            for layout, fn in (("tc", tc_call), ("tiled", tiled_call), ("soa", soa_call)):
+            for layout, fn in (("tc", tc_call), ("tiled", tiled_call), ("soa", soa_call),
+                               ("soa_static", soa_static_call)):
                 ms = _timed(torch, dist, dev, world, fn, warmup, steps)
                 per = ms / steps
                 b = alg_bytes(fmt, rows, K, N)

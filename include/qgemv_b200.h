@@ -146,7 +146,10 @@ QGEMV_API int qgemv_soa_q8_1(int format, const void* q, const void* d, const flo
 QGEMV_API int qgemv_aos_q8_1(int format, const void* blocks, const float* x, float* y,
                              int64_t M, int64_t K, void* stream);
 
-/* Workspace bytes of a batched SoA call (0 when the call needs none). */
+/* Workspace bytes of a batched SoA call on the current device (0 when the
+ * call needs none).  With 2..16 columns and K % 256 == 0 the call runs the
+ * tcgen05 batch kernel, whose workspace grows with M (per-row-tile counters)
+ * and the SM count; a smaller workspace is refused. */
 QGEMV_API size_t qgemv_soa_workspace_bytes(int format, int64_t M, int64_t K, int32_t ncols);
 
 /* qgemv_q8_0_soa / qgemv_q4_0_soa (format QGEMV_Q8_0 or QGEMV_Q4_0) with a

@@ -140,9 +140,21 @@ int check_mk(int64_t M, int64_t K) {
   return OK;
 }
 
+// Workspace of a batched SoA call: the tcgen05 kernel's (when it may run) or
+// the mma.sync kernel's, whichever is larger (0 when neither runs).
+size_t soa_batch_workspace(const GemvCall& probe, bool allow_tc) {
+  if (!mma_eligible(probe)) return 0;
+  size_t need = mma_workspace_bytes(probe.K, probe.N);
+  DeviceInfo dev;
+  if (allow_tc && current_device_info(dev) == OK)
+    need = std::max(need, tc_soa_workspace_bytes(probe.M, probe.K, probe.N, dev.sms));
+  return need;
+}
+
 int gemv_entry(int fmt, bool aos, const void* q, const void* d, const float* x, float* y,
                int64_t M, int64_t K, int32_t ncols, int64_t ldx, int64_t ldy, void* stream,
-               void* ws = nullptr, size_t ws_bytes = 0, bool caller_ws = false) {
+               void* ws = nullptr, size_t ws_bytes = 0, bool caller_ws = false,
+               bool allow_tc = true) {
   if (int rc = check_mk(M, K)) return rc;
   if (ncols < 0) return set_error(ERR_SHAPE, "ncols=%d is negative", ncols);
   if (M == 0 || ncols == 0) return OK;
@@ -174,13 +186,14 @@ int gemv_entry(int fmt, bool aos, const void* q, const void* d, const float* x, 
   c.N = ncols;
   c.ldx = ldx;
   c.ldy = ldy;
+  c.no_tc = !allow_tc;
   if (!aos) {
-    // the tensor-core batch kernel needs a workspace: the caller's, or one
+    // the tensor-core batch kernels need a workspace: the caller's, or one
     // cached for this stream
     GemvCall probe = c;
     probe.N = std::min(ncols, 16);
     if (probe.N >= 2 && mma_eligible(probe)) {
-      const size_t need = mma_workspace_bytes(K, probe.N);
+      const size_t need = soa_batch_workspace(probe, allow_tc);
       if (caller_ws) {
         if (!ws || ws_bytes < need)
           return set_error(ERR_ARG, "this call needs a workspace of %zu bytes, got %zu", need,
@@ -383,7 +396,7 @@ QGEMV_API size_t qgemv_soa_workspace_bytes(int format, int64_t M, int64_t K, int
   // alignment is checked per call; assume aligned planes here
   probe.q = reinterpret_cast<const void*>((uintptr_t)256);
   probe.d = probe.q;
-  return mma_eligible(probe) ? mma_workspace_bytes(K, probe.N) : 0;
+  return soa_batch_workspace(probe, true);
 }
 
 QGEMV_API int qgemv_soa_ws(int format, const void* q, const void* d, const float* x, float* y,
@@ -580,7 +593,8 @@ QGEMV_API int qgemv_soa_static_ws(int format, const void* q, const void* d, cons
                        need, kStaticWsBytes);
     if (int rc = static_workspace(&ws, &ws_bytes)) return rc;
   }
-  return gemv_entry(format, false, q, d, x, y, M, K, ncols, ldx, ldy, stream, ws, ws_bytes, true);
+  return gemv_entry(format, false, q, d, x, y, M, K, ncols, ldx, ldy, stream, ws, ws_bytes, true,
+                    /*allow_tc=*/false);
 }
 
 QGEMV_API size_t qgemv_tiled_bytes(int format, int64_t M, int64_t K) {

@@ -1239,6 +1239,23 @@ int check_ws(const GemvCall& c) {
 
 }  // namespace
 
+int encode_tensor_2d(CUtensorMap* map, bool u16, const void* base, uint64_t inner, uint64_t outer,
+                     uint64_t row_bytes, uint32_t box_inner, uint32_t box_outer, bool swizzle128) {
+  EncodeTiledFn enc;
+  if (int rc = get_encode(&enc)) return rc;
+  const cuuint64_t dim[2] = {(cuuint64_t)inner, (cuuint64_t)outer};
+  const cuuint64_t stride[1] = {(cuuint64_t)row_bytes};
+  const cuuint32_t box[2] = {box_inner, box_outer};
+  const cuuint32_t one[2] = {1, 1};
+  const CUresult r =
+      enc(map, u16 ? CU_TENSOR_MAP_DATA_TYPE_UINT16 : CU_TENSOR_MAP_DATA_TYPE_UINT8, 2,
+          const_cast<void*>(base), dim, stride, box, one, CU_TENSOR_MAP_INTERLEAVE_NONE,
+          swizzle128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
+          CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return set_error(ERR_CUDA, "cuTensorMapEncodeTiled: error %d", (int)r);
+  return OK;
+}
+
 size_t mma_workspace_bytes(int64_t K, int N) {
   const int64_t nkt = (K + KC - 1) / KC;
   const int cols = std::max(1, std::min(N, MAXC));

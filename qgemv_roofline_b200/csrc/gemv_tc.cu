@@ -64,6 +64,7 @@
 #include "qgemv_internal.h"
 
 #include <algorithm>
+#include <cstring>
 
 namespace qg {
 
@@ -131,6 +132,7 @@ struct TcFmt : TcCfg<NC> {
   static constexpr int G = 2;
   static constexpr int EPI = 4 * G;
   static constexpr int SA = FMT == 8 ? 0 : 3;         // A ring slots (q4_0)
+  static constexpr int SAD = SA > 0 ? SA : 1;         // SA as a divisor (q8_0 never divides)
   static constexpr int THREADS = 32 * (TC_W0E + EPI + CONV);
   // weight stage: quants + x digits (what the MMAs, or the converters, read)
   static constexpr int WSTAGE = QB + TcCfg<NC>::XB;   // a multiple of 1024
@@ -226,6 +228,17 @@ __device__ __forceinline__ uint64_t sw128_desc(uint32_t addr) {
          ((uint64_t)1u << 46) | ((uint64_t)2u << 61);
 }
 
+// 2-D tiled tensor copy global -> shared (no multicast); c0 is the inner
+// coordinate in elements (its byte offset a multiple of 16), c1 the row.
+__device__ __forceinline__ void tensor_g2s(uint32_t dst, const CUtensorMap* map, int c0, int c1,
+                                           uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3}], [%4];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(bar)
+      : "memory");
+}
+
 __device__ __forceinline__ void tc_fence_before() {
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
 }
@@ -268,7 +281,13 @@ __device__ __forceinline__ void tmem_ld(uint32_t ta, uint32_t (&v)[NC]) {
 }
 
 struct TcArgs {
-  const uint8_t* tiles;  // tc tiles [row tile][K tile]
+  // SoA planes (soa != 0): quants [M][K or K/2] bytes in boxes of 128 bytes x
+  // 128 rows, 128-byte swizzle (exactly the MMA's A layout for q8_0); scales
+  // [M][K/32] fp16 in boxes of 8 x 128 rows ([row][block], as in a tc tile)
+  alignas(64) CUtensorMap qmap;
+  alignas(64) CUtensorMap dmap;
+  int soa;
+  const uint8_t* tiles;  // tc tiles [row tile][K tile] (soa == 0)
   uint8_t* ws;           // header, counters, partial sums, x tiles
   float* y;
   int64_t ldy;
@@ -378,12 +397,30 @@ __global__ void __launch_bounds__(TcFmt<FMT, NC>::THREADS, 1)
       const uint8_t* xt = p.ws + p.xt_off;
       // weights do not depend on the previous kernel: prefetch them first
       const int pre = min(SW, nunits);
+      // unit u's quants and fp16 scales: one tc tile (two bulk copies) or,
+      // from SoA planes, 2-D tensor copies of 128 rows (q8_0: two 128-byte
+      // boxes; q4_0: one) and one scale box; rows past M read as zeros
+      auto load_w = [&](int64_t u, uint32_t wdst, uint32_t sdst, uint32_t fb, uint32_t sb) {
+        if (p.soa) {
+          const int rt = (int)(u / p.nkt), kt = (int)(u % p.nkt);
+          if (FMT == 8) {
+            tensor_g2s(wdst, &p.qmap, kt * TC_KT, rt * TC_M, fb);
+            tensor_g2s(wdst + TC_BOX, &p.qmap, kt * TC_KT + 128, rt * TC_M, fb);
+          } else {
+            tensor_g2s(wdst, &p.qmap, kt * (TC_KT / 2), rt * TC_M, fb);
+          }
+          tensor_g2s(sdst, &p.dmap, kt * TC_BLK, rt * TC_M, sb);
+        } else {
+          const uint8_t* t = p.tiles + u * C::TILE;
+          bulk_g2s(wdst, t, C::QB, fb);
+          bulk_g2s(sdst, t + C::QB, TC_DBYTES, sb);
+        }
+      };
       for (int i = 0; i < pre; ++i) {
-        const uint8_t* t = p.tiles + (u0 + i) * C::TILE;
         mbar_expect_tx(saddr(&full[i]), (uint32_t)(C::QB + C::XB));
         mbar_expect_tx(saddr(&sfull[i]), (uint32_t)(TC_DBYTES + C::XSB));
-        bulk_g2s(ring_s + (uint32_t)(i * C::WSTAGE), t, C::QB, saddr(&full[i]));
-        bulk_g2s(sring_s + (uint32_t)(i * C::SSLOT), t + C::QB, TC_DBYTES, saddr(&sfull[i]));
+        load_w(u0 + i, ring_s + (uint32_t)(i * C::WSTAGE), sring_s + (uint32_t)(i * C::SSLOT),
+               saddr(&full[i]), saddr(&sfull[i]));
       }
       asm volatile("griddepcontrol.wait;" ::: "memory");  // x tiles are written by the prep kernel
       for (int i = 0; i < pre; ++i) {
@@ -399,13 +436,12 @@ __global__ void __launch_bounds__(TcFmt<FMT, NC>::THREADS, 1)
             !mbar_wait(saddr(&sempty[j]), (uint32_t)(((i / TC_SS) - 1) & 1), &abort_flag))
           break;
         const int64_t u = u0 + i;
-        const uint8_t* t = p.tiles + u * C::TILE;
         const uint8_t* x = xt + (int64_t)(u % p.nkt) * C::XT;
         mbar_expect_tx(saddr(&full[s]), (uint32_t)(C::QB + C::XB));
         mbar_expect_tx(saddr(&sfull[j]), (uint32_t)(TC_DBYTES + C::XSB));
-        bulk_g2s(ring_s + (uint32_t)(s * C::WSTAGE), t, C::QB, saddr(&full[s]));
+        load_w(u, ring_s + (uint32_t)(s * C::WSTAGE), sring_s + (uint32_t)(j * C::SSLOT),
+               saddr(&full[s]), saddr(&sfull[j]));
         bulk_g2s(ring_s + (uint32_t)(s * C::WSTAGE + C::QB), x, C::XB, saddr(&full[s]));
-        bulk_g2s(sring_s + (uint32_t)(j * C::SSLOT), t + C::QB, TC_DBYTES, saddr(&sfull[j]));
         bulk_g2s(sring_s + (uint32_t)(j * C::SSLOT + TC_DBYTES), x + C::XB, C::XSB, saddr(&sfull[j]));
         issued = i + 1;
       }
@@ -431,12 +467,12 @@ __global__ void __launch_bounds__(TcFmt<FMT, NC>::THREADS, 1)
         ok = mbar_wait(saddr(&full[s]), (uint32_t)((i / SW) & 1), &abort_flag);
         // q4_0: the widened quants of unit i are in A slot i % SA
         if (ok && FMT == 4)
-          ok = mbar_wait(saddr(&afull[i % C::SA]), (uint32_t)((i / C::SA) & 1), &abort_flag);
+          ok = mbar_wait(saddr(&afull[i % C::SAD]), (uint32_t)((i / C::SAD) & 1), &abort_flag);
         if (!ok) break;
         tc_fence_after();
         const uint32_t b0 = ring_s + (uint32_t)(s * C::WSTAGE + C::QB);
         const uint32_t a0 = FMT == 8 ? ring_s + (uint32_t)(s * C::WSTAGE)
-                                     : aring_s + (uint32_t)((i % C::SA) * TC_ABYTES);
+                                     : aring_s + (uint32_t)((i % C::SAD) * TC_ABYTES);
         // descriptors of block 0; block b adds its byte offset >> 4 (the start
         // address field, bits 0-13, cannot carry: shared addresses < 256 KB)
         const uint64_t da0 = sw128_desc(a0), db0 = sw128_desc(b0);
@@ -468,7 +504,7 @@ __global__ void __launch_bounds__(TcFmt<FMT, NC>::THREADS, 1)
         }
         if (!ok) break;
         tc_commit(saddr(&empty[s]));  // the stage is free once these MMAs have read it
-        if (FMT == 4) tc_commit(saddr(&aempty[i % C::SA]));  // and so is the A slot
+        if (FMT == 4) tc_commit(saddr(&aempty[i % C::SAD]));  // and so is the A slot
       }
       // every MMA issued completes before the accumulators are freed
       tc_commit(saddr(&mma_done));
@@ -487,15 +523,21 @@ __global__ void __launch_bounds__(TcFmt<FMT, NC>::THREADS, 1)
       const int s = i % SW;
       ok = mbar_wait(saddr(&full[s]), (uint32_t)((i / SW) & 1), &abort_flag);
       if (ok && i >= C::SA)
-        ok = mbar_wait(saddr(&aempty[i % C::SA]), (uint32_t)(((i / C::SA) - 1) & 1), &abort_flag);
+        ok = mbar_wait(saddr(&aempty[i % C::SAD]), (uint32_t)(((i / C::SAD) - 1) & 1), &abort_flag);
       if (!ok) break;
       tc_fence_after();  // the A slot was last read by MMAs (async proxy)
       const uint8_t* pk = ring + (size_t)s * C::WSTAGE;
-      uint8_t* arow = aring + (size_t)(i % C::SA) * TC_ABYTES + h * TC_BOX + (r >> 3) * 1024 +
+      uint8_t* arow = aring + (size_t)(i % C::SAD) * TC_ABYTES + h * TC_BOX + (r >> 3) * 1024 +
                       (r & 7) * 128;
       uint4 w[4];
 #pragma unroll
-      for (int k = 0; k < 4; ++k) w[k] = *reinterpret_cast<const uint4*>(pk + ((4 * h + k) * TC_M + r) * 16);
+      for (int k = 0; k < 4; ++k) {
+        // block 4h + k of row r: tc tile [block][row][16 bytes]; SoA box
+        // [row][128 bytes], 16-byte chunk c at position c ^ (r % 8)
+        const int b = 4 * h + k;
+        w[k] = *reinterpret_cast<const uint4*>(pk + (p.soa ? r * 128 + ((b ^ (r & 7)) << 4)
+                                                            : (b * TC_M + r) * 16));
+      }
 #pragma unroll
       for (int k = 0; k < 4; ++k) {
         uint4 lo, hi;
@@ -512,7 +554,7 @@ __global__ void __launch_bounds__(TcFmt<FMT, NC>::THREADS, 1)
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
       __syncwarp();
       if (lane == 0) {
-        mbar_arrive(saddr(&afull[i % C::SA]));
+        mbar_arrive(saddr(&afull[i % C::SAD]));
         mbar_arrive(saddr(&empty[s]));  // the packed quants are read
       }
     }
@@ -833,10 +875,12 @@ int tc_grid(int64_t M, int64_t K, int sms) {
   return (int)std::max<int64_t>(1, std::min<int64_t>(sms, U));
 }
 
+// tiles != nullptr: tc tiles; else SoA planes q, d (K % 256 == 0, 16-byte
+// aligned), streamed through 2-D tensor maps.
 template <int FMT, int NC>
-int launch_tc(const void* tiles, int64_t M, int64_t K, const float* x, int64_t ldx, float* y,
-              int64_t ldy, int N, void* ws, size_t ws_bytes, const DeviceInfo& dev,
-              cudaStream_t st) {
+int launch_tc(const void* tiles, const void* q, const void* d, int64_t M, int64_t K,
+              const float* x, int64_t ldx, float* y, int64_t ldy, int N, void* ws,
+              size_t ws_bytes, const DeviceInfo& dev, cudaStream_t st) {
   using C = TcFmt<FMT, NC>;
   const int grid = tc_grid(M, K, dev.sms);
   const WsLayout w = ws_layout<NC>(M, K, grid);
@@ -851,6 +895,16 @@ int launch_tc(const void* tiles, int64_t M, int64_t K, const float* x, int64_t l
     attr_done[dev.device] = true;
   }
   TcArgs a;
+  memset(&a, 0, sizeof(a));
+  a.soa = tiles == nullptr;
+  if (a.soa) {
+    const uint64_t qrow = FMT == 8 ? (uint64_t)K : (uint64_t)K / 2;
+    if (int rc = encode_tensor_2d(&a.qmap, false, q, qrow, (uint64_t)M, qrow, 128, TC_M, true))
+      return rc;
+    if (int rc = encode_tensor_2d(&a.dmap, true, d, (uint64_t)(K / QK), (uint64_t)M,
+                                  (uint64_t)(K / QK) * 2, TC_BLK, TC_M, false))
+      return rc;
+  }
   a.tiles = static_cast<const uint8_t*>(tiles);
   a.ws = static_cast<uint8_t*>(ws);
   a.y = y;
@@ -910,13 +964,13 @@ int tile_weights_tc(int fmt, bool aos, const void* q, const void* d, int64_t M, 
 }
 
 template <int FMT>
-int gemv_tc_fmt(const void* tiles, int64_t M, int64_t K, const float* x, int64_t ldx, float* y,
-                int64_t ldy, int N, void* ws, size_t ws_bytes, const DeviceInfo& dev,
-                cudaStream_t st) {
-  if (N <= 2) return launch_tc<FMT, 2>(tiles, M, K, x, ldx, y, ldy, N, ws, ws_bytes, dev, st);
-  if (N <= 4) return launch_tc<FMT, 4>(tiles, M, K, x, ldx, y, ldy, N, ws, ws_bytes, dev, st);
-  if (N <= 8) return launch_tc<FMT, 8>(tiles, M, K, x, ldx, y, ldy, N, ws, ws_bytes, dev, st);
-  return launch_tc<FMT, 16>(tiles, M, K, x, ldx, y, ldy, N, ws, ws_bytes, dev, st);
+int gemv_tc_fmt(const void* tiles, const void* q, const void* d, int64_t M, int64_t K,
+                const float* x, int64_t ldx, float* y, int64_t ldy, int N, void* ws,
+                size_t ws_bytes, const DeviceInfo& dev, cudaStream_t st) {
+  if (N <= 2) return launch_tc<FMT, 2>(tiles, q, d, M, K, x, ldx, y, ldy, N, ws, ws_bytes, dev, st);
+  if (N <= 4) return launch_tc<FMT, 4>(tiles, q, d, M, K, x, ldx, y, ldy, N, ws, ws_bytes, dev, st);
+  if (N <= 8) return launch_tc<FMT, 8>(tiles, q, d, M, K, x, ldx, y, ldy, N, ws, ws_bytes, dev, st);
+  return launch_tc<FMT, 16>(tiles, q, d, M, K, x, ldx, y, ldy, N, ws, ws_bytes, dev, st);
 }
 
 int gemv_tc(int fmt, const void* tiles, int64_t M, int64_t K, const float* x, int64_t ldx,
@@ -924,8 +978,32 @@ int gemv_tc(int fmt, const void* tiles, int64_t M, int64_t K, const float* x, in
   if (M == 0 || N == 0) return OK;
   DeviceInfo dev;
   if (int rc = current_device_info(dev)) return rc;
-  if (fmt == 8) return gemv_tc_fmt<8>(tiles, M, K, x, ldx, y, ldy, N, ws, ws_bytes, dev, st);
-  return gemv_tc_fmt<4>(tiles, M, K, x, ldx, y, ldy, N, ws, ws_bytes, dev, st);
+  if (fmt == 8)
+    return gemv_tc_fmt<8>(tiles, nullptr, nullptr, M, K, x, ldx, y, ldy, N, ws, ws_bytes, dev, st);
+  return gemv_tc_fmt<4>(tiles, nullptr, nullptr, M, K, x, ldx, y, ldy, N, ws, ws_bytes, dev, st);
+}
+
+size_t tc_soa_workspace_bytes(int64_t M, int64_t K, int N, int sms) {
+  const int grid = tc_grid(M, K, sms);
+  if (N <= 2) return ws_layout<2>(M, K, grid).bytes;
+  if (N <= 4) return ws_layout<4>(M, K, grid).bytes;
+  if (N <= 8) return ws_layout<8>(M, K, grid).bytes;
+  return ws_layout<16>(M, K, grid).bytes;
+}
+
+int gemv_soa_tc(int fmt, const GemvCall& c, cudaStream_t st) {
+  if (c.no_tc || c.N < 2 || c.N > 16 || c.K < 256 || c.K % 256 || c.K > (1 << 20) || c.M < 1 ||
+      (reinterpret_cast<uintptr_t>(c.q) & 15) || (reinterpret_cast<uintptr_t>(c.d) & 15) ||
+      !c.ws || (reinterpret_cast<uintptr_t>(c.ws) & 15))
+    return -1;
+  DeviceInfo dev;
+  if (int rc = current_device_info(dev)) return rc;
+  if (c.ws_bytes < tc_soa_workspace_bytes(c.M, c.K, c.N, dev.sms)) return -1;
+  if (fmt == 8)
+    return gemv_tc_fmt<8>(nullptr, c.q, c.d, c.M, c.K, c.x, c.ldx, c.y, c.ldy, c.N, c.ws,
+                          c.ws_bytes, dev, st);
+  return gemv_tc_fmt<4>(nullptr, c.q, c.d, c.M, c.K, c.x, c.ldx, c.y, c.ldy, c.N, c.ws,
+                        c.ws_bytes, dev, st);
 }
 
 int set_tc_spin_limit(long long cycles) {

@@ -1,6 +1,7 @@
 // Internal (C++) interfaces between the kernel files and the C ABI in capi.cu.
 #pragma once
 
+#include <cuda.h>
 #include <cuda_runtime.h>
 #include <stddef.h>
 #include <stdint.h>
@@ -57,6 +58,7 @@ struct GemvCall {
   size_t ws_bytes = 0;
   FuseArgs f;             // fused all-gather (f.nranks == 0: none)
   int act = 0;            // activations: 0 exact (fixed-point planes), 1 q8_1 (opt-in)
+  bool no_tc = false;     // batched SoA: keep to the mma.sync kernel (fixed workspace)
 };
 
 int gemv_soa(int fmt, const GemvCall& c, cudaStream_t st);
@@ -122,6 +124,14 @@ int tile_weights_tc(int fmt, bool aos, const void* q, const void* d, int64_t M, 
                     void* out, cudaStream_t st);
 int gemv_tc(int fmt, const void* tiles, int64_t M, int64_t K, const float* x, int64_t ldx,
             float* y, int64_t ldy, int N, void* ws, size_t ws_bytes, cudaStream_t st);
+// The same kernel streaming SoA planes through 2-D tensor copies (no
+// re-layout): K % 256 == 0, q and d 16-byte aligned; -1 when not eligible or
+// when c.ws_bytes is below tc_soa_workspace_bytes.
+int gemv_soa_tc(int fmt, const GemvCall& c, cudaStream_t st);
+size_t tc_soa_workspace_bytes(int64_t M, int64_t K, int N, int sms);
+// A 2-D tensor map (uint8 or uint16 elements; inner dimension contiguous).
+int encode_tensor_2d(CUtensorMap* map, bool u16, const void* base, uint64_t inner, uint64_t outer,
+                     uint64_t row_bytes, uint32_t box_inner, uint32_t box_outer, bool swizzle128);
 int set_tc_spin_limit(long long cycles);
 int read_tc_error(int clear, cudaStream_t st, int* out);
 // Workspace cached per (device, stream) for callers that pass none; grows on

@@ -186,6 +186,10 @@ def test_workspace_contract():
     n4 = lib.qgemv_soa_workspace_bytes(8, 1000, 4096, 4)
     n16 = lib.qgemv_soa_workspace_bytes(4, 1000, 4096, 16)
     assert 0 < n4 < n16 == lib.qgemv_soa_workspace_bytes(4, 1000, 4096, 40)
+    # the need grows with M (the tcgen05 kernel keeps per-row-tile counters)
+    assert lib.qgemv_soa_workspace_bytes(8, 64, 4096, 4) <= n4
+    assert n4 <= lib.qgemv_soa_workspace_bytes(8, 100000, 4096, 4)
+    n4 = lib.qgemv_soa_workspace_bytes(8, 64, 4096, 4)
     q, d, X = make("q8_0", 64, 4096, 4, seed=1)
     qt, dt = planes(q, d)
     Xt = torch.from_numpy(X).to(DEV)
@@ -289,12 +293,31 @@ def test_tiled_gemv(fmt, M, K, N):
 
 
 @pytest.mark.parametrize("fmt", ["q8_0", "q4_0"])
-def test_tiled_matches_soa_batch(fmt):
+@pytest.mark.parametrize("M,N", [(2000, 12), (4099, 2), (300, 16), (129, 5)])
+def test_soa_batch_matches_tc_tiles(fmt, M, N):
+    """Batched SoA calls run the tcgen05 kernel straight from the planes (2-D
+    tensor copies, 128-byte swizzle): the same smem image as the tc tiles and
+    the same arithmetic in the same order, so identical bits."""
+    K = 8192
+    q, d, X = make(fmt, M, K, N, seed=77 + M)
+    qt, dt = planes(q, d)
+    Xt = torch.from_numpy(X).to(DEV)
+    Ys = qg.qgemv(fmt, qt, dt, Xt)
+    Yc = qg.qgemv_tc(qg.tile_weights_tc(q=qt, d=dt, fmt=fmt), M, K, Xt, fmt=fmt)
+    assert torch.equal(Ys, Yc)
+    check(fmt, q, d, X, Ys.cpu().numpy())
+
+
+@pytest.mark.parametrize("fmt", ["q8_0", "q4_0"])
+def test_tiled_matches_static_ws_batch(fmt):
+    """The static-workspace entry keeps the mma.sync kernel: on SoA planes it
+    gives the same bits as the same kernel on batch tiles."""
     M, K, N = 2000, 8192, 12
     q, d, X = make(fmt, M, K, N, seed=77)
     qt, dt = planes(q, d)
     Xt = torch.from_numpy(X).to(DEV)
-    Ys = qg.qgemv(fmt, qt, dt, Xt)
+    Ys = torch.empty((N, M), device=DEV)
+    _lib.call("qgemv_soa_static_ws", FMT_ID[fmt], qt.data_ptr(), dt.data_ptr(), Xt.data_ptr(),
+              Ys.data_ptr(), M, K, N, K, M, torch.cuda.current_stream().cuda_stream)
     Yt = qg.qgemv_tiled(fmt, qg.tile_weights(fmt, q=qt, d=dt), M, K, Xt)
-    # same tiles, same arithmetic in the same order: identical bits
     assert torch.equal(Ys, Yt)

@@ -105,7 +105,8 @@ def test_python_raises_typed_error():
 
 def test_workspace_and_tile_sizes_are_host_computations():
     lib = _lib.lib()
-    # batched SoA calls: 128 + 2064 * ceil(K / 512) * min(N, 16) bytes, 0 when no workspace
+    # batched SoA calls with no device: the mma.sync kernel's 128 + 2064 * ceil(K / 512) *
+    # min(N, 16) bytes, 0 when no workspace (on a B200 the tcgen05 kernel's need, larger)
     assert lib.qgemv_soa_workspace_bytes(8, 1000, 4096, 4) == 128 + 2064 * 8 * 4
     assert lib.qgemv_soa_workspace_bytes(4, 1000, 4096, 40) == 128 + 2064 * 8 * 16
     assert lib.qgemv_soa_workspace_bytes(8, 1000, 4096, 1) == 0
