@@ -89,8 +89,13 @@ constexpr int TC_PMAX = 64;                     // x prep chunks per column, at 
 constexpr int TC_HDR = 16 * TC_PMAX * 4;
 constexpr int TC_EMPTY = -100000;               // block exponent of an all-zero block
 constexpr int TC_SMEM_MAX = 227 * 1024 - 1024;  // shared memory we use at most (dynamic + scratch)
-constexpr int TC_SS = 8;                        // scale ring slots
 constexpr int TC_MAXSLOTS = 8;                  // TMEM slots, at most
+// units whose weights are copied before the dependency wait (the x digits of
+// every unit come after it); the rest of the ring fills after the x copies
+// of these, so x does not queue behind a whole ring of weights (28672x8192,
+// against prefetching the whole ring: q8_0 8 columns 53.4 -> 52.7 us, q4_0
+// 1-2 columns 49.5 -> 49.1 us)
+constexpr int TC_PRE = 2;
 
 // What depends on the column count only (the x side, shared with the prep).
 template <int NC>
@@ -133,23 +138,34 @@ struct TcFmt : TcCfg<NC> {
   static constexpr int EPI = 4 * G;
   static constexpr int SA = FMT == 8 ? 0 : 3;         // A ring slots (q4_0)
   static constexpr int SAD = SA > 0 ? SA : 1;         // SA as a divisor (q8_0 never divides)
+  // scale ring slots: q8_0 at 8 and 16 columns 12, where the epilogue's
+  // arithmetic makes it the slowest consumer and a deeper ring lets the
+  // weights run ahead (28672x8192, 8 columns: 54.8 -> 53.7 us, though it
+  // leaves one weight stage fewer; 10 slots and 5 stages: 54.2 us); 8
+  // otherwise (q8_0 at 2 columns with 12 slots and 5 weight stages: 44.6 ->
+  // 47.2 us; q4_0 at 8 columns: 65.2 -> 66.0 us)
+  static constexpr int SS = FMT == 8 && NC >= 8 ? 12 : 8;
   static constexpr int THREADS = 32 * (TC_W0E + EPI + CONV);
   // weight stage: quants + x digits (what the MMAs, or the converters, read)
   static constexpr int WSTAGE = QB + TcCfg<NC>::XB;   // a multiple of 1024
   // left for weight stages: the budget minus alignment slack, the scale and A
   // rings and the epilogue warps' static scratch (8 x 8 NC floats)
   static constexpr int FREE =
-      TC_SMEM_MAX - 1024 - TC_SS * TcCfg<NC>::SSLOT - SA * TC_ABYTES - 8 * NC * 4 * 4;
-  static constexpr int SW = FREE / WSTAGE > 8 ? 8 : FREE / WSTAGE;
+      TC_SMEM_MAX - 1024 - SS * TcCfg<NC>::SSLOT - SA * TC_ABYTES - 8 * NC * 4 * 4;
+  // weight stages: q4_0 at most 4 (28672x8192, 1-2 columns: 3 / 4 / 5 / 6
+  // stages 52.2 / 49.5 / 50.4 / 51.0 us; its 3 A slots, not the weight ring,
+  // set the pace: 1 A slot 62 us, 2 slots 51.0 us)
+  static constexpr int SWMAX = FMT == 8 ? 8 : 4;
+  static constexpr int SW = FREE / WSTAGE > SWMAX ? SWMAX : FREE / WSTAGE;
   static constexpr size_t SMEM =
-      (size_t)SW * WSTAGE + (size_t)SA * TC_ABYTES + (size_t)TC_SS * TcCfg<NC>::SSLOT + 1024;
+      (size_t)SW * WSTAGE + (size_t)SA * TC_ABYTES + (size_t)SS * TcCfg<NC>::SSLOT + 1024;
 };
 static_assert(TcFmt<8, 16>::SMEM + 8 * 16 * 4 * 4 <= TC_SMEM_MAX &&
                   TcFmt<4, 16>::SMEM + 8 * 16 * 4 * 4 <= TC_SMEM_MAX &&
                   TcFmt<8, 2>::SMEM <= TC_SMEM_MAX && TcFmt<4, 2>::SMEM <= TC_SMEM_MAX,
               "ring too large");
-static_assert(TcFmt<8, 16>::SW >= 4 && TcFmt<8, 8>::SW >= 5 && TcFmt<4, 16>::SW >= 3 &&
-                  TcFmt<4, 2>::SW <= TC_SS,
+static_assert(TcFmt<8, 16>::SW >= 4 && TcFmt<8, 8>::SW >= 4 && TcFmt<4, 16>::SW >= 3 &&
+                  TcFmt<8, 2>::SW == 6 && TcFmt<4, 2>::SW == 4,
               "ring depth");
 static_assert(TcCfg<16>::SLW == 2 && TcCfg<8>::SLW == 2 && TcCfg<4>::SLW == 4 &&
                   TcCfg<2>::SLW == 8 && TcCfg<16>::SPW >= 1 && TcCfg<2>::SPW >= 1 &&
@@ -334,8 +350,10 @@ __global__ void __launch_bounds__(TcFmt<FMT, NC>::THREADS, 1)
   __shared__ __align__(8) unsigned long long empty[SW];      // its MMAs (and converters) read it
   __shared__ __align__(8) unsigned long long afull[4];       // q4_0: A slot widened
   __shared__ __align__(8) unsigned long long aempty[4];      // q4_0: its MMAs have read it
-  __shared__ __align__(8) unsigned long long sfull[TC_SS];   // scale slot landed
-  __shared__ __align__(8) unsigned long long sempty[TC_SS];  // the epilogue is done with it
+  constexpr int SS = C::SS;
+  static_assert(SW <= SS, "the first SW units' scales are prefetched into distinct slots");
+  __shared__ __align__(8) unsigned long long sfull[SS];   // scale slot landed
+  __shared__ __align__(8) unsigned long long sempty[SS];  // the epilogue is done with it
   __shared__ __align__(8) unsigned long long tfull[TC_MMAW][TC_MAXSLOTS];   // MMAs of a slot done
   __shared__ __align__(8) unsigned long long tempty[TC_MMAW][TC_MAXSLOTS];  // the epilogue read it
   __shared__ __align__(8) unsigned long long mma_done;
@@ -364,7 +382,7 @@ __global__ void __launch_bounds__(TcFmt<FMT, NC>::THREADS, 1)
       mbar_init(saddr(&afull[s]), C::CONV);  // every converter warp
       mbar_init(saddr(&aempty[s]), TC_MMAW);  // each MMA warp's commit
     }
-    for (int s = 0; s < TC_SS; ++s) {
+    for (int s = 0; s < SS; ++s) {
       mbar_init(saddr(&sfull[s]), 1);
       mbar_init(saddr(&sempty[s]), C::EPI);  // every epilogue warp
     }
@@ -392,11 +410,13 @@ __global__ void __launch_bounds__(TcFmt<FMT, NC>::THREADS, 1)
   if (warp == 0) {
     // ------------------------------------------------------------ producer
     // unit i: quants -> weight stage i % SW, x digits behind them; the tile's
-    // scales and the x block scales -> scale slot i % TC_SS
+    // scales and the x block scales -> scale slot i % SS
     if (lane == 0) {
       const uint8_t* xt = p.ws + p.xt_off;
-      // weights do not depend on the previous kernel: prefetch them first
-      const int pre = min(SW, nunits);
+      // weights do not depend on the previous kernel: prefetch TC_PRE units
+      // first; the loop below waits on a stage's release only once it has
+      // been used (a fresh barrier passes the wait for the phase before it)
+      const int pre = min(min(SW, TC_PRE), nunits);
       // unit u's quants and fp16 scales: one tc tile (two bulk copies) or,
       // from SoA planes, 2-D tensor copies of 128 rows (q8_0: two 128-byte
       // boxes; q4_0: one) and one scale box; rows past M read as zeros
@@ -430,10 +450,10 @@ __global__ void __launch_bounds__(TcFmt<FMT, NC>::THREADS, 1)
       }
       int issued = pre;
       for (int i = pre; i < nunits; ++i) {
-        const int s = i % SW, j = i % TC_SS;
+        const int s = i % SW, j = i % SS;
         if (!mbar_wait(saddr(&empty[s]), (uint32_t)(((i / SW) - 1) & 1), &abort_flag)) break;
-        if (i >= TC_SS &&
-            !mbar_wait(saddr(&sempty[j]), (uint32_t)(((i / TC_SS) - 1) & 1), &abort_flag))
+        if (i >= SS &&
+            !mbar_wait(saddr(&sempty[j]), (uint32_t)(((i / SS) - 1) & 1), &abort_flag))
           break;
         const int64_t u = u0 + i;
         const uint8_t* x = xt + (int64_t)(u % p.nkt) * C::XT;
@@ -448,8 +468,8 @@ __global__ void __launch_bounds__(TcFmt<FMT, NC>::THREADS, 1)
       if (issued < nunits) {  // aborted: wait (bounded) for the copies still in flight
         for (int i = max(0, issued - SW); i < issued; ++i)
           mbar_wait_drain(saddr(&full[i % SW]), (uint32_t)((i / SW) & 1));
-        for (int i = max(0, issued - TC_SS); i < issued; ++i)
-          mbar_wait_drain(saddr(&sfull[i % TC_SS]), (uint32_t)((i / TC_SS) & 1));
+        for (int i = max(0, issued - SS); i < issued; ++i)
+          mbar_wait_drain(saddr(&sfull[i % SS]), (uint32_t)((i / SS) & 1));
       }
     }
   } else if (warp <= TC_MMAW) {
@@ -602,11 +622,11 @@ __global__ void __launch_bounds__(TcFmt<FMT, NC>::THREADS, 1)
 #pragma unroll
     for (int c = 0; c < NCH; ++c) acc[c] = 0.0f;
     for (int i = 0; i < nunits; ++i) {
-      const int j = i % TC_SS;
+      const int j = i % SS;
       const int64_t u = u0 + i;
       const int rt = (int)(u / p.nkt), kt = (int)(u % p.nkt);
       // the unit's scales: scale slot j
-      mbar_wait(saddr(&sfull[j]), (uint32_t)((i / TC_SS) & 1), &abort_flag);
+      mbar_wait(saddr(&sfull[j]), (uint32_t)((i / SS) & 1), &abort_flag);
       const uint8_t* sst = sring + (size_t)j * C::SSLOT;
       const uint4 d8 = *reinterpret_cast<const uint4*>(sst + row * 16);  // 8 fp16
       // block scales 2^(e + sh - 22) of this warp's columns, e = the block's
