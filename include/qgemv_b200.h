@@ -168,9 +168,13 @@ QGEMV_API int qgemv_release_workspaces(void);
  * callers that must not allocate on the call path and have no device buffer
  * of their own to lend, e.g. a plugin host that forbids device allocation
  * after its initialisation, or a foreign-language binding that cannot own
- * CUDA memory.  Limit: calls needing more than 2 MiB of workspace (above
- * K = 32256 at 16 columns) fail with QGEMV_ERR_UNSUPPORTED before anything
- * is launched.  The first call on a device looks up the array's address
+ * CUDA memory.  Kernel: the tcgen05 batch kernel when its workspace fits
+ * the array (at 7B-layer shapes up to 8 columns; it grows with M, the column
+ * count and the SM count), otherwise the mma.sync batch kernel, whose
+ * workspace depends on K and the column count only.  Limit: calls needing
+ * more than 2 MiB of mma.sync workspace (above K = 32256 at 16 columns) fail
+ * with QGEMV_ERR_UNSUPPORTED before anything is launched.  The first call on
+ * a device looks up the array's address
  * (cudaGetSymbolAddress) and caches it; make that call before any stream
  * capture.  The cached address assumes the device's primary context lives
  * as long as the process: after cudaDeviceReset the array moves, so a caller

@@ -584,8 +584,12 @@ QGEMV_API int qgemv_soa_static_ws(int format, const void* q, const void* d, cons
   probe.M = M;
   probe.K = K;
   probe.N = std::min(std::max(ncols, 0), 16);
+  // the tcgen05 kernel where its workspace fits the array (it grows with M,
+  // the column count and the SM count), else the mma.sync kernel
+  bool allow_tc = false;
   if (M > 0 && probe.N >= 2 && mma_eligible(probe)) {
-    const size_t need = mma_workspace_bytes(K, probe.N);
+    allow_tc = soa_batch_workspace(probe, true) <= kStaticWsBytes;
+    const size_t need = soa_batch_workspace(probe, allow_tc);
     if (need > kStaticWsBytes)
       return set_error(ERR_UNSUPPORTED,
                        "this call needs %zu bytes of workspace; the static workspace holds %zu "
@@ -594,7 +598,7 @@ QGEMV_API int qgemv_soa_static_ws(int format, const void* q, const void* d, cons
     if (int rc = static_workspace(&ws, &ws_bytes)) return rc;
   }
   return gemv_entry(format, false, q, d, x, y, M, K, ncols, ldx, ldy, stream, ws, ws_bytes, true,
-                    /*allow_tc=*/false);
+                    allow_tc);
 }
 
 QGEMV_API size_t qgemv_tiled_bytes(int format, int64_t M, int64_t K) {

@@ -1,13 +1,15 @@
 // Workspace compiled into the library, for callers that must not allocate.
 //
 // The batched SoA GEMV (2..16 columns per launch on the tensor cores) needs a
-// workspace for the re-laid activations.  qgemv_soa_static_ws takes it from
-// this fixed array instead of from the caller or from cudaMalloc, so that no
-// call of that entry point allocates device memory.
+// workspace for the re-laid activations (and, on tcgen05, per-row-tile
+// counters and partial sums).  qgemv_soa_static_ws takes it from this fixed
+// array instead of from the caller or from cudaMalloc, so that no call of
+// that entry point allocates device memory.
 //
-// * Size: kStaticWsBytes (2 MiB) per device; enough for K <= 32256 with 16
-//   columns (the workspace is 128 + 2064 * min(ncols, 16) * ceil(K / 512)
-//   bytes).  Larger calls are rejected before anything is launched.
+// * Size: kStaticWsBytes (2 MiB) per device.  The tcgen05 kernel runs when
+//   its workspace fits; otherwise the mma.sync kernel, whose workspace
+//   (128 + 2064 * min(ncols, 16) * ceil(K / 512) bytes) fits for K <= 32256
+//   with 16 columns.  Larger calls are rejected before anything is launched.
 // * Set-up: the first call on a device looks up the array's address on that
 //   device (cudaGetSymbolAddress, with that device current) and caches it;
 //   later calls reuse it.  Make that first call before any stream capture.

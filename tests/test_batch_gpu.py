@@ -310,8 +310,10 @@ def test_soa_batch_matches_tc_tiles(fmt, M, N):
 
 @pytest.mark.parametrize("fmt", ["q8_0", "q4_0"])
 def test_tiled_matches_static_ws_batch(fmt):
-    """The static-workspace entry keeps the mma.sync kernel: on SoA planes it
-    gives the same bits as the same kernel on batch tiles."""
+    """Where the tcgen05 workspace does not fit its 2 MiB array (here 12
+    columns: 2.4 MB of partial sums on 148 SMs), the static-workspace entry
+    runs the mma.sync kernel: on SoA planes it gives the same bits as the
+    same kernel on batch tiles."""
     M, K, N = 2000, 8192, 12
     q, d, X = make(fmt, M, K, N, seed=77)
     qt, dt = planes(q, d)

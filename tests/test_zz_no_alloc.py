@@ -26,7 +26,8 @@ def make(fmt, M, K, N, seed):
 
 
 @pytest.mark.parametrize("fmt", ["q8_0", "q4_0"])
-@pytest.mark.parametrize("M,K,N", [(1000, 4096, 16), (257, 11008, 5), (64, 2048, 1)])
+@pytest.mark.parametrize("M,K,N", [(1000, 4096, 16), (257, 11008, 5), (64, 2048, 1),
+                                   (4096, 4096, 8), (11008, 4096, 2)])
 def test_static_workspace_matches_caller_workspace(fmt, M, K, N):
     lib = _lib.lib()
     q, d, X = make(fmt, M, K, N, seed=M + K + N)
@@ -52,6 +53,10 @@ def test_static_workspace_matches_caller_workspace(fmt, M, K, N):
         bound = 1e-5 * wn[None, :] * np.linalg.norm(X.astype(np.float64), axis=1)[:, None]
         assert (np.abs(yh - y_ref.cpu().numpy()) <= bound).all()
         assert (np.abs(yh - y64) <= bound).all()
+        if nb <= 2 << 20:
+            # the whole workspace fits the array: the same (tcgen05) kernel as
+            # with the caller's workspace, so the same bits
+            assert torch.equal(y, y_ref)
     assert lib.qgemv_check_device_error(0, None) == 0
 
 
