@@ -460,6 +460,48 @@ typedef struct qgemv_call_desc {
 QGEMV_API int qgemv_time_steps(const qgemv_call_desc* calls, int32_t ncalls, int32_t warmup,
                                int32_t steps, int32_t grouped, void* stream, float* ms_out);
 
+/* ---- Multi-GPU handle: one process drives several GPUs ----------------------
+ * A q8_0 / q4_0 matrix sharded by rows over the handle's P devices (rows
+ * [g*M/P, (g+1)*M/P) on devices[g], copied there by qgemv_mg_shard), one GEMV
+ * per device on that device's stream, and, when asked, an all-gather of y so
+ * that every device holds all M rows: each device pushes its rows of every
+ * column into every other device's y with one 2-D peer copy (NVLink through
+ * NVSwitch where the devices can address each other; peer access is enabled
+ * by qgemv_mg_init).  For hosts that run one process per GPU instead, the
+ * Python ShardedQGemv shards the same way and all-gathers with NCCL.  No
+ * counterpart in the reference, which runs on one GPU. */
+
+/* devices: ndev (1..QGEMV_MAX_RANKS) distinct device ordinals; *handle
+ * receives the handle (streams and events per device). */
+QGEMV_API int qgemv_mg_init(int32_t ndev, const int32_t* devices, void** handle);
+
+/* Copies the matrix's row shards onto the devices (synchronous; replaces a
+ * matrix the handle held before).  layout 0: SoA planes q [M][K] int8 (q8_0)
+ * or [M][K/2] uint8 (q4_0) and d [M][K/32] fp16; layout 1: ggml blocks in q,
+ * d unused.  q and d may live in host memory or on any device. */
+QGEMV_API int qgemv_mg_shard(void* handle, int format, int layout, const void* q, const void* d,
+                             int64_t M, int64_t K);
+
+/* The first row and the row count of shard `index` (the index-th device). */
+QGEMV_API int qgemv_mg_rows(void* handle, int32_t index, int64_t* r0, int64_t* rows);
+
+/* Y = X W^T for ncols columns: x[g] is devices[g]'s copy of X ([ncols][K]
+ * floats, ldx = K), y[g] devices[g]'s Y ([ncols][M] floats, ldy = M); device
+ * g writes its rows of y[g] and, with allgather != 0, every other device's
+ * rows arrive in y[g] as well.  streams[g]: the stream of devices[g] (NULL,
+ * or a NULL entry: the handle's own stream).  Asynchronous: work queued
+ * afterwards on streams[g] sees y[g] complete; the copies into y[g] start
+ * only after what was queued on streams[g] before the call. */
+QGEMV_API int qgemv_mg_gemv(void* handle, const float* const* x, float* const* y, int32_t ncols,
+                            int32_t allgather, void* const* streams);
+
+/* Waits for the handle's own streams. */
+QGEMV_API int qgemv_mg_synchronize(void* handle);
+
+/* Waits for the handle's own streams, then frees the shards, streams and
+ * events (NULL: no-op). */
+QGEMV_API int qgemv_mg_destroy(void* handle);
+
 #ifdef __cplusplus
 }
 #endif

@@ -122,6 +122,13 @@ SIGNATURES = {
     "qgemv_stack_run": ([_vp, _vp], ctypes.c_int),
     "qgemv_stack_reset": ([_vp, _vp], ctypes.c_int),
     "qgemv_stack_destroy": ([_vp], ctypes.c_int),
+    "qgemv_mg_init": ([_i32, ctypes.POINTER(_i32), ctypes.POINTER(_vp)], ctypes.c_int),
+    "qgemv_mg_shard": ([_vp, ctypes.c_int, ctypes.c_int, _vp, _vp, _i64, _i64], ctypes.c_int),
+    "qgemv_mg_rows": ([_vp, _i32, ctypes.POINTER(_i64), ctypes.POINTER(_i64)], ctypes.c_int),
+    "qgemv_mg_gemv": ([_vp, ctypes.POINTER(_vp), ctypes.POINTER(_vp), _i32, _i32,
+                       ctypes.POINTER(_vp)], ctypes.c_int),
+    "qgemv_mg_synchronize": ([_vp], ctypes.c_int),
+    "qgemv_mg_destroy": ([_vp], ctypes.c_int),
     "qgemv_soa_static_ws": ([ctypes.c_int, _vp, _vp, _vp, _vp, _i64, _i64, _i32, _i64, _i64, _vp],
                             ctypes.c_int),
     "qgemv_tiled_bytes": ([ctypes.c_int, _i64, _i64], ctypes.c_size_t),

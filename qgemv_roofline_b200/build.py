@@ -17,7 +17,7 @@ REPO = os.path.dirname(HERE)
 CSRC = os.path.join(HERE, "csrc")
 LIB = os.path.join(HERE, "libqgemv_b200.so")
 SOURCES = ["capi.cu", "gemv_soa.cu", "gemv_aos.cu", "quant.cu", "roof.cu", "harness.cu", "gemv_tma.cu", "gemv_mma.cu",
-           "gemv_tc.cu", "static_ws.cu"]
+           "gemv_tc.cu", "static_ws.cu", "multi_gpu.cu"]
 HEADERS = ["qgemv_common.cuh", "qgemv_internal.h", "gemv_core.cuh"]
 NVCC = os.environ.get("NVCC", "nvcc")
 FLAGS = [

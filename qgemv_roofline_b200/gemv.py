@@ -10,6 +10,7 @@ the GPU: this is the hot path and it does no implicit copies.
 
 from __future__ import annotations
 
+import functools
 from dataclasses import dataclass
 
 import torch
@@ -19,6 +20,20 @@ from .qformats import BLOCK_BYTES, QK
 
 _SOA_FN = {"q8_0": "qgemv_q8_0_soa", "q4_0": "qgemv_q4_0_soa"}
 _AOS_FN = {"q8_0": "qgemv_q8_0_aos", "q4_0": "qgemv_q4_0_aos"}
+
+
+def _on_tensor_device(fn):
+    """Runs ``fn`` with the device of its first CUDA tensor argument current:
+    the C ABI launches on the current device, and the per-device state it
+    keeps (workspaces, tile counters) belongs to that device too."""
+    @functools.wraps(fn)
+    def wrapper(*args, **kwargs):
+        for a in (*args, *kwargs.values()):
+            if isinstance(a, torch.Tensor) and a.is_cuda:
+                with torch.cuda.device(a.device):
+                    return fn(*args, **kwargs)
+        return fn(*args, **kwargs)
+    return wrapper
 
 
 def _check_fmt(fmt: str):
@@ -81,6 +96,7 @@ def _check_act(activations: str, N: int):
         raise ValueError("q8_1 activations are a single-column path (x must be [K])")
 
 
+@_on_tensor_device
 def qgemv(fmt: str, q: torch.Tensor, d: torch.Tensor, x: torch.Tensor,
           y: torch.Tensor | None = None, stream: int | None = None,
           activations: str = "exact") -> torch.Tensor:
@@ -118,6 +134,7 @@ def qgemv(fmt: str, q: torch.Tensor, d: torch.Tensor, x: torch.Tensor,
     return y
 
 
+@_on_tensor_device
 def qgemv_aos(fmt: str, blocks: torch.Tensor, x: torch.Tensor,
               y: torch.Tensor | None = None, stream: int | None = None,
               activations: str = "exact") -> torch.Tensor:
@@ -142,6 +159,7 @@ def qgemv_aos(fmt: str, blocks: torch.Tensor, x: torch.Tensor,
     return y
 
 
+@_on_tensor_device
 def tile_weights(fmt: str, q: torch.Tensor | None = None, d: torch.Tensor | None = None,
                  blocks: torch.Tensor | None = None, stream: int | None = None) -> torch.Tensor:
     """Batch tiles (uint8, 1-D) of a matrix given as SoA planes (q, d) or ggml
@@ -166,6 +184,7 @@ def tile_weights(fmt: str, q: torch.Tensor | None = None, d: torch.Tensor | None
     return out
 
 
+@_on_tensor_device
 def qgemv_tiled(fmt: str, tiled: torch.Tensor, M: int, K: int, x: torch.Tensor,
                 y: torch.Tensor | None = None, stream: int | None = None) -> torch.Tensor:
     """GEMV over batch tiles (tile_weights); x [K] or [N, K] for any N."""
@@ -184,6 +203,7 @@ def qgemv_tiled(fmt: str, tiled: torch.Tensor, M: int, K: int, x: torch.Tensor,
     return y
 
 
+@_on_tensor_device
 def tile_weights_tc(q: torch.Tensor | None = None, d: torch.Tensor | None = None,
                     blocks: torch.Tensor | None = None, stream: int | None = None,
                     fmt: str = "q8_0") -> torch.Tensor:
@@ -210,6 +230,7 @@ def tile_weights_tc(q: torch.Tensor | None = None, d: torch.Tensor | None = None
     return out
 
 
+@_on_tensor_device
 def qgemv_tc(tiles: torch.Tensor, M: int, K: int, x: torch.Tensor, y: torch.Tensor | None = None,
              stream: int | None = None, fmt: str = "q8_0") -> torch.Tensor:
     """GEMV over tc tiles (tile_weights_tc) on the tcgen05 tensor cores;
@@ -222,8 +243,7 @@ def qgemv_tc(tiles: torch.Tensor, M: int, K: int, x: torch.Tensor, y: torch.Tens
         raise ValueError(f"tiles hold {tiles.numel()} bytes, not those of a [{M}, {K}] {fmt} matrix")
     X, Y, y, N, ldx, ldy = _xy(x, M, K, y, tiles.device)
     st = torch.cuda.current_stream(tiles.device).cuda_stream if stream is None else stream
-    with torch.cuda.device(tiles.device):
-        nbytes = _lib.lib().qgemv_tc_workspace_bytes(M, K)
+    nbytes = _lib.lib().qgemv_tc_workspace_bytes(M, K)  # on the tiles' device
     ws = _workspace(tiles.device, nbytes, stream)
     _lib.call("qgemv_tc_gemv", fid, tiles.data_ptr(), M, K, X.data_ptr(), Y.data_ptr(), N, ldx,
               ldy, ws.data_ptr(), ws.numel(), st)

@@ -93,3 +93,83 @@ class ShardedQGemv:
                 for g in range(P)]
         full = torch.cat(cols, dim=0).t().contiguous()  # [N, M]
         return full[0] if vec else full
+
+
+class MultiDeviceQGemv:
+    """One process, several GPUs: a quantized matrix sharded by rows over
+    ``devices`` (the same ``row_range`` partition) through the C-ABI
+    multi-GPU handle (``qgemv_mg_*``), with the all-gather of y done by peer
+    copies between the devices instead of NCCL.
+
+    ``forward(xs, allgather=True)`` takes one X per device (``[K]`` or
+    ``[N, K]``, on that device) and returns one Y per device (``[M]`` or
+    ``[N, M]``): the device's own rows, and with ``allgather`` every row.
+    Each device's work runs on its current torch stream.
+    """
+
+    def __init__(self, full: QuantizedMatrix, devices):
+        import ctypes
+
+        from . import _lib
+
+        if full.layout not in ("soa", "aos"):
+            raise ValueError("shard a matrix held as SoA planes or ggml blocks")
+        self._lib = _lib
+        self.devices = [torch.device("cuda", d) if isinstance(d, int) else torch.device(d)
+                        for d in devices]
+        n = len(self.devices)
+        ids = (ctypes.c_int32 * n)(*[d.index for d in self.devices])
+        h = ctypes.c_void_p()
+        _lib.call("qgemv_mg_init", n, ids, ctypes.byref(h))
+        self._h = h
+        self.M, self.K, self.fmt = full.M, full.K, full.fmt
+        soa = full.layout == "soa"
+        src = full.q if soa else full.blocks
+        if src.is_cuda:
+            torch.cuda.synchronize(src.device)  # the shards are copied from finished bytes
+        try:
+            _lib.call("qgemv_mg_shard", self._h, _lib.FORMAT_CODE[self.fmt], 0 if soa else 1,
+                      src.data_ptr(), full.d.data_ptr() if soa else None, self.M, self.K)
+            self.row_ranges = []
+            for g in range(n):
+                r0, rows = ctypes.c_int64(), ctypes.c_int64()
+                _lib.call("qgemv_mg_rows", self._h, g, ctypes.byref(r0), ctypes.byref(rows))
+                self.row_ranges.append((r0.value, r0.value + rows.value))
+        except Exception:
+            self.close()
+            raise
+
+    def forward(self, xs, ys=None, allgather: bool = True):
+        import ctypes
+
+        n = len(self.devices)
+        if len(xs) != n:
+            raise ValueError(f"one x per device: {n} expected, {len(xs)} given")
+        one = xs[0].dim() == 1
+        N = 1 if one else xs[0].shape[0]
+        for x, dev in zip(xs, self.devices):
+            if x.device != dev or x.dtype != torch.float32 or not x.is_contiguous() \
+                    or x.shape[-1] != self.K or (1 if x.dim() == 1 else x.shape[0]) != N:
+                raise ValueError(f"x must be contiguous fp32 [{'' if one else 'N, '}K] on {dev}")
+        if ys is None:
+            ys = [torch.empty((self.M,) if one else (N, self.M), device=dev)
+                  for dev in self.devices]
+        xp = (ctypes.c_void_p * n)(*[x.data_ptr() for x in xs])
+        yp = (ctypes.c_void_p * n)(*[y.data_ptr() for y in ys])
+        sp = (ctypes.c_void_p * n)(*[torch.cuda.current_stream(dev).cuda_stream
+                                     for dev in self.devices])
+        self._lib.call("qgemv_mg_gemv", self._h, xp, yp, N, int(allgather), sp)
+        return ys
+
+    __call__ = forward
+
+    def close(self):
+        if getattr(self, "_h", None) is not None and self._h.value:
+            self._lib.call("qgemv_mg_destroy", self._h)
+        self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass

@@ -137,3 +137,21 @@ def test_fused_and_tiled_validation():
               None) == 5
     assert rc("qgemv_tiled_gemv", 8, FAKE + 4, 16, 512, FAKE, FAKE, 1, 512, 16, None, 0,
               None) == 3
+
+
+def test_multi_gpu_handle_validation():
+    lib = _lib.lib()
+    h = ctypes.c_void_p()
+    devs = (ctypes.c_int32 * 2)(0, 1)
+    assert lib.qgemv_mg_init(2, None, ctypes.byref(h)) == 1
+    assert lib.qgemv_mg_init(2, devs, None) == 1
+    assert lib.qgemv_mg_init(0, devs, ctypes.byref(h)) == 7
+    assert lib.qgemv_mg_init(9, devs, ctypes.byref(h)) == 7
+    assert not h.value
+    # a NULL handle is refused by every entry point; destroying it is a no-op
+    r0, rows = ctypes.c_int64(), ctypes.c_int64()
+    assert lib.qgemv_mg_shard(None, 8, 0, FAKE, FAKE, 64, 64) == 1
+    assert lib.qgemv_mg_rows(None, 0, ctypes.byref(r0), ctypes.byref(rows)) == 1
+    assert lib.qgemv_mg_gemv(None, None, None, 1, 1, None) == 1
+    assert lib.qgemv_mg_synchronize(None) == 1
+    assert lib.qgemv_mg_destroy(None) == 0
