@@ -73,25 +73,32 @@ class ShardedQGemv:
     __call__ = forward
 
     def all_gather(self, y_local: torch.Tensor) -> torch.Tensor:
-        """[rows] or [N, rows] slices of every rank -> full [M] or [N, M]."""
+        """[rows] or [N, rows] slices of every rank -> full [M] or [N, M].
+
+        One all-gather into a [P, N, S] buffer (S = the largest slice).  When
+        every rank holds S rows (M divisible by P) a vector needs nothing more
+        (the buffer is y in row order) and N columns one transposing copy;
+        otherwise the slices are padded to S before the gather and the
+        padding dropped after it."""
         vec = y_local.dim() == 1
         Y = y_local.unsqueeze(0) if vec else y_local
         N, rows = Y.shape
         P, S = self.world, self.slice_max
-        pad = torch.zeros((N, S), dtype=Y.dtype, device=Y.device)
-        pad[:, :rows] = Y
-        send = pad.t().contiguous()  # [S, N]: rank-major after the gather
-        if dist.get_backend(self.group) == "nccl":
-            out = torch.empty((P * S, N), dtype=Y.dtype, device=Y.device)
-            dist.all_gather_into_tensor(out, send, group=self.group)
-            parts = out.view(P, S, N)
+        even = self.M == P * S
+        if rows == S:
+            send = Y.contiguous()
         else:
-            bufs = [torch.empty_like(send) for _ in range(P)]
-            dist.all_gather(bufs, send, group=self.group)
-            parts = torch.stack(bufs)
-        cols = [parts[g, : row_range(self.M, g, P)[1] - row_range(self.M, g, P)[0]]
-                for g in range(P)]
-        full = torch.cat(cols, dim=0).t().contiguous()  # [N, M]
+            send = torch.zeros((N, S), dtype=Y.dtype, device=Y.device)
+            send[:, :rows] = Y
+        out = torch.empty((P * N, S), dtype=Y.dtype, device=Y.device)
+        dist.all_gather_into_tensor(out, send, group=self.group)
+        out = out.view(P, N, S)
+        if even:
+            if vec:
+                return out.view(self.M)
+            return out.permute(1, 0, 2).reshape(N, self.M)
+        sizes = [row_range(self.M, g, P)[1] - row_range(self.M, g, P)[0] for g in range(P)]
+        full = torch.cat([out[g, :, :sizes[g]] for g in range(P)], dim=1)  # [N, M]
         return full[0] if vec else full
 
 
