@@ -276,10 +276,10 @@ def _gpu_uuid(dev):
 def batch_records(args, rank, world, dev, steps, warmup):
     """W [28672, 8192] (rows sharded) with X [N, 8192], N in 1..16, both formats
     from tc tiles (the tcgen05 kernel), from batch tiles, from SoA planes (the
-    tcgen05 kernel through 2-D tensor copies) and from SoA planes through the
-    static-workspace entry (the mma.sync kernel);
-    weights rotated over >= 4x L2.  Returns a list of records (us per call,
-    aggregate GB/s)."""
+    tcgen05 kernel through 2-D tensor copies; q4_0 at two columns the TMA pair
+    kernel), from SoA planes through the static-workspace entry, and (N = 1, 2)
+    from GGUF blocks (the TMA kernels); weights rotated over >= 4x L2.
+    Returns a list of records (us per call, aggregate GB/s)."""
     import torch
     import torch.distributed as dist
 
@@ -301,6 +301,8 @@ def batch_records(args, rank, world, dev, steps, warmup):
         tiles = [qg.tile_weights(fmt, q=a, d=b) for a, b in soa]
         # also as tc tiles (the tcgen05 kernel)
         tcs = [qg.tile_weights_tc(q=a, d=b, fmt=fmt) for a, b in soa]
+        # and as GGUF blocks (no repack)
+        aos = [qg.to_aos(fmt, a, b) for a, b in soa]
         nb_tc = max(lib.qgemv_tc_workspace_bytes(rows, K), 16)
         ws_tc = torch.empty(nb_tc, dtype=torch.uint8, device=dev)
         fid = 8 if fmt == "q8_0" else 4
@@ -315,7 +317,8 @@ def batch_records(args, rank, world, dev, steps, warmup):
             it = [0]
 
             def soa_call():
-                # 2..16 columns: the tcgen05 kernel straight from the planes
+                # the tcgen05 kernel straight from the planes (q4_0 at 2
+                # columns: the TMA pair kernel)
                 a, b = soa[it[0] % copies]
                 it[0] += 1
                 _lib.call("qgemv_soa_ws", fid, a.data_ptr(), b.data_ptr(), X.data_ptr(),
@@ -340,15 +343,24 @@ def batch_records(args, rank, world, dev, steps, warmup):
                 _lib.call("qgemv_tc_gemv", fid, t.data_ptr(), rows, K, X.data_ptr(), Y.data_ptr(),
                           N, K, rows, ws_tc.data_ptr(), nb_tc, sp)
 
-            for layout, fn in (("tc", tc_call), ("tiled", tiled_call), ("soa", soa_call),
-                               ("soa_static", soa_static_call)):
+            def aos_call():
+                t = aos[it[0] % copies]
+                it[0] += 1
+                _lib.call("qgemv_q8_0_aos" if fmt == "q8_0" else "qgemv_q4_0_aos",
+                          t.data_ptr(), X.data_ptr(), Y.data_ptr(), rows, K, N, K, rows, sp)
+
+            runs = [("tc", tc_call), ("tiled", tiled_call), ("soa", soa_call),
+                    ("soa_static", soa_static_call)]
+            if N <= 2:
+                runs.append(("ggml_blocks", aos_call))
+            for layout, fn in runs:
                 ms = _timed(torch, dist, dev, world, fn, warmup, steps)
                 per = ms / steps
                 b = alg_bytes(fmt, rows, K, N)
                 out.append({"fmt": fmt, "layout": layout, "N": N, "us_per_call": per * 1e3,
                             "gbps_aggregate": world * b / (per * 1e-3) / 1e9,
                             "copies_rotated": copies})
-        del soa, tiles, tcs, ws_tc, q, d
+        del soa, tiles, tcs, aos, ws_tc, q, d
         torch.cuda.empty_cache()
     return out
 

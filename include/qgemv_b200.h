@@ -119,7 +119,15 @@ QGEMV_API int qgemv_q4_0_soa(const void* q, const void* d, const float* x, float
                              int64_t M, int64_t K, int32_t ncols, int64_t ldx, int64_t ldy,
                              void* stream);
 
-/* Batched SoA calls (ncols >= 2) run on the tensor cores when K % 256 == 0,
+/* Two columns (ncols == 2) of q4_0 SoA planes, or of GGUF blocks of either
+ * format (qgemv_q8_0_aos / qgemv_q4_0_aos), with K % 256 == 0,
+ * 256 <= K <= 16384, x 16-byte aligned and ldx a multiple of 4, run on the
+ * single-column TMA kernel in its two-column form: the weights stream once
+ * for both columns, no workspace is used (a workspace passed in is left
+ * untouched), and each column is bit-identical to a one-column call on it
+ * whenever every 32-element block of both columns is finite with its largest
+ * magnitude between 2^-74 and 2^100 (otherwise within the same 1e-5 bound).
+ * Other batched SoA calls (ncols >= 2) run on the tensor cores when K % 256 == 0,
  * K <= 2^20 and q, d are 16-byte aligned; they need a workspace (the
  * activations re-laid as fp16 hi/lo pairs, about 4 * K * min(ncols, 16)
  * bytes).  qgemv_q8_0_soa / qgemv_q4_0_soa keep one per (device, stream),

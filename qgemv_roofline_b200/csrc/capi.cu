@@ -190,9 +190,10 @@ int gemv_entry(int fmt, bool aos, const void* q, const void* d, const float* x, 
   if (!aos) {
     // the tensor-core batch kernels need a workspace: the caller's, or one
     // cached for this stream
+    // (two columns on the TMA path need none)
     GemvCall probe = c;
     probe.N = std::min(ncols, 16);
-    if (probe.N >= 2 && mma_eligible(probe)) {
+    if (probe.N >= 2 && mma_eligible(probe) && !tma_pair_taken(fmt, false, c)) {
       const size_t need = soa_batch_workspace(probe, allow_tc);
       if (caller_ws) {
         if (!ws || ws_bytes < need)

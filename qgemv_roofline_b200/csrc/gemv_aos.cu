@@ -225,7 +225,8 @@ int gemv_aos(int fmt, const GemvCall& c, cudaStream_t st) {
     part.N = std::min(16, c.N - n0);
     part.x = c.x + (int64_t)n0 * c.ldx;
     part.y = c.y + (int64_t)n0 * c.ldy;
-    rc = fmt == 8 ? dispatch_aos<8>(part, dev, st) : dispatch_aos<4>(part, dev, st);
+    rc = part.N == 2 ? gemv_tma_pair(fmt, true, part, st) : -1;
+    if (rc == -1) rc = fmt == 8 ? dispatch_aos<8>(part, dev, st) : dispatch_aos<4>(part, dev, st);
     if (rc) return rc;
   }
   return OK;

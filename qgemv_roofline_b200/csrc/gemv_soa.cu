@@ -247,7 +247,8 @@ int gemv_soa(int fmt, const GemvCall& c, cudaStream_t st) {
     part.x = c.x + (int64_t)n0 * c.ldx;
     part.y = c.y + (int64_t)n0 * c.ldy;
     rc = -1;
-    if (part.N >= 2 && part.ws) rc = gemv_soa_tc(fmt, part, st);  // tcgen05 batch kernel
+    if (part.N == 2) rc = gemv_tma_pair(fmt, false, part, st);  // q4_0: dp4a, weights once
+    if (rc == -1 && part.N >= 2 && part.ws) rc = gemv_soa_tc(fmt, part, st);  // tcgen05 batch kernel
     if (rc == -1 && part.N >= 2 && part.ws) rc = gemv_soa_mma(fmt, part, st);  // mma.sync
     if (rc == -1) rc = fmt == 8 ? dispatch_soa<8>(part, dev, st) : dispatch_soa<4>(part, dev, st);
     if (rc) return rc;

@@ -334,33 +334,53 @@ __device__ __forceinline__ void make_planes_smem(uint32_t xb, int lane, XPlanes&
 // the -8 offset).  wq: the block's quant words (q8_0: 8 words of int8, word w
 // = elements 4w..4w+3; q4_0: 4 words, word t = elements 4t..4t+3 in the low
 // nibbles and 16+4t.. in the high nibbles).
+// q4_0 quant words split into nibble words: wm[t] = low nibbles of word t
+// (elements 4t..4t+3), wm[4 + t] = its high nibbles in place (16 * n of
+// elements 16+4t..16+4t+3).
+__device__ __forceinline__ void q4_masks(const uint32_t* wq, uint32_t (&wm)[8]) {
+#pragma unroll
+  for (int t4 = 0; t4 < 4; ++t4) {
+    wm[t4] = wq[t4] & 0x0F0F0F0Fu;
+    wm[t4 + 4] = wq[t4] & 0xF0F0F0F0u;
+  }
+}
+
+// block_sums for q4_0 from the nibble words of q4_masks.
+__device__ __forceinline__ void block_sums_q4m(const uint32_t (&wm)[8], const XPlanes& xp, int& lo,
+                                               int& hi) {
+  uint32_t L0 = 0u, L1 = 0u, H0 = 0u, H1 = 0u;
+  int L2 = 0, H2 = 0;
+#pragma unroll
+  for (int t4 = 0; t4 < 4; ++t4) {
+    L0 = dp4a_uu(wm[t4], xp.pl[t4][0], L0);
+    L1 = dp4a_uu(wm[t4], xp.pl[t4][1], L1);
+    L2 = dp4a_us(wm[t4], xp.pl[t4][2], L2);
+    H0 = dp4a_uu(wm[t4 + 4], xp.pl[t4 + 4][0], H0);
+    H1 = dp4a_uu(wm[t4 + 4], xp.pl[t4 + 4][1], H1);
+    H2 = dp4a_us(wm[t4 + 4], xp.pl[t4 + 4][2], H2);
+  }
+  // 16 * sum n X per plane (all below 2^21 in magnitude); the two low planes
+  // fold in int32 (< 2^30), plane 2 stays apart
+  const int S0 = (int)((L0 << 4) + H0);
+  const int S1 = (int)((L1 << 4) + H1);
+  lo = (S1 << 8) + S0;
+  hi = (L2 << 4) + H2;
+}
+
 template <int FMT>
 __device__ __forceinline__ void block_sums(const uint32_t* wq, const XPlanes& xp, int& lo, int& hi) {
+  if (FMT == 4) {
+    uint32_t wm[8];
+    q4_masks(wq, wm);
+    block_sums_q4m(wm, xp, lo, hi);
+    return;
+  }
   int S0 = 0, S1 = 0, S2 = 0;
-  if (FMT == 8) {
 #pragma unroll
-    for (int w = 0; w < 8; ++w) {
-      S0 = dp4a_su(wq[w], xp.pl[w][0], S0);
-      S1 = dp4a_su(wq[w], xp.pl[w][1], S1);
-      S2 = dp4a_ss(wq[w], xp.pl[w][2], S2);
-    }
-  } else {
-    uint32_t L0 = 0u, L1 = 0u, H0 = 0u, H1 = 0u;
-    int H2 = 0;
-#pragma unroll
-    for (int t4 = 0; t4 < 4; ++t4) {
-      const uint32_t lo = wq[t4] & 0x0F0F0F0Fu, hi = wq[t4] & 0xF0F0F0F0u;
-      L0 = dp4a_uu(lo, xp.pl[t4][0], L0);
-      L1 = dp4a_uu(lo, xp.pl[t4][1], L1);
-      S2 = dp4a_us(lo, xp.pl[t4][2], S2);
-      H0 = dp4a_uu(hi, xp.pl[t4 + 4][0], H0);
-      H1 = dp4a_uu(hi, xp.pl[t4 + 4][1], H1);
-      H2 = dp4a_us(hi, xp.pl[t4 + 4][2], H2);
-    }
-    // 16 * sum n X per plane (all below 2^21 in magnitude)
-    S0 = (int)((L0 << 4) + H0);
-    S1 = (int)((L1 << 4) + H1);
-    S2 = (S2 << 4) + H2;
+  for (int w = 0; w < 8; ++w) {
+    S0 = dp4a_su(wq[w], xp.pl[w][0], S0);
+    S1 = dp4a_su(wq[w], xp.pl[w][1], S1);
+    S2 = dp4a_ss(wq[w], xp.pl[w][2], S2);
   }
   // the two low planes fold in int32 (< 2^30); plane 2 stays apart
   lo = (S1 << 8) + S0;
@@ -522,6 +542,9 @@ struct TmaArgs {
   // claim (each CTA makes exactly one failing claim) resets the counter.
   unsigned* tctr;
   FuseArgs f;  // all-gather of y into peer buffers (f.nranks == 0: none)
+  // Column strides (elements) of x and y when the kernel runs NC > 1 columns:
+  // column n of x starts at x + n * ldx (16-byte aligned), of y at y + n * ldy.
+  int64_t ldx, ldy;
 };
 
 __device__ __forceinline__ unsigned ld_acquire_sys(const unsigned* p) {
@@ -570,9 +593,15 @@ __host__ __device__ constexpr int slices_of(int K) {
 
 // KF != 0: the kernel is compiled for K == KF (the row strides of the stage
 // become immediate offsets of the shared-memory loads).
-template <int FMT, int MODE, int R, int CONSUMERS, bool AOS = false, int KF = 0>
+// NC: columns of x per launch (1, or 2 in MODE 1).  With two, every lane keeps
+// the planes of its x block for both columns and runs each quant word (and,
+// for q4_0, its two nibble masks) against both: the weights stream once for
+// the pair, and each column's result is bit-identical to a one-column call.
+template <int FMT, int MODE, int R, int CONSUMERS, bool AOS = false, int KF = 0, int NC = 1>
 __global__ void __launch_bounds__(tma_threads(CONSUMERS), tma_ctas_per_sm(CONSUMERS))
 k_gemv_tma(const TmaArgs p) {
+  static_assert(NC == 1 || (NC == 2 && MODE == 1), "two columns: exact mode only");
+  static_assert(R * NC <= 32, "one reduced value per lane at most");
   using F = Fmt<FMT>;
   constexpr int EPC = F::ELEMS_PER_CHUNK;
   extern __shared__ __align__(128) uint8_t sm[];
@@ -590,7 +619,7 @@ k_gemv_tma(const TmaArgs p) {
   const int QB = AOS ? (K / QK) * F::BLOCK_BYTES : K / F::ROW_DIV;
   const int DB = AOS ? 0 : K / 16;
   const int STG = TR * (QB + DB);
-  float* part = reinterpret_cast<float*>(sm + (size_t)S * STG);  // [S][TR][KS]
+  float* part = reinterpret_cast<float*>(sm + (size_t)S * STG);  // [S][TR][KS][NC]
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int a = (int)((int64_t)p.M * blockIdx.x / gridDim.x);
   const int nrows = (int)((int64_t)p.M * (blockIdx.x + 1) / gridDim.x) - a;
@@ -633,8 +662,9 @@ k_gemv_tma(const TmaArgs p) {
     const unsigned nclaims = (unsigned)(max(0, T - 2 * G) + G);  // each CTA fails once
     bool have_claim = false;
     unsigned claim = 0u;
-    if (p.xstage && lane == 0)  // x into L2 while the previous kernel drains (a hint only)
-      asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p.x), "r"((uint32_t)K * 4u)
+    if (p.xstage && lane < NC)  // x into L2 while the previous kernel drains (a hint only)
+      asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p.x + lane * p.ldx),
+                   "r"((uint32_t)K * 4u)
                    : "memory");
     for (int t = 0; ok && (end_t < 0 || t < end_t + S); ++t) {
       // Tile 0 (weights only) is prefetched before the dependency wait, the
@@ -650,11 +680,15 @@ k_gemv_tma(const TmaArgs p) {
           // last stage, issued before any further weight tile; the stage
           // receives its first tile once every consumer has read x
           if (lane == 0) {
+            // column n of x lands at byte n * K * 4 of the stage
             const uint32_t bar = saddr(&xfull);
             asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar),
-                         "r"((uint32_t)K * 4u)
+                         "r"((uint32_t)(K * 4 * NC))
                          : "memory");
-            bulk_g2s(saddr(sm + (size_t)(S - 1) * STG), p.x, (uint32_t)K * 4u, bar);
+#pragma unroll
+            for (int n = 0; n < NC; ++n)
+              bulk_g2s(saddr(sm + (size_t)(S - 1) * STG + (size_t)n * K * 4), p.x + n * p.ldx,
+                       (uint32_t)K * 4u, bar);
           }
           x_issued = true;
         }
@@ -693,12 +727,16 @@ k_gemv_tma(const TmaArgs p) {
         ok = __all_sync(0xffffffffu, mbar_wait(saddr(&empty[s]), (cyc - 1u) & 1u, &abort_flag));
         if (!ok) break;
         const int fr0 = fin_r0[s], fnr = fin_nr[s];
-        const float* ps = part + (size_t)s * TR * KS;
+        const float* ps = part + (size_t)s * TR * KS * NC;
         for (int i = lane; i < fnr; i += 32) {
-          float v = 0.0f;
-          for (int k = 0; k < KS; ++k) v += ps[i * KS + k];
-          p.y[fr0 + i] = v;
-          for (int k = 0; k < p.f.npeer; ++k) p.f.peer_y[k][fr0 + i] = v;  // NVLink stores
+#pragma unroll
+          for (int n = 0; n < NC; ++n) {
+            float v = 0.0f;
+            for (int k = 0; k < KS; ++k) v += ps[(i * KS + k) * NC + n];
+            p.y[n * p.ldy + fr0 + i] = v;
+            if (NC == 1)
+              for (int k = 0; k < p.f.npeer; ++k) p.f.peer_y[k][fr0 + i] = v;  // NVLink stores
+          }
         }
         __syncwarp();
         fin_nr[s] = 0;
@@ -790,9 +828,11 @@ k_gemv_tma(const TmaArgs p) {
   const uint32_t aos_sel = aos_odd ? 0x7654u : 0x5432u;
 
   float xr[MODE == 0 ? EPC : 1];
-  XPlanes xp;
-  XScale xq{};        // MODE 1: the scale 2^t of the lane's x block
-  bool fast = false;  // the fast form holds for every lane of the warp
+  XPlanes xps[NC];    // MODE 1: the planes of the lane's x block, per column
+  XPlanes& xp = xps[0];
+  XScale xqs[NC] = {};  // MODE 1: the scale 2^t of the lane's x block, per column
+  XScale& xq = xqs[0];
+  bool fast = false;  // the fast form holds for every lane of the warp (and column)
   XQ81 x8{};          // MODE 2: the lane's x block as int8 quants
   if (MODE == 0) {
     asm volatile("griddepcontrol.wait;" ::: "memory");
@@ -812,31 +852,42 @@ k_gemv_tma(const TmaArgs p) {
     // wait); every consumer warp releases the stage once it has converted x
     const bool got = __all_sync(0xffffffffu, mbar_wait(saddr(&xfull), 0u, &abort_flag));
     const uint32_t xb = saddr(sm) + (uint32_t)((S - 1) * STG + cidx * 128);
-    if (MODE == 2) {
-      if (got && cval) make_q81_smem(xb, lane, x8);  // lanes past K: zero quants, never stored
-    } else if (got && cval) {
-      make_planes_smem(xb, lane, xp);
-    } else {
-      for (int w = 0; w < 8; ++w)
-        for (int pl = 0; pl < NPL; ++pl) xp.pl[w][pl] = 0u;
-      xp.e = -149;
-      xp.bias = 0.0f;
-      xp.finite = true;
+#pragma unroll
+    for (int n = 0; n < NC; ++n) {
+      if (MODE == 2) {
+        if (got && cval) make_q81_smem(xb, lane, x8);  // lanes past K: zero quants, never stored
+      } else if (got && cval) {
+        make_planes_smem(xb + (uint32_t)(n * K * 4), lane, xps[n]);
+      } else {
+        for (int w = 0; w < 8; ++w)
+          for (int pl = 0; pl < NPL; ++pl) xps[n].pl[w][pl] = 0u;
+        xps[n].e = -149;
+        xps[n].bias = 0.0f;
+        xps[n].finite = true;
+      }
     }
     __syncwarp();
     if (lane == 0)
       asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(saddr(&xempty)) : "memory");
     if (MODE == 1) {
-      xq = x_scale<FMT>(xp);
-      fast = __all_sync(0xffffffffu, !cval || xq.fast);
+      bool f = true;
+#pragma unroll
+      for (int n = 0; n < NC; ++n) {
+        xqs[n] = x_scale<FMT>(xps[n]);
+        f = f && xqs[n].fast;
+      }
+      fast = __all_sync(0xffffffffu, !cval || f);
     }
   } else {
     // Pull the lane's 128 bytes of x into L2 while the previous kernel
     // finishes (a prefetch consumes no data, so it may precede the wait; the
     // previous kernel's own writes to x still land in L2 before the loads).
     if (cval) {
-      asm volatile("prefetch.global.L2 [%0];" ::"l"(p.x + cidx * 32));
-      asm volatile("prefetch.global.L2 [%0];" ::"l"(p.x + cidx * 32 + 31));
+#pragma unroll
+      for (int n = 0; n < NC; ++n) {
+        asm volatile("prefetch.global.L2 [%0];" ::"l"(p.x + n * p.ldx + cidx * 32));
+        asm volatile("prefetch.global.L2 [%0];" ::"l"(p.x + n * p.ldx + cidx * 32 + 31));
+      }
     }
     asm volatile("griddepcontrol.wait;" ::: "memory");  // x may be the previous kernel's y
     if (p.f.sig_in) {
@@ -855,16 +906,19 @@ k_gemv_tma(const TmaArgs p) {
         if (r || abort_flag || clock64() - t0 > lim) break;
       }
     }
-    if (MODE == 2) {
-      if (cval) make_q81(p.x + cidx * 32, x8);  // lanes past K: zero quants, never stored
-    } else if (cval) {
-      make_planes(p.x + cidx * 32, xp);
-    } else {
-      for (int w = 0; w < 8; ++w)
-        for (int pl = 0; pl < NPL; ++pl) xp.pl[w][pl] = 0u;
-      xp.e = -149;
-      xp.bias = 0.0f;
-      xp.finite = true;
+#pragma unroll
+    for (int n = 0; n < NC; ++n) {
+      if (MODE == 2) {
+        if (cval) make_q81(p.x + cidx * 32, x8);  // lanes past K: zero quants, never stored
+      } else if (cval) {
+        make_planes(p.x + n * p.ldx + cidx * 32, xps[n]);
+      } else {
+        for (int w = 0; w < 8; ++w)
+          for (int pl = 0; pl < NPL; ++pl) xps[n].pl[w][pl] = 0u;
+        xps[n].e = -149;
+        xps[n].bias = 0.0f;
+        xps[n].finite = true;
+      }
     }
     // X_j = x_j 2^(22-e): the block's dot is its integer dot times 2^(e-22)
     // (q4_0: times 2^-4 more).  With one factor (d * 2^t exact for every fp16
@@ -872,8 +926,13 @@ k_gemv_tma(const TmaArgs p) {
     // product as (d * F) * 2^t; otherwise two exact factors, so the product
     // only rounds where the true value itself under- or overflows.
     if (MODE == 1) {
-      xq = x_scale<FMT>(xp);
-      fast = __all_sync(0xffffffffu, !cval || xq.fast);  // lanes past K compute nothing
+      bool f = true;
+#pragma unroll
+      for (int n = 0; n < NC; ++n) {
+        xqs[n] = x_scale<FMT>(xps[n]);
+        f = f && xqs[n].fast;
+      }
+      fast = __all_sync(0xffffffffu, !cval || f);  // lanes past K compute nothing
     }
   }
 
@@ -886,11 +945,11 @@ k_gemv_tma(const TmaArgs p) {
     if (nr <= 0) break;
     const uint8_t* st = sm + (size_t)s * STG;
     const uint8_t* sd = st + (size_t)TR * QB;
-    float* ps = part + (size_t)s * TR * KS;
+    float* ps = part + (size_t)s * TR * KS * NC;
     for (int r0 = rg * R; r0 < nr; r0 += RG * R) {
-      float acc[R];
+      float acc[R * NC];  // acc[r * NC + n]: row r0 + r, column n
 #pragma unroll
-      for (int r = 0; r < R; ++r) acc[r] = 0.0f;
+      for (int i = 0; i < R * NC; ++i) acc[i] = 0.0f;
       if (cval) {
         // Rows r0 + r >= nr of a partial last tile read stale (in-bounds)
         // bytes of the stage; their results are never stored, and rows never
@@ -978,10 +1037,21 @@ k_gemv_tma(const TmaArgs p) {
             }
             if (MODE == 2) {
               acc[r] = block_q81<FMT>(wq, x8, dvr);
-            } else {
+            } else if (NC == 1) {
               int lo, hi;
               block_sums<FMT>(wq, xp, lo, hi);
               acc[r] = block_value<FMT, FAST>(lo, hi, dvr, xq, xp);
+            } else {
+              // the same quant words (q4_0: masked once) against each column's planes
+              uint32_t wm[8];
+              if (FMT == 4) q4_masks(wq, wm);
+#pragma unroll
+              for (int n = 0; n < NC; ++n) {
+                int lo, hi;
+                if (FMT == 4) block_sums_q4m(wm, xps[n], lo, hi);
+                else block_sums<FMT>(wq, xps[n], lo, hi);
+                acc[r * NC + n] = block_value<FMT, FAST>(lo, hi, dvr, xqs[n], xps[n]);
+              }
             }
           }
           };
@@ -989,9 +1059,10 @@ k_gemv_tma(const TmaArgs p) {
           else rows(std::true_type{});
         }
       }
-      const float v = reduce_rows<R>(acc, lane);
-      const int r = row_of_lane<R>(lane);
-      if ((lane & (32 / R - 1)) == 0 && r0 + r < nr) ps[(r0 + r) * KS + ks] = v;
+      const float v = reduce_rows<R * NC>(acc, lane);
+      const int rn = row_of_lane<R * NC>(lane);  // r * NC + n
+      const int r = rn / NC, n = rn % NC;
+      if ((lane & (32 / (R * NC) - 1)) == 0 && r0 + r < nr) ps[((r0 + r) * KS + ks) * NC + n] = v;
     }
     __syncwarp();
     if (lane == 0)
@@ -1405,7 +1476,7 @@ std::map<PlanKey, TmaPlan> g_plans;
 
 // Tile rows, stages and grid for one (kernel, device, M, K); cached, so a
 // launch costs one map lookup besides the launch itself.
-template <int FMT, int MODE, int R, int CONSUMERS, bool AOS = false>
+template <int FMT, int MODE, int R, int CONSUMERS, bool AOS = false, int NC = 1>
 int plan_tma(const void* kern, int M, int K, const DeviceInfo& dev, TmaPlan* out) {
   const PlanKey key{kern, dev.device, M, K};
   {
@@ -1434,16 +1505,19 @@ int plan_tma(const void* kern, int M, int K, const DeviceInfo& dev, TmaPlan* out
                     (int)fa.sharedSizeBytes;
   const int tile_target = ctas_per_sm == 1 ? 32 * 1024 : 36 * 1024;
   int TR = unit * std::max(1, tile_target / (unit * row_bytes));
-  int S = std::min(MAX_STAGES, avail / (TR * row_bytes + TR * KS * 4));
+  // per stage: the tile, and the partial sums of its rows per slice and column
+  const int part_row = KS * 4 * NC;
+  int S = std::min(MAX_STAGES, avail / (TR * row_bytes + TR * part_row));
   while (S < 2 && TR > unit) {  // very long rows: fewer rows per tile
     TR -= unit;
-    S = std::min(MAX_STAGES, avail / (TR * row_bytes + TR * KS * 4));
+    S = std::min(MAX_STAGES, avail / (TR * row_bytes + TR * part_row));
   }
   if (S < 2) return -1;
-  if (MODE != 0 && TR * row_bytes < K * 4) {
+  const int xbytes = K * 4 * NC;  // x, every column
+  if (MODE != 0 && TR * row_bytes < xbytes) {
     // x is staged in a ring stage: more rows per tile, if three stages still fit
-    const int TRx = unit * ((K * 4 + unit * row_bytes - 1) / (unit * row_bytes));
-    const int Sx = std::min(MAX_STAGES, avail / (TRx * row_bytes + TRx * KS * 4));
+    const int TRx = unit * ((xbytes + unit * row_bytes - 1) / (unit * row_bytes));
+    const int Sx = std::min(MAX_STAGES, avail / (TRx * row_bytes + TRx * part_row));
     if (Sx >= 3) {
       TR = TRx;
       S = Sx;
@@ -1453,7 +1527,7 @@ int plan_tma(const void* kern, int M, int K, const DeviceInfo& dev, TmaPlan* out
   pl.TR = TR;
   pl.S = S;
   pl.KS = KS;
-  pl.smem = (size_t)S * (TR * row_bytes + TR * KS * 4);
+  pl.smem = (size_t)S * (TR * row_bytes + TR * part_row);
   pl.grid = std::max(1, std::min(dev.sms * ctas_per_sm, (M + TR - 1) / TR));
   std::lock_guard<std::mutex> lk(g_plan_mu);
   g_plans[key] = pl;
@@ -1461,14 +1535,14 @@ int plan_tma(const void* kern, int M, int K, const DeviceInfo& dev, TmaPlan* out
   return OK;
 }
 
-template <int FMT, int MODE, int R, int CONSUMERS, bool AOS = false, int KF = 0>
+template <int FMT, int MODE, int R, int CONSUMERS, bool AOS = false, int KF = 0, int NC = 1>
 int launch_tma(const GemvCall& c, const DeviceInfo& dev, cudaStream_t st) {
   if (KF != 0 && c.K != KF) return -1;
-  auto kern = k_gemv_tma<FMT, MODE, R, CONSUMERS, AOS, KF>;
+  auto kern = k_gemv_tma<FMT, MODE, R, CONSUMERS, AOS, KF, NC>;
   const int K = (int)c.K, M = (int)c.M;
   TmaPlan pl;
-  if (int rc = plan_tma<FMT, MODE, R, CONSUMERS, AOS>(reinterpret_cast<const void*>(kern), M, K,
-                                                       dev, &pl))
+  if (int rc = plan_tma<FMT, MODE, R, CONSUMERS, AOS, NC>(reinterpret_cast<const void*>(kern), M,
+                                                           K, dev, &pl))
     return rc;
   const int grid = c.grid_override > 0 ? c.grid_override : pl.grid;
   using F = Fmt<FMT>;
@@ -1477,7 +1551,8 @@ int launch_tma(const GemvCall& c, const DeviceInfo& dev, cudaStream_t st) {
   // x by one bulk copy per CTA: measured 1.8-2.6 us less per call than
   // per-lane loads of x (every warp of every CTA reading the same 16 KB at
   // the same moment), from 4096 to 98304 rows of K = 4096
-  const int xstage = MODE != 0 && c.f.nranks == 0 && pl.S >= 3 && (int64_t)K * 4 <= stage_bytes;
+  const int xstage =
+      MODE != 0 && c.f.nranks == 0 && pl.S >= 3 && (int64_t)K * 4 * NC <= stage_bytes;
   TmaArgs a{static_cast<const uint8_t*>(c.q), static_cast<const unsigned short*>(c.d), c.x, c.y,
             M, K, pl.TR, pl.S, pl.KS, xstage,
             // claimed tiles with two CTAs per SM (measured 2-5 % less per call
@@ -1488,7 +1563,7 @@ int launch_tma(const GemvCall& c, const DeviceInfo& dev, cudaStream_t st) {
             // CTA without a first tile would claim before its dependency wait.
             CONSUMERS < 16 && grid <= (M + pl.TR - 1) / pl.TR ? tile_counter(dev.device, st)
                                                              : nullptr,
-            c.f};
+            c.f, NC > 1 ? c.ldx : (int64_t)K, NC > 1 ? c.ldy : (int64_t)M};
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(grid);
   cfg.blockDim = dim3(tma_threads(CONSUMERS));
@@ -1618,6 +1693,53 @@ int gemv_soa_tma(int fmt, const GemvCall& c, cudaStream_t st) {
                : launch_tma<8, 1, 4, 16, false, 4096>(c, dev, st);
   if (rc == -1 && small) rc = launch_tma<8, 1, 4, 8>(c, dev, st);
   if (rc == -1) rc = launch_tma<8, 1, 4, 16>(c, dev, st);
+  return rc;
+}
+
+bool tma_pair_eligible(const GemvCall& c) {
+  // tma_eligible's shape and alignment rules, and column 1 of x 16-byte
+  // aligned too (ldx a multiple of 4 floats); exact activations, no fused
+  // all-gather
+  if (c.N != 2 || c.act != 0 || c.f.nranks != 0 || c.ldx % 4 != 0) return false;
+  GemvCall one = c;
+  one.N = 1;
+  return tma_eligible(one);
+}
+
+// Which two-column calls the pair kernel takes.  Its time is set by the
+// integer pipe (48 dp4a per 32-weight block-row for the two columns), so it
+// pays where the alternative is slower: q4_0 on SoA planes (W [28672, 8192]:
+// 41.9 us against 49.7 us on tcgen05) and GGUF blocks (whose other batch
+// kernel streams registers).  q8_0 on SoA planes stays on tcgen05 (45.5 us
+// against 49.2 us).
+bool tma_pair_taken(int fmt, bool aos, const GemvCall& c) {
+  return (aos || fmt == 4) && tma_pair_eligible(c);
+}
+
+// Two columns in one launch (SoA planes or GGUF blocks): the weights stream
+// once for both.  Consumers per SM and rows per pass follow the one-column
+// rules (one CTA of 16 consumer warps for long streams, two of 8 below),
+// with 4 rows per pass (8 reduced values per lane, as q4_0's 8 rows of one
+// column).  -1 when the call is not taken (tma_pair_taken).
+int gemv_tma_pair(int fmt, bool aos, const GemvCall& c, cudaStream_t st) {
+  if (!tma_pair_taken(fmt, aos, c)) return -1;
+  DeviceInfo dev;
+  if (int rc = current_device_info(dev)) return rc;
+  const int64_t wbytes = aos ? c.M * (c.K / 32) * (fmt == 8 ? 34 : 18)
+                             : c.M * (c.K / (fmt == 8 ? 1 : 2) + c.K / 16);
+  const bool big = wbytes >= ((int64_t)(fmt == 8 ? 256 : 150) << 20);
+  int rc = -1;
+  if (fmt == 4) {
+    if (!big) rc = aos ? launch_tma<4, 1, 4, 8, true, 0, 2>(c, dev, st)
+                       : launch_tma<4, 1, 4, 8, false, 0, 2>(c, dev, st);
+    if (rc == -1) rc = aos ? launch_tma<4, 1, 4, 16, true, 0, 2>(c, dev, st)
+                           : launch_tma<4, 1, 4, 16, false, 0, 2>(c, dev, st);
+    return rc;
+  }
+  if (!big) rc = aos ? launch_tma<8, 1, 4, 8, true, 0, 2>(c, dev, st)
+                     : launch_tma<8, 1, 4, 8, false, 0, 2>(c, dev, st);
+  if (rc == -1) rc = aos ? launch_tma<8, 1, 4, 16, true, 0, 2>(c, dev, st)
+                         : launch_tma<8, 1, 4, 16, false, 0, 2>(c, dev, st);
   return rc;
 }
 

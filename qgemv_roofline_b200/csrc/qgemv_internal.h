@@ -70,6 +70,13 @@ bool tma_eligible(const GemvCall& c);
 int gemv_soa_tma_mode(int fmt, int mode, const GemvCall& c, cudaStream_t st);
 // GGUF-layout blocks on the TMA path; -1 when the shape is not eligible.
 int gemv_aos_tma(int fmt, const GemvCall& c, cudaStream_t st);
+// Two columns (N == 2) on the TMA path in one launch, SoA planes or GGUF
+// blocks (exact activations; x columns 16-byte aligned); -1 when the call is
+// not taken (tma_pair_taken: q4_0 planes and GGUF blocks).  Needs no
+// workspace.
+bool tma_pair_eligible(const GemvCall& c);
+bool tma_pair_taken(int fmt, bool aos, const GemvCall& c);
+int gemv_tma_pair(int fmt, bool aos, const GemvCall& c, cudaStream_t st);
 int read_device_error(int clear, cudaStream_t st, int* out);
 // Persistent decode stack: a sequence of single-column SoA GEMVs in one
 // cooperative launch (GEMV j reads GEMV j-1's output).  Outputs are 8-byte

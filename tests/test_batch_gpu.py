@@ -293,11 +293,12 @@ def test_tiled_gemv(fmt, M, K, N):
 
 
 @pytest.mark.parametrize("fmt", ["q8_0", "q4_0"])
-@pytest.mark.parametrize("M,N", [(2000, 12), (4099, 2), (300, 16), (129, 5)])
+@pytest.mark.parametrize("M,N", [(2000, 12), (4099, 3), (300, 16), (129, 5)])
 def test_soa_batch_matches_tc_tiles(fmt, M, N):
-    """Batched SoA calls run the tcgen05 kernel straight from the planes (2-D
-    tensor copies, 128-byte swizzle): the same smem image as the tc tiles and
-    the same arithmetic in the same order, so identical bits."""
+    """Batched SoA calls of 3..16 columns run the tcgen05 kernel straight from
+    the planes (2-D tensor copies, 128-byte swizzle): the same smem image as
+    the tc tiles and the same arithmetic in the same order, so identical bits.
+    (Two columns run the TMA pair kernel: tests/test_pair_gpu.py.)"""
     K = 8192
     q, d, X = make(fmt, M, K, N, seed=77 + M)
     qt, dt = planes(q, d)

@@ -2,7 +2,8 @@
 
 The benchmark times the single-column kernels at W [98304, 4096] (SoA planes
 and GGUF blocks), the batch-tile and SoA-plane tensor-core kernels at
-W [28672, 8192] with 16 columns, and the 7B decode layer.  Here every output
+W [28672, 8192] with 16 columns, two columns there (SoA planes and GGUF
+blocks), and the 7B decode layer.  Here every output
 row of those calls is compared with the reference's float64 dequant-matvec
 (src/bench.cu:75-111: the reference's own C++ built into oracle/_ref, run on
 all host threads; the numpy restatement in chunks when it was not built),
@@ -134,6 +135,15 @@ def test_small_batch_28672x8192_every_row(fmt):
     assert_all_rows(Yt.cpu().numpy(), y_ref, wn, Xh, "batch tiles, 16 columns")
     Ys = qg.qgemv(fmt, q, d, X)
     assert_all_rows(Ys.cpu().numpy(), y_ref, wn, Xh, "SoA planes, 16 columns")
+    # two columns: SoA planes (q4_0: the TMA pair kernel; q8_0: tcgen05) and
+    # GGUF blocks (the TMA pair kernel)
+    Yp = qg.qgemv(fmt, q, d, X[6:8])
+    assert_all_rows(Yp.cpu().numpy(), y_ref[6:8], wn, Xh[6:8], "SoA planes, 2 columns")
+    Ya = qg.qgemv_aos(fmt, qg.to_aos(fmt, q, d), X[6:8])
+    assert_all_rows(Ya.cpu().numpy(), y_ref[6:8], wn, Xh[6:8], "GGUF blocks, 2 columns")
+    if fmt == "q4_0":
+        assert torch.equal(Ya, Yp)  # the same kernel arithmetic on the same rows
+    del Ya
     Y2 = qg.qgemv_tiled(fmt, tiles, M, K, 2.0 * X)
     assert torch.equal(Y2, 2.0 * Yt)  # power-of-two scaling is exact end to end
     Y5 = qg.qgemv_tiled(fmt, tiles, M, K, X[3:8])
