@@ -1717,10 +1717,11 @@ bool tma_pair_taken(int fmt, bool aos, const GemvCall& c) {
 }
 
 // Two columns in one launch (SoA planes or GGUF blocks): the weights stream
-// once for both.  Consumers per SM and rows per pass follow the one-column
-// rules (one CTA of 16 consumer warps for long streams, two of 8 below),
-// with 4 rows per pass (8 reduced values per lane, as q4_0's 8 rows of one
-// column).  -1 when the call is not taken (tma_pair_taken).
+// once for both.  GGUF blocks follow the one-column rule for CTAs per SM (one
+// CTA of 16 consumer warps for long streams, two of 8 below) with 4 rows per
+// pass (8 reduced values per lane, as q4_0's 8 rows of one column); q4_0
+// planes have their own measured rule below.  -1 when the call is not taken
+// (tma_pair_taken).
 int gemv_tma_pair(int fmt, bool aos, const GemvCall& c, cudaStream_t st) {
   if (!tma_pair_taken(fmt, aos, c)) return -1;
   DeviceInfo dev;
@@ -1729,6 +1730,18 @@ int gemv_tma_pair(int fmt, bool aos, const GemvCall& c, cudaStream_t st) {
                              : c.M * (c.K / (fmt == 8 ? 1 : 2) + c.K / 16);
   const bool big = wbytes >= ((int64_t)(fmt == 8 ? 256 : 150) << 20);
   int rc = -1;
+  if (fmt == 4 && !aos) {
+    // q4_0 planes, measured per (rows per pass, CTAs per SM), same bits for
+    // all: K >= 8192 one CTA of 16 with 4 rows (28672 x 8192: 39.4 us against
+    // 41.5 with two CTAs of 8); long K = 4096 streams one CTA with 8 rows
+    // (70000 x 4096: 45.4 us against 50.2 with 4 rows); shorter ones two CTAs
+    // with 4 rows (11008 x 4096: 13.1-13.3 us, every variant within 0.8 us)
+    if (c.K >= 8192) rc = launch_tma<4, 1, 4, 16, false, 0, 2>(c, dev, st);
+    else if (big) rc = launch_tma<4, 1, 8, 16, false, 0, 2>(c, dev, st);
+    else rc = launch_tma<4, 1, 4, 8, false, 0, 2>(c, dev, st);
+    if (rc == -1) rc = launch_tma<4, 1, 4, 16, false, 0, 2>(c, dev, st);
+    return rc;
+  }
   if (fmt == 4) {
     if (!big) rc = aos ? launch_tma<4, 1, 4, 8, true, 0, 2>(c, dev, st)
                        : launch_tma<4, 1, 4, 8, false, 0, 2>(c, dev, st);
