@@ -1709,7 +1709,7 @@ bool tma_pair_eligible(const GemvCall& c) {
 // Which two-column calls the pair kernel takes.  Its time is set by the
 // integer pipe (48 dp4a per 32-weight block-row for the two columns), so it
 // pays where the alternative is slower: q4_0 on SoA planes (W [28672, 8192]:
-// 41.9 us against 49.7 us on tcgen05) and GGUF blocks (whose other batch
+// 39.4 us against 49.7 us on tcgen05) and GGUF blocks (whose other batch
 // kernel streams registers).  q8_0 on SoA planes stays on tcgen05 (45.5 us
 // against 49.2 us).
 bool tma_pair_taken(int fmt, bool aos, const GemvCall& c) {
