@@ -1710,18 +1710,15 @@ bool tma_pair_eligible(const GemvCall& c) {
 // integer pipe (48 dp4a per 32-weight block-row for the two columns), so it
 // pays where the alternative is slower: q4_0 on SoA planes (W [28672, 8192]:
 // 39.4 us against 49.7 us on tcgen05) and GGUF blocks (whose other batch
-// kernel streams registers).  q8_0 on SoA planes stays on tcgen05 (45.5 us
-// against 49.2 us).
+// kernel streams registers: 42.8 / 40.7 us against 221 / 203 us).  q8_0 on
+// SoA planes stays on tcgen05 (45.5 us against 49.2 us for the pair kernel).
 bool tma_pair_taken(int fmt, bool aos, const GemvCall& c) {
   return (aos || fmt == 4) && tma_pair_eligible(c);
 }
 
-// Two columns in one launch (SoA planes or GGUF blocks): the weights stream
-// once for both.  GGUF blocks follow the one-column rule for CTAs per SM (one
-// CTA of 16 consumer warps for long streams, two of 8 below) with 4 rows per
-// pass (8 reduced values per lane, as q4_0's 8 rows of one column); q4_0
-// planes have their own measured rule below.  -1 when the call is not taken
-// (tma_pair_taken).
+// Two columns in one launch (q4_0 planes or GGUF blocks): the weights stream
+// once for both.  CTAs per SM and rows per pass were chosen by measurement
+// (below).  -1 when the call is not taken (tma_pair_taken).
 int gemv_tma_pair(int fmt, bool aos, const GemvCall& c, cudaStream_t st) {
   if (!tma_pair_taken(fmt, aos, c)) return -1;
   DeviceInfo dev;
@@ -1742,17 +1739,19 @@ int gemv_tma_pair(int fmt, bool aos, const GemvCall& c, cudaStream_t st) {
     if (rc == -1) rc = launch_tma<4, 1, 4, 16, false, 0, 2>(c, dev, st);
     return rc;
   }
-  if (fmt == 4) {
-    if (!big) rc = aos ? launch_tma<4, 1, 4, 8, true, 0, 2>(c, dev, st)
-                       : launch_tma<4, 1, 4, 8, false, 0, 2>(c, dev, st);
-    if (rc == -1) rc = aos ? launch_tma<4, 1, 4, 16, true, 0, 2>(c, dev, st)
-                           : launch_tma<4, 1, 4, 16, false, 0, 2>(c, dev, st);
+  // GGUF blocks (the only other calls taken), 4 rows per pass, same bits
+  // either way: one CTA of 16 consumers for K >= 8192 or long streams
+  // (28672 x 8192: q8_0 42.8 us against 48.5 with two CTAs of 8, q4_0 40.7
+  // against 44.7), two CTAs of 8 otherwise (and one when K needs more than 8
+  // slices)
+  const bool one = c.K >= 8192 || big;
+  if (fmt == 8) {
+    if (!one) rc = launch_tma<8, 1, 4, 8, true, 0, 2>(c, dev, st);
+    if (rc == -1) rc = launch_tma<8, 1, 4, 16, true, 0, 2>(c, dev, st);
     return rc;
   }
-  if (!big) rc = aos ? launch_tma<8, 1, 4, 8, true, 0, 2>(c, dev, st)
-                     : launch_tma<8, 1, 4, 8, false, 0, 2>(c, dev, st);
-  if (rc == -1) rc = aos ? launch_tma<8, 1, 4, 16, true, 0, 2>(c, dev, st)
-                         : launch_tma<8, 1, 4, 16, false, 0, 2>(c, dev, st);
+  if (!one) rc = launch_tma<4, 1, 4, 8, true, 0, 2>(c, dev, st);
+  if (rc == -1) rc = launch_tma<4, 1, 4, 16, true, 0, 2>(c, dev, st);
   return rc;
 }
 
