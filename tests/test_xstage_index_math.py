@@ -7,7 +7,8 @@ reads its eight 16-byte chunks in the order (i + l) & 7; the plane words come
 out in that order and three conditional shifts (by 1, 2, 4 when bit k of the
 lane is set) rotate them back.  Checked here: every lane ends with chunk c in
 position c, and each 16-byte read of a quarter-warp touches 8 different
-4-bank groups (no shared-memory bank conflict)."""
+4-bank groups (no shared-memory bank conflict), also for the second column of a
+two-column launch, staged K * 4 bytes after the first."""
 
 import pytest
 
@@ -28,7 +29,9 @@ def test_rotation_restores_chunk_order(lane):
     assert rotate_back(read_order, lane) == list(range(8))
 
 
-@pytest.mark.parametrize("slice_base", [0, 4096, 8192])
+# slice offsets of the first column, and of the second column of a two-column
+# launch (staged at byte K * 4: K = 4096 and K = 11008, K % 256 == 0)
+@pytest.mark.parametrize("slice_base", [0, 4096, 8192, 16384 + 4096, 44032, 44032 + 8192])
 def test_quarter_warp_reads_are_conflict_free(slice_base):
     for i in range(8):
         for q in range(4):  # quarter-warps: a 16-byte access per lane, 8 lanes per wavefront
